@@ -1,0 +1,237 @@
+#!/usr/bin/env python
+"""Headline benchmark: training tokens/s of the 0.494B Qwen-style MoE.
+
+    python bench.py --gpus N --steps K --warmup W [--impl ours|reference]
+
+Workload (fixed at every N, i.e. strong scaling): global batch 8 sequences of
+2048 tokens, synthetic uniform-random token ids, random N(0, 0.02) weights,
+bf16 compute with fp32 master weights and AdamW.  Layout by N:
+
+    N=1  one replica on one GPU
+    N=2  2 DP replicas x 1 GPU    (cross-replica fused reduce + AdamW)
+    N=4  2 DP replicas x TP2
+    N=8  2 DP replicas x (TP2 x PP2)
+
+Timing: W untimed warm-up steps, then K steps bracketed by a barrier and
+torch.cuda.synchronize() on both sides, timed with CUDA events on the
+launching stream; the step time is the max over ranks.  The working set of
+one step (weights, optimizer state, ~10 GB of activations) is far larger
+than the 126 MB L2, so no separate flush is needed.  SM clocks and throttle
+reasons are sampled with nvidia-smi during the timed region.  A second timed
+loop measures the same metric end to end through the public API, including
+the pinned host->device copy of each step's tokens and the device->host read
+of each step's loss.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+BASELINE_TOKENS_PER_S = 5591.0   # reference SHIFT 2x8 H800, 8 x 512 tokens / 0.7326 s median step
+GLOBAL_BATCH = 8
+SEQ = 2048
+METRIC = "tokens/s (device-timed, max over ranks)"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--seq", type=int, default=SEQ)
+    p.add_argument("--batch", type=int, default=GLOBAL_BATCH)
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-launch-count", action="store_true")
+    return p.parse_args()
+
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_bench_{os.getpid()}.csv")
+
+    def start(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.gpu)], stdout=self.f,
+                                         stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.close()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    mx = float(parts[2])
+                except ValueError:
+                    continue
+                for n, v in zip(names, parts[5:9]):
+                    if v.lower().startswith("active"):
+                        reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def reference_arm(args):
+    line = {"impl": "reference",
+            "unavailable": ("reference is not installable: no setup.py/pyproject in Zwhao0/SHIFT, and its model, "
+                            "parallel layers and kernels (FLASH1022, Megatron-LM, torchft) are external and absent "
+                            "from the offline image")}
+    rank = int(os.environ.get("RANK", "0"))
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        reference_arm(args)
+        return
+    import torch
+    import torch.distributed as dist
+
+    from shift_b200.runner import make_runner
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    runner = make_runner(args.gpus, rank, local, args.batch, args.seq)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for i in range(args.warmup):
+        runner.step(i)
+    torch.cuda.synchronize()
+
+    # ---------------- launch count (one untimed profiled step) ----------------
+    per_step_launches, library_launches = None, None
+    if not args.no_launch_count:
+        from torch.profiler import ProfilerActivity, profile
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            runner.step(args.warmup)
+            torch.cuda.synchronize()
+        ours = lib = 0
+        for evt in prof.events():
+            if evt.device_type.name != "CUDA":
+                continue
+            name = evt.name
+            if "Memcpy" in name or "Memset" in name:
+                continue
+            if "sb::" in name or name.startswith("void sb::") or "_ZN2sb" in name:
+                ours += 1
+            else:
+                lib += 1
+        per_step_launches, library_launches = ours, lib
+
+    # ---------------- device-timed loop ----------------
+    clocks = ClockSampler(local)
+    barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for i in range(args.steps):
+        runner.step(args.warmup + 1 + i)
+    t1.record()
+    torch.cuda.synchronize()
+    barrier()
+    ck = clocks.stop()
+    ms = t0.elapsed_time(t1) / args.steps
+    ms_t = torch.tensor([ms], device="cuda")
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms = float(ms_t)
+    tokens = args.batch * args.seq
+    value = tokens / (ms / 1e3)
+
+    # ---------------- end-to-end loop through the public API ----------------
+    e2e = None
+    if not args.no_e2e:
+        barrier()
+        torch.cuda.synchronize()
+        w0 = time.perf_counter()
+        h2d = d2h = 0
+        for i in range(args.steps):
+            loss, nb_in, nb_out = runner.step_e2e(args.warmup + 1 + args.steps + i)
+            h2d, d2h = nb_in, nb_out
+        torch.cuda.synchronize()
+        barrier()
+        el = time.perf_counter() - w0
+        el_t = torch.tensor([el], device="cuda")
+        if world > 1:
+            dist.all_reduce(el_t, op=dist.ReduceOp.MAX)
+        e2e = {"value": tokens / (float(el_t) / args.steps), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "ms_per_step": float(el_t) / args.steps * 1e3, "timer": "host wall clock"}
+
+    runner.close()
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": round(value, 1),
+            "unit": "tokens/s",
+            "n_gpus": args.gpus,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms, 3),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": round(value / BASELINE_TOKENS_PER_S, 2),
+            "dtype": "bf16",
+            "data": "synthetic (uniform random token ids, random N(0,0.02) init)",
+            "config": {"model": "qwen-moe-0.494b (12L, h1024, 16q/4kv x64, 16 experts top-4 ffn672, vocab 32768)",
+                       "global_batch": args.batch, "seq_len": args.seq, "parallelism": runner.layout,
+                       "l2": "working set per step >> 126 MB L2 (no flush needed)",
+                       "optimizer": "AdamW fp32 master, fused"},
+            "clocks": ck,
+            "e2e": e2e,
+            "gpu_launches": None if per_step_launches is None else per_step_launches * args.steps,
+            "gpu_launches_per_step": per_step_launches,
+            "library_launches_per_step": library_launches,
+            "impl": "ours",
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

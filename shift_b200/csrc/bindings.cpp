@@ -1,0 +1,78 @@
+// Python bindings for the sm_100a kernels of shift_b200 (module shift_b200._C).
+#include <torch/extension.h>
+
+#include "gemm_sm100.h"
+
+namespace sb {
+namespace norm {
+std::vector<at::Tensor> rmsnorm_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& delta, const at::Tensor& w,
+                                    double eps);
+at::Tensor rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& rstd, const at::Tensor& w,
+                       const c10::optional<at::Tensor>& dres, at::Tensor& dw_out, bool accumulate);
+void column_reduce(const at::Tensor& partial, at::Tensor& out, bool accumulate);
+void rope_(at::Tensor& qkv, const at::Tensor& cos_t, const at::Tensor& sin_t, int64_t S, int64_t n_rot_heads,
+           int64_t head_dim, int64_t pos0, bool inverse);
+}  // namespace norm
+namespace moe {
+std::vector<at::Tensor> router_fwd(const at::Tensor& x, const at::Tensor& wr, int64_t k, bool normalize);
+at::Tensor router_bwd(const at::Tensor& probs, const at::Tensor& topk_idx, const at::Tensor& topk_w,
+                      const at::Tensor& d_topk_w, const c10::optional<at::Tensor>& aux_grad, bool normalize);
+at::Tensor router_input_weight_grad(const at::Tensor& x, const at::Tensor& wr, const at::Tensor& dlogits,
+                                    at::Tensor& dx);
+std::vector<at::Tensor> bucket_sort(const at::Tensor& keys, int64_t lo, int64_t hi, int64_t pad, int64_t src_div);
+void gather_rows(const at::Tensor& src, const at::Tensor& row_src, const c10::optional<at::Tensor>& total,
+                 at::Tensor& out);
+at::Tensor combine(const at::Tensor& y, const at::Tensor& pos, const at::Tensor& w, int64_t T);
+std::vector<at::Tensor> combine_bwd(const at::Tensor& dout, const at::Tensor& y, const at::Tensor& pos,
+                                    const at::Tensor& w, const at::Tensor& row_src, const at::Tensor& slot_of_row,
+                                    const at::Tensor& total);
+void scatter_back(const at::Tensor& dperm, const at::Tensor& pos, at::Tensor& dx, bool accumulate);
+at::Tensor invert_pos(const at::Tensor& pos, int64_t cap);
+void embedding_bwd(const at::Tensor& dout, const at::Tensor& ids, at::Tensor& dW, int64_t vocab_lo);
+at::Tensor embedding_fwd(const at::Tensor& W, const at::Tensor& ids, int64_t vocab_lo);
+at::Tensor swiglu_fwd(const at::Tensor& h);
+at::Tensor swiglu_bwd(const at::Tensor& h, const at::Tensor& da);
+}  // namespace moe
+namespace xent {
+at::Tensor xent_fwd_bwd(at::Tensor& logits, const at::Tensor& labels, double scale, int64_t label_lo);
+}
+namespace adam {
+void adamw_step(const at::Tensor& master, const at::Tensor& m, const at::Tensor& v, const std::vector<at::Tensor>& grads,
+                at::Tensor& master_out, at::Tensor& m_out, at::Tensor& v_out, at::Tensor& param_out, double lr,
+                double beta1, double beta2, double eps, double wd, int64_t step, double grad_scale,
+                const c10::optional<at::Tensor>& nonfinite);
+void nonfinite_check(const at::Tensor& x, at::Tensor& flag);
+}  // namespace adam
+namespace attn {
+std::vector<at::Tensor> attn_fwd(const at::Tensor& qkv, int64_t B, int64_t S, int64_t Hq, int64_t Hkv, double scale);
+at::Tensor attn_bwd(const at::Tensor& qkv, const at::Tensor& o, const at::Tensor& lse, const at::Tensor& dout,
+                    int64_t B, int64_t S, int64_t Hq, int64_t Hkv, double scale);
+}  // namespace attn
+}  // namespace sb
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "shift_b200 sm_100a kernels";
+  m.def("gemm", &sb::gemm::gemm, "tcgen05 GEMM (dense / grouped)");
+  m.def("rmsnorm_fwd", &sb::norm::rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &sb::norm::rmsnorm_bwd);
+  m.def("column_reduce", &sb::norm::column_reduce);
+  m.def("rope_", &sb::norm::rope_);
+  m.def("router_fwd", &sb::moe::router_fwd);
+  m.def("router_bwd", &sb::moe::router_bwd);
+  m.def("router_input_weight_grad", &sb::moe::router_input_weight_grad);
+  m.def("bucket_sort", &sb::moe::bucket_sort);
+  m.def("gather_rows", &sb::moe::gather_rows);
+  m.def("combine", &sb::moe::combine);
+  m.def("combine_bwd", &sb::moe::combine_bwd);
+  m.def("scatter_back", &sb::moe::scatter_back);
+  m.def("invert_pos", &sb::moe::invert_pos);
+  m.def("embedding_fwd", &sb::moe::embedding_fwd);
+  m.def("embedding_bwd", &sb::moe::embedding_bwd);
+  m.def("swiglu_fwd", &sb::moe::swiglu_fwd);
+  m.def("swiglu_bwd", &sb::moe::swiglu_bwd);
+  m.def("xent_fwd_bwd", &sb::xent::xent_fwd_bwd);
+  m.def("adamw_step", &sb::adam::adamw_step);
+  m.def("nonfinite_check", &sb::adam::nonfinite_check);
+  m.def("attn_fwd", &sb::attn::attn_fwd);
+  m.def("attn_bwd", &sb::attn::attn_bwd);
+}

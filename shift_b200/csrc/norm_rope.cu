@@ -1,0 +1,284 @@
+// RMSNorm (forward / backward, with fused residual add) and rotary embedding
+// for sm_100a.  One warp owns one row; rows are 128-bit vectorised.  Weight
+// gradients are reduced deterministically: per-block partials in a fixed row
+// order, then a column reduction over blocks in block order.
+//
+// Parity: HF Qwen2 RMSNorm (x * rsqrt(mean(x^2) + eps) * w, fp32 statistics)
+// and HF rotate-half RoPE, as used by the model the reference trains
+// (shift_full/train.py:209-216 loads it; the model code itself is external).
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common.cuh"
+
+namespace sb {
+namespace norm {
+
+constexpr int kWarps = 8;
+
+// NV = H / 256: number of 8-element vectors per lane.
+template <int NV, bool kAdd>
+__global__ void __launch_bounds__(kWarps * 32)
+rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ delta,
+                   const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ h_out,
+                   __nv_bfloat16* __restrict__ y, float* __restrict__ rstd_out, int rows, float eps) {
+  constexpr int H = NV * 256;
+  const int lane = threadIdx.x % 32;
+  const int warp = blockIdx.x * kWarps + threadIdx.x / 32;
+  const int nwarps = gridDim.x * kWarps;
+  float wv[NV][8];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) bf16x8_to_float(reinterpret_cast<const bf16x8*>(w)[i * 32 + lane], wv[i]);
+  for (int r = warp; r < rows; r += nwarps) {
+    const bf16x8* xr = reinterpret_cast<const bf16x8*>(x + static_cast<long>(r) * H);
+    float v[NV][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      bf16x8_to_float(xr[i * 32 + lane], v[i]);
+      if (kAdd) {
+        float d[8];
+        bf16x8_to_float(reinterpret_cast<const bf16x8*>(delta + static_cast<long>(r) * H)[i * 32 + lane], d);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] += d[j];
+        bf16x8 hv = float_to_bf16x8(v[i]);
+        reinterpret_cast<bf16x8*>(h_out + static_cast<long>(r) * H)[i * 32 + lane] = hv;
+        bf16x8_to_float(hv, v[i]);  // normalise the rounded residual stream
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
+    }
+    ss = warp_sum(ss);
+    const float rs = rsqrtf(ss / H + eps);
+    if (lane == 0) rstd_out[r] = rs;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      float o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = v[i][j] * rs * wv[i][j];
+      reinterpret_cast<bf16x8*>(y + static_cast<long>(r) * H)[i * 32 + lane] = float_to_bf16x8(o);
+    }
+  }
+}
+
+// dx = rstd * (dy*w - xhat * mean(dy*w*xhat)) (+ dres);  partial dw per block.
+template <int NV, bool kRes>
+__global__ void __launch_bounds__(kWarps * 32)
+rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
+                   const float* __restrict__ rstd, const __nv_bfloat16* __restrict__ w,
+                   const __nv_bfloat16* __restrict__ dres, __nv_bfloat16* __restrict__ dx,
+                   float* __restrict__ dw_partial, int rows) {
+  constexpr int H = NV * 256;
+  __shared__ float red[kWarps][H];
+  const int lane = threadIdx.x % 32;
+  const int wib = threadIdx.x / 32;
+  const int warp = blockIdx.x * kWarps + wib;
+  const int nwarps = gridDim.x * kWarps;
+  float wv[NV][8], dwacc[NV][8];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    bf16x8_to_float(reinterpret_cast<const bf16x8*>(w)[i * 32 + lane], wv[i]);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) dwacc[i][j] = 0.f;
+  }
+  for (int r = warp; r < rows; r += nwarps) {
+    const float rs = rstd[r];
+    float xh[NV][8], g[NV][8];
+    float dot = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      float dv[8];
+      bf16x8_to_float(reinterpret_cast<const bf16x8*>(x + static_cast<long>(r) * H)[i * 32 + lane], xh[i]);
+      bf16x8_to_float(reinterpret_cast<const bf16x8*>(dy + static_cast<long>(r) * H)[i * 32 + lane], dv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        xh[i][j] *= rs;
+        g[i][j] = dv[j] * wv[i][j];
+        dot += g[i][j] * xh[i][j];
+        dwacc[i][j] += dv[j] * xh[i][j];
+      }
+    }
+    dot = warp_sum(dot) / H;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      float o[8];
+      float rr[8];
+      if (kRes) bf16x8_to_float(reinterpret_cast<const bf16x8*>(dres + static_cast<long>(r) * H)[i * 32 + lane], rr);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = rs * (g[i][j] - xh[i][j] * dot) + (kRes ? rr[j] : 0.f);
+      reinterpret_cast<bf16x8*>(dx + static_cast<long>(r) * H)[i * 32 + lane] = float_to_bf16x8(o);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < NV; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) red[wib][(i * 32 + lane) * 8 + j] = dwacc[i][j];
+  __syncthreads();
+  for (int c = threadIdx.x; c < H; c += blockDim.x) {
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < kWarps; ++k) s += red[k][c];
+    dw_partial[static_cast<long>(blockIdx.x) * H + c] = s;
+  }
+}
+
+// out[c] (+)= sum_b partial[b, c] in block order (deterministic).
+__global__ void column_reduce_kernel(const float* __restrict__ partial, int nblocks, int cols,
+                                     float* __restrict__ out_f32, __nv_bfloat16* __restrict__ out_bf16,
+                                     int accumulate) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= cols) return;
+  float s = 0.f;
+  for (int b = 0; b < nblocks; ++b) s += partial[static_cast<long>(b) * cols + c];
+  if (out_f32) out_f32[c] = accumulate ? out_f32[c] + s : s;
+  if (out_bf16) out_bf16[c] = __float2bfloat16(accumulate ? __bfloat162float(out_bf16[c]) + s : s);
+}
+
+static int blocks_for(int rows) {
+  int dev;
+  cudaGetDevice(&dev);
+  int sms;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return std::max(1, std::min((rows + kWarps - 1) / kWarps, sms * 4));
+}
+
+#define SB_NORM_DISPATCH(H, MACRO) \
+  switch (H) {                     \
+    case 256: MACRO(1); break;     \
+    case 512: MACRO(2); break;     \
+    case 1024: MACRO(4); break;    \
+    default: TORCH_CHECK(false, "rmsnorm: hidden size must be 256/512/1024"); \
+  }
+
+// Returns (y, rstd) ; if delta is given also h = x + delta (written to h_out).
+std::vector<at::Tensor> rmsnorm_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& delta,
+                                    const at::Tensor& w, double eps) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous(), "rmsnorm: bf16 contiguous x");
+  TORCH_CHECK(w.scalar_type() == at::kBFloat16, "rmsnorm: bf16 weight");
+  const at::cuda::CUDAGuard guard(x.device());
+  const int H = static_cast<int>(x.size(-1));
+  const int rows = static_cast<int>(x.numel() / H);
+  auto y = at::empty_like(x);
+  auto rstd = at::empty({rows}, x.options().dtype(at::kFloat));
+  at::Tensor h;
+  const bool add = delta.has_value();
+  if (add) {
+    TORCH_CHECK(delta->is_contiguous() && delta->sizes() == x.sizes(), "rmsnorm: delta shape");
+    h = at::empty_like(x);
+  }
+  const int blocks = blocks_for(rows);
+  auto stream = at::cuda::getCurrentCUDAStream();
+  auto xp = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+  auto dp = add ? reinterpret_cast<const __nv_bfloat16*>(delta->data_ptr()) : nullptr;
+  auto wp = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
+  auto hp = add ? reinterpret_cast<__nv_bfloat16*>(h.data_ptr()) : nullptr;
+  auto yp = reinterpret_cast<__nv_bfloat16*>(y.data_ptr());
+#define SB_LAUNCH(NV)                                                                                       \
+  if (add) rmsnorm_fwd_kernel<NV, true><<<blocks, kWarps * 32, 0, stream>>>(xp, dp, wp, hp, yp, rstd.data_ptr<float>(), rows, (float)eps); \
+  else rmsnorm_fwd_kernel<NV, false><<<blocks, kWarps * 32, 0, stream>>>(xp, dp, wp, hp, yp, rstd.data_ptr<float>(), rows, (float)eps);
+  SB_NORM_DISPATCH(H, SB_LAUNCH)
+#undef SB_LAUNCH
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  if (add) return {y, rstd, h};
+  return {y, rstd};
+}
+
+// Returns dx; accumulates dw into dw_out (fp32 or bf16 tensor of shape [H]).
+at::Tensor rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& rstd, const at::Tensor& w,
+                       const c10::optional<at::Tensor>& dres, at::Tensor& dw_out, bool accumulate) {
+  TORCH_CHECK(dy.is_contiguous() && x.is_contiguous(), "rmsnorm_bwd: contiguous inputs");
+  const at::cuda::CUDAGuard guard(x.device());
+  const int H = static_cast<int>(x.size(-1));
+  const int rows = static_cast<int>(x.numel() / H);
+  auto dx = at::empty_like(x);
+  const int blocks = blocks_for(rows);
+  auto partial = at::empty({blocks, H}, x.options().dtype(at::kFloat));
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const bool res = dres.has_value();
+  auto dyp = reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr());
+  auto xp = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+  auto wp = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
+  auto rp = res ? reinterpret_cast<const __nv_bfloat16*>(dres->data_ptr()) : nullptr;
+  auto dxp = reinterpret_cast<__nv_bfloat16*>(dx.data_ptr());
+#define SB_LAUNCH(NV)                                                                                       \
+  if (res) rmsnorm_bwd_kernel<NV, true><<<blocks, kWarps * 32, 0, stream>>>(dyp, xp, rstd.data_ptr<float>(), wp, rp, dxp, partial.data_ptr<float>(), rows); \
+  else rmsnorm_bwd_kernel<NV, false><<<blocks, kWarps * 32, 0, stream>>>(dyp, xp, rstd.data_ptr<float>(), wp, rp, dxp, partial.data_ptr<float>(), rows);
+  SB_NORM_DISPATCH(H, SB_LAUNCH)
+#undef SB_LAUNCH
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  float* of = dw_out.scalar_type() == at::kFloat ? dw_out.data_ptr<float>() : nullptr;
+  __nv_bfloat16* ob = dw_out.scalar_type() == at::kBFloat16 ? reinterpret_cast<__nv_bfloat16*>(dw_out.data_ptr()) : nullptr;
+  column_reduce_kernel<<<(H + 255) / 256, 256, 0, stream>>>(partial.data_ptr<float>(), blocks, H, of, ob, accumulate ? 1 : 0);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return dx;
+}
+
+void column_reduce(const at::Tensor& partial, at::Tensor& out, bool accumulate) {
+  const at::cuda::CUDAGuard guard(partial.device());
+  const int cols = static_cast<int>(partial.size(1));
+  const int nb = static_cast<int>(partial.size(0));
+  float* of = out.scalar_type() == at::kFloat ? out.data_ptr<float>() : nullptr;
+  __nv_bfloat16* ob = out.scalar_type() == at::kBFloat16 ? reinterpret_cast<__nv_bfloat16*>(out.data_ptr()) : nullptr;
+  column_reduce_kernel<<<(cols + 255) / 256, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      partial.data_ptr<float>(), nb, cols, of, ob, accumulate ? 1 : 0);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// ---------------------------------------------------------------------------
+// RoPE on the fused QKV activation [T, (Hq + 2*Hkv) * D] in place.
+// q heads [0, Hq), k heads [Hq, Hq+Hkv); v untouched.  Position of row t is
+// pos0 + (t % S).  cos/sin tables are [max_pos, D/2] fp32.
+// sign = +1 forward rotation, -1 inverse (backward).
+// ---------------------------------------------------------------------------
+template <int D>
+__global__ void rope_kernel(__nv_bfloat16* __restrict__ qkv, const float* __restrict__ cos_t,
+                            const float* __restrict__ sin_t, int T, int S, int n_rot_heads, int row_stride,
+                            int pos0, float sign) {
+  constexpr int HALF = D / 2;
+  // one thread handles 2 element pairs (x1[i], x2[i]) for i in [2j, 2j+1]
+  const long idx = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long per_row = static_cast<long>(n_rot_heads) * (HALF / 2);
+  if (idx >= per_row * T) return;
+  const int t = static_cast<int>(idx / per_row);
+  const int rem = static_cast<int>(idx % per_row);
+  const int head = rem / (HALF / 2);
+  const int i = (rem % (HALF / 2)) * 2;
+  const int pos = pos0 + (t % S);
+  __nv_bfloat16* base = qkv + static_cast<long>(t) * row_stride + head * D;
+  const float2 c = *reinterpret_cast<const float2*>(cos_t + static_cast<long>(pos) * HALF + i);
+  float2 s = *reinterpret_cast<const float2*>(sin_t + static_cast<long>(pos) * HALF + i);
+  s.x *= sign;
+  s.y *= sign;
+  const float2 a = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(base + i));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(base + HALF + i));
+  const float2 oa = make_float2(a.x * c.x - b.x * s.x, a.y * c.y - b.y * s.y);
+  const float2 ob = make_float2(b.x * c.x + a.x * s.x, b.y * c.y + a.y * s.y);
+  *reinterpret_cast<__nv_bfloat162*>(base + i) = __floats2bfloat162_rn(oa.x, oa.y);
+  *reinterpret_cast<__nv_bfloat162*>(base + HALF + i) = __floats2bfloat162_rn(ob.x, ob.y);
+}
+
+void rope_(at::Tensor& qkv, const at::Tensor& cos_t, const at::Tensor& sin_t, int64_t S, int64_t n_rot_heads,
+           int64_t head_dim, int64_t pos0, bool inverse) {
+  TORCH_CHECK(qkv.scalar_type() == at::kBFloat16 && qkv.stride(-1) == 1, "rope: bf16 qkv");
+  TORCH_CHECK(head_dim == 64 || head_dim == 128, "rope: head_dim 64 or 128");
+  const at::cuda::CUDAGuard guard(qkv.device());
+  const int T = static_cast<int>(qkv.numel() / qkv.size(-1));
+  const int row_stride = static_cast<int>(qkv.size(-1));
+  const long work = static_cast<long>(T) * n_rot_heads * (head_dim / 4);
+  const int threads = 256;
+  const int blocks = static_cast<int>((work + threads - 1) / threads);
+  auto stream = at::cuda::getCurrentCUDAStream();
+  auto p = reinterpret_cast<__nv_bfloat16*>(qkv.data_ptr());
+  const float sign = inverse ? -1.f : 1.f;
+  if (head_dim == 64)
+    rope_kernel<64><<<blocks, threads, 0, stream>>>(p, cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), T, (int)S,
+                                                    (int)n_rot_heads, row_stride, (int)pos0, sign);
+  else
+    rope_kernel<128><<<blocks, threads, 0, stream>>>(p, cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), T, (int)S,
+                                                     (int)n_rot_heads, row_stride, (int)pos0, sign);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace norm
+}  // namespace sb

@@ -1,0 +1,145 @@
+"""GEMM entry points on the sm_100a tcgen05 kernel (``csrc/gemm_sm100.cu``).
+
+Naming follows the training step of a linear layer ``y = x @ w.T``:
+
+* ``linear_fwd``   y[M,N]  = x[M,K] @ w[N,K]^T        (A K-major, B K-major)
+* ``linear_dgrad`` dx[M,K] = dy[M,N] @ w[N,K]         (A K-major, B MN-major)
+* ``linear_wgrad`` dw[N,K] (+)= dy[M,N]^T @ x[M,K]    (A MN-major, B MN-major)
+
+and the grouped (MoE expert) forms, where rows of ``x`` are split into
+contiguous per-expert segments by ``offs`` (int32 [G+1], device):
+
+* ``grouped_fwd``   y[r]  = x[r] @ w[g]^T        w [G, N, K]
+* ``grouped_dgrad`` dx[r] = dy[r] @ w[g]         w [G, N, K]
+* ``grouped_wgrad`` dw[g] (+)= dy[seg g]^T @ x[seg g]
+
+CPU tensors fall back to fp32 ``torch.matmul`` (oracle / CPU harness only).
+"""
+from __future__ import annotations
+
+import torch
+
+from ._ext import ext, status_word
+
+ROW_GROUPS, K_GROUPS = 0, 1
+EPI_BF16, EPI_F32, EPI_ACC_BF16, EPI_ACC_F32, EPI_SWIGLU = 0, 1, 2, 3, 4
+
+
+def pick_bn(n: int) -> int:
+    """Tile width with the least padding of N (ties -> wider tile)."""
+    best, waste = 256, None
+    for bn in (256, 192, 128):
+        w = -(-n // bn) * bn - n
+        if waste is None or w < waste:
+            best, waste = bn, w
+    return best
+
+
+def _run(A, B, D, D2, offs, M, N, K, G, mode, a_mn, b_mn, epi, alpha, max_rows):
+    ext().gemm(A, B, D, D2, offs, M, N, K, G, mode, a_mn, b_mn, epi, float(alpha), pick_bn(N),
+               status_word(A.device), max_rows)
+
+
+def linear_fwd(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    M, K = x.shape
+    N = w.shape[0]
+    if not x.is_cuda:
+        y = x.float() @ w.float().t()
+        return y.to(x.dtype) if out is None else out.copy_(y)
+    if out is None:
+        out = torch.empty(M, N, dtype=x.dtype, device=x.device)
+    _run(x, w, out, None, None, M, N, K, 1, ROW_GROUPS, False, False, EPI_BF16, 1.0, M)
+    return out
+
+
+def linear_dgrad(dy: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    M, N = dy.shape
+    K = w.shape[1]
+    if not dy.is_cuda:
+        d = dy.float() @ w.float()
+        return d.to(dy.dtype) if out is None else out.copy_(d)
+    if out is None:
+        out = torch.empty(M, K, dtype=dy.dtype, device=dy.device)
+    _run(dy, w, out, None, None, M, K, N, 1, ROW_GROUPS, False, True, EPI_BF16, 1.0, M)
+    return out
+
+
+def linear_wgrad(dy: torch.Tensor, x: torch.Tensor, dw: torch.Tensor, accumulate: bool = False) -> torch.Tensor:
+    """dw[N,K] = dy^T x (or +=).  dw may be bf16 or fp32."""
+    M, N = dy.shape
+    K = x.shape[1]
+    if not dy.is_cuda:
+        g = dy.float().t() @ x.float()
+        if accumulate:
+            dw.add_(g.to(dw.dtype))
+        else:
+            dw.copy_(g)
+        return dw
+    if dw.dtype == torch.float32:
+        epi = EPI_ACC_F32 if accumulate else EPI_F32
+    else:
+        epi = EPI_ACC_BF16 if accumulate else EPI_BF16
+    _run(dy, x, dw, None, None, N, K, M, 1, K_GROUPS, True, True, epi, 1.0, N)
+    return dw
+
+
+def grouped_fwd(x: torch.Tensor, w: torch.Tensor, offs: torch.Tensor, swiglu: bool = False):
+    """x [R, K] (segments by offs), w [G, N, K].  Returns y [R, N] or, with
+    swiglu, (h [R, N], act [R, N/2]) where h holds interleaved gate/up blocks."""
+    G, N, K = w.shape
+    R = x.shape[0]
+    if not x.is_cuda:
+        from . import reference as ref
+        y = torch.zeros(R, N, dtype=torch.float32)
+        o = offs.tolist()
+        for g in range(G):
+            if o[g + 1] > o[g]:
+                y[o[g]:o[g + 1]] = x[o[g]:o[g + 1]].float() @ w[g].float().t()
+        y = y.to(x.dtype)
+        if swiglu:
+            return y, ref.swiglu_interleaved(y)
+        return y
+    y = torch.empty(R, N, dtype=x.dtype, device=x.device)
+    if swiglu:
+        act = torch.empty(R, N // 2, dtype=x.dtype, device=x.device)
+        _run(x, w.view(G * N, K), y, act, offs, R, N, K, G, ROW_GROUPS, False, False, EPI_SWIGLU, 1.0, R)
+        return y, act
+    _run(x, w.view(G * N, K), y, None, offs, R, N, K, G, ROW_GROUPS, False, False, EPI_BF16, 1.0, R)
+    return y
+
+
+def grouped_dgrad(dy: torch.Tensor, w: torch.Tensor, offs: torch.Tensor) -> torch.Tensor:
+    """dx[r] = dy[r] @ w[g]; dy [R, N], w [G, N, K] -> [R, K]."""
+    G, N, K = w.shape
+    R = dy.shape[0]
+    if not dy.is_cuda:
+        out = torch.zeros(R, K, dtype=torch.float32)
+        o = offs.tolist()
+        for g in range(G):
+            if o[g + 1] > o[g]:
+                out[o[g]:o[g + 1]] = dy[o[g]:o[g + 1]].float() @ w[g].float()
+        return out.to(dy.dtype)
+    out = torch.empty(R, K, dtype=dy.dtype, device=dy.device)
+    _run(dy, w.view(G * N, K), out, None, offs, R, K, N, G, ROW_GROUPS, False, True, EPI_BF16, 1.0, R)
+    return out
+
+
+def grouped_wgrad(dy: torch.Tensor, x: torch.Tensor, offs: torch.Tensor, dw: torch.Tensor,
+                  accumulate: bool = False) -> torch.Tensor:
+    """dw[g] (+)= dy[seg]^T x[seg]; dy [R, N], x [R, K], dw [G, N, K]."""
+    G, N, K = dw.shape
+    if not dy.is_cuda:
+        o = offs.tolist()
+        for g in range(G):
+            gr = dy[o[g]:o[g + 1]].float().t() @ x[o[g]:o[g + 1]].float()
+            if accumulate:
+                dw[g].add_(gr.to(dw.dtype))
+            else:
+                dw[g].copy_(gr)
+        return dw
+    if dw.dtype == torch.float32:
+        epi = EPI_ACC_F32 if accumulate else EPI_F32
+    else:
+        epi = EPI_ACC_BF16 if accumulate else EPI_BF16
+    _run(dy, x, dw.view(G * N, K), None, offs, N, K, dy.shape[0], G, K_GROUPS, True, True, epi, 1.0, N)
+    return dw

@@ -1,0 +1,279 @@
+"""Every sm_100a kernel against a plain fp32 PyTorch statement of the same op."""
+import math
+
+import pytest
+import torch
+
+from shift_b200.ops import functional as Fn
+from shift_b200.ops import gemm as G
+from shift_b200.ops import reference as ref
+from shift_b200.ops._ext import check_status
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _close(out, expect, tol=2e-2):
+    out, expect = out.float(), expect.float()
+    scale = expect.abs().max().item() + 1e-6
+    err = (out - expect).abs().max().item()
+    assert err <= tol * scale, f"max err {err:.4g} vs scale {scale:.4g}"
+
+
+def _bf(*shape, std=1.0):
+    return (torch.randn(*shape, device=DEV) * std).to(torch.bfloat16)
+
+
+# ----------------------------------------------------------------------------- GEMM
+@pytest.mark.parametrize("M,N,K", [(256, 256, 128), (300, 336, 200), (1024, 1536, 1024), (128, 672, 672)])
+def test_linear_fwd(M, N, K):
+    torch.manual_seed(0)
+    x, w = _bf(M, K), _bf(N, K)
+    y = G.linear_fwd(x, w)
+    torch.cuda.synchronize()
+    check_status()
+    _close(y, x.float() @ w.float().t())
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 256, 128), (384, 1024, 672), (200, 512, 1344)])
+def test_linear_dgrad(M, N, K):
+    torch.manual_seed(1)
+    dy, w = _bf(M, N), _bf(N, K)
+    dx = G.linear_dgrad(dy, w)
+    torch.cuda.synchronize()
+    check_status()
+    _close(dx, dy.float() @ w.float())
+
+
+@pytest.mark.parametrize("dtype,acc", [(torch.float32, False), (torch.float32, True), (torch.bfloat16, False),
+                                       (torch.bfloat16, True)])
+def test_linear_wgrad(dtype, acc):
+    torch.manual_seed(2)
+    M, N, K = 640, 384, 256
+    dy, x = _bf(M, N), _bf(M, K)
+    base = torch.randn(N, K, device=DEV).to(dtype)
+    dw = base.clone()
+    G.linear_wgrad(dy, x, dw, accumulate=acc)
+    torch.cuda.synchronize()
+    check_status()
+    expect = dy.float().t() @ x.float() + (base.float() if acc else 0)
+    _close(dw, expect)
+
+
+def _offsets(counts, pad=128):
+    offs = [0]
+    for c in counts:
+        offs.append(offs[-1] + (c + pad - 1) // pad * pad)
+    return torch.tensor(offs, dtype=torch.int32, device=DEV)
+
+
+def _segments(x, counts, offs):
+    """zero the padding rows of a [R, C] tensor laid out by offs"""
+    o = offs.tolist()
+    for g, c in enumerate(counts):
+        x[o[g] + c:o[g + 1]] = 0
+    return x
+
+
+def test_grouped_fwd_dgrad_wgrad():
+    torch.manual_seed(3)
+    counts = [130, 0, 5, 256, 77]
+    offs = _offsets(counts)
+    R = int(offs[-1])
+    Gn, N, K = len(counts), 1344, 1024
+    x = _segments(_bf(R, K), counts, offs)
+    w = _bf(Gn, N, K, std=0.05)
+    y = G.grouped_fwd(x, w, offs)
+    dy = _segments(_bf(R, N), counts, offs)
+    dx = G.grouped_dgrad(dy, w, offs)
+    dw = torch.zeros(Gn, N, K, device=DEV, dtype=torch.bfloat16)
+    G.grouped_wgrad(dy, x, offs, dw)
+    torch.cuda.synchronize()
+    check_status()
+    o = offs.tolist()
+    for g in range(Gn):
+        a, b = o[g], o[g + 1]
+        if b > a:
+            _close(y[a:b], x[a:b].float() @ w[g].float().t())
+            _close(dx[a:b], dy[a:b].float() @ w[g].float())
+            _close(dw[g], dy[a:b].float().t() @ x[a:b].float())
+        else:
+            assert dw[g].abs().max().item() == 0.0
+
+
+def test_grouped_swiglu_epilogue():
+    torch.manual_seed(4)
+    counts = [200, 64, 0, 300]
+    offs = _offsets(counts)
+    R = int(offs[-1])
+    Gn, F, K = len(counts), 672, 1024
+    x = _bf(R, K)
+    w = _bf(Gn, 2 * F, K, std=0.05)
+    h, a = G.grouped_fwd(x, w, offs, swiglu=True)
+    torch.cuda.synchronize()
+    check_status()
+    o = offs.tolist()
+    for g in range(Gn):
+        s, e = o[g], o[g + 1]
+        if e > s:
+            hr = x[s:e].float() @ w[g].float().t()
+            _close(h[s:e], hr)
+            _close(a[s:e], ref.swiglu_interleaved(h[s:e].float()))
+
+
+# ----------------------------------------------------------------------------- norm / rope
+@pytest.mark.parametrize("H", [256, 1024])
+def test_rmsnorm_fwd_bwd(H):
+    torch.manual_seed(5)
+    T = 1000
+    x, d = _bf(T, H), _bf(T, H)
+    w = (1 + 0.1 * torch.randn(H, device=DEV)).to(torch.bfloat16)
+    y, rstd, h = Fn.rmsnorm_fwd(x, w, 1e-6, delta=d)
+    hr = (x.float() + d.float())
+    _close(h, hr)
+    _close(y, ref.rmsnorm(h.float(), w.float(), 1e-6))
+    dy, dres = _bf(T, H), _bf(T, H)
+    dw = torch.zeros(H, device=DEV, dtype=torch.float32)
+    dx = Fn.rmsnorm_bwd(dy, h, rstd, w, 1e-6, dw, dres=dres)
+    gx, gw = ref.grad_of(lambda a, b: ref.rmsnorm(a, b, 1e-6), [h.float(), w.float()], dy.float())
+    _close(dx, gx + dres.float())
+    _close(dw, gw, tol=1e-2)
+
+
+def test_rope_roundtrip_and_reference():
+    torch.manual_seed(6)
+    B, S, Hq, Hkv, D = 2, 128, 4, 2, 64
+    cos, sin = ref.rope_tables(512, D, 1e6, DEV)
+    qkv = _bf(B * S, (Hq + 2 * Hkv) * D)
+    orig = qkv.clone()
+    Fn.rope_(qkv, cos, sin, S, Hq + Hkv, D)
+    rot = ref.rope(orig[:, : (Hq + Hkv) * D].view(B * S, Hq + Hkv, D).float(), cos, sin, S)
+    _close(qkv[:, : (Hq + Hkv) * D].view(B * S, Hq + Hkv, D), rot)
+    assert torch.equal(qkv[:, (Hq + Hkv) * D:], orig[:, (Hq + Hkv) * D:])
+    Fn.rope_(qkv, cos, sin, S, Hq + Hkv, D, inverse=True)
+    _close(qkv, orig)
+
+
+# ----------------------------------------------------------------------------- attention
+@pytest.mark.parametrize("B,S,Hq,Hkv", [(2, 128, 4, 2), (1, 256, 16, 4)])
+def test_attention_fwd_bwd(B, S, Hq, Hkv):
+    torch.manual_seed(7)
+    D = 64
+    T = B * S
+    qkv = _bf(T, (Hq + 2 * Hkv) * D)
+    scale = 1 / math.sqrt(D)
+    o, lse = Fn.attention_fwd(qkv, B, S, Hq, Hkv, D, scale)
+
+    def f(x):
+        q = x[:, : Hq * D].view(T, Hq, D)
+        k = x[:, Hq * D:(Hq + Hkv) * D].view(T, Hkv, D)
+        v = x[:, (Hq + Hkv) * D:].view(T, Hkv, D)
+        return ref.attention(q, k, v, B, S, scale).reshape(T, Hq * D)
+
+    _close(o, f(qkv.float()))
+    do = _bf(T, Hq * D)
+    dqkv = Fn.attention_bwd(qkv, o, lse, do, B, S, Hq, Hkv, D, scale)
+    (g,) = ref.grad_of(f, [qkv.float()], do.float())
+    _close(dqkv, g, tol=3e-2)
+
+
+# ----------------------------------------------------------------------------- MoE plumbing
+def test_router_sort_gather_combine():
+    torch.manual_seed(8)
+    T, H, E, k = 700, 1024, 16, 4
+    x = _bf(T, H)
+    wr = _bf(E, H, std=0.05)
+    probs, idx, w = Fn.router_fwd(x, wr, k, True)
+    pr, ir, wref = ref.router(x.float(), wr.float(), k, True)
+    _close(probs, pr, tol=1e-3)
+    agree = (idx == ir.to(idx.device)).float().mean().item()
+    assert agree > 0.99
+    pos, offs, counts, row_src = Fn.bucket_sort(idx, 0, E, 128, k)
+    # every (token, choice) has a unique slot inside its expert's segment
+    o = offs.tolist()
+    flat = idx.reshape(-1).tolist()
+    pl = pos.tolist()
+    assert len(set(pl)) == len(pl)
+    for i, (e, p) in enumerate(zip(flat, pl)):
+        assert o[e] <= p < o[e] + int(counts[e])
+        assert int(row_src[p]) == i // k
+    # stability: within an expert, slots follow (token, choice) order
+    for e in range(E):
+        ps = [p for ee, p in zip(flat, pl) if ee == e]
+        assert ps == sorted(ps)
+    cap = row_src.shape[0]
+    total = offs[E:E + 1]
+    xp = Fn.gather_rows(x, row_src, total, cap)
+    valid = row_src >= 0
+    assert torch.equal(xp[valid], x[row_src[valid].long()])
+    y = _bf(cap, H)
+    out = Fn.combine(y, pos.view(T, k), w, T)
+    expect = torch.zeros(T, H, device=DEV)
+    for j in range(k):
+        expect += w[:, j:j + 1] * y[pos.view(T, k)[:, j].long()].float()
+    _close(out, expect)
+
+
+def test_xent_fwd_bwd():
+    torch.manual_seed(9)
+    T, V = 64, 32768
+    logits = _bf(T, V, std=2.0)
+    labels = torch.randint(0, V, (T,), device=DEV, dtype=torch.int32)
+    labels[3] = -100
+    ref_loss = ref.cross_entropy(logits.float(), labels)
+    (g,) = ref.grad_of(lambda z: ref.cross_entropy(z, labels).sum(), [logits.float()], torch.tensor(1.0, device=DEV))
+    lg = logits.clone()
+    loss = Fn.xent_fwd_bwd(lg, labels, 1.0)
+    _close(loss, ref_loss, tol=1e-3)
+    _close(lg, g, tol=1e-2)
+
+
+def test_embedding_fwd_bwd_deterministic():
+    torch.manual_seed(10)
+    V, H, T = 4096, 1024, 5000
+    W = _bf(V, H)
+    ids = torch.randint(0, V, (T,), device=DEV, dtype=torch.int32)
+    out = Fn.embedding_fwd(W, ids)
+    assert torch.equal(out, W[ids.long()])
+    dout = _bf(T, H)
+    d1 = torch.zeros(V, H, device=DEV)
+    d2 = torch.zeros(V, H, device=DEV)
+    Fn.embedding_bwd(dout, ids, d1)
+    Fn.embedding_bwd(dout, ids, d2)
+    assert torch.equal(d1, d2)
+    expect = torch.zeros(V, H, device=DEV).index_add_(0, ids.long(), dout.float())
+    _close(d1, expect, tol=1e-5)
+
+
+def test_swiglu_kernels():
+    torch.manual_seed(11)
+    R, F = 300, 672
+    h = _bf(R, 2 * F)
+    a = Fn.swiglu_fwd(h)
+    _close(a, ref.swiglu_interleaved(h.float()))
+    da = _bf(R, F)
+    dh = Fn.swiglu_bwd(h, da)
+    (g,) = ref.grad_of(ref.swiglu_interleaved, [h.float()], da.float())
+    _close(dh, g)
+
+
+def test_adamw_matches_torch():
+    torch.manual_seed(12)
+    n = 10_007
+    master = torch.randn(n, device=DEV)
+    m = torch.randn(n, device=DEV).abs() * 0.01
+    v = torch.randn(n, device=DEV).abs() * 0.001
+    g1, g2 = _bf(n), _bf(n)
+    outs = [torch.empty_like(master) for _ in range(3)]
+    pb = torch.empty(n, device=DEV, dtype=torch.bfloat16)
+    flag = torch.zeros(1, dtype=torch.int32, device=DEV)
+    Fn.adamw_step(master, m, v, [g1, g2], *outs, pb, 1e-3, 0.9, 0.999, 1e-8, 0.01, 7, 0.5, flag)
+    g = (g1.float() + g2.float()) * 0.5
+    em, emm, ev = ref.adamw(master, m, v, g, 1e-3, 0.9, 0.999, 1e-8, 0.01, 7)
+    _close(outs[0], em, tol=1e-6)
+    _close(outs[1], emm, tol=1e-6)
+    _close(outs[2], ev, tol=1e-6)
+    assert int(flag) == 0
+    g1[5] = float("inf")
+    Fn.adamw_step(master, m, v, [g1], *outs, pb, 1e-3, 0.9, 0.999, 1e-8, 0.01, 7, 1.0, flag)
+    assert int(flag) == 1

@@ -1,0 +1,201 @@
+"""Kernel micro-benchmarks at the shapes of the 0.494B MoE training step.
+
+    python -m shift_b200.ops.microbench [--ops gemm,attn,norm,moe,adam] [--iters N]
+
+Each case is timed with CUDA events on the launching stream after warm-up,
+with a synchronize on both sides; inputs of the timed cases are larger than
+the 126 MB L2 or an L2-sized buffer is rewritten between iterations.  The
+achieved rate is reported against MEASURED_PEAKS.json (the driver-measured
+copy bandwidth and cuBLAS bf16 throughput of this GPU type), and GEMMs are
+also timed against torch.matmul (cuBLAS) on the same operands.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+
+import torch
+
+from . import functional as Fn
+from . import gemm as G
+from . import reference as ref
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
+
+
+_flush = None
+
+
+def flush_l2():
+    global _flush
+    if _flush is None:
+        _flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+    _flush.zero_()
+
+
+def timeit(fn, iters=20, warmup=3, flush=True):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(iters):
+        if flush:
+            flush_l2()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b))
+    times.sort()
+    return times[len(times) // 2]
+
+
+def bf(*shape, std=1.0):
+    return (torch.randn(*shape, device="cuda") * std).to(torch.bfloat16)
+
+
+def gemm_cases(T=16384):
+    H, F, V, E, k = 1024, 672, 32768, 16, 4
+    cases = []
+    for (name, M, N, K) in [("qkv", T, 1536, H), ("o", T, H, H), ("lm_head", T, V, H)]:
+        x, w = bf(M, K), bf(N, K)
+        dy = bf(M, N)
+        dw = torch.empty(N, K, device="cuda", dtype=torch.bfloat16)
+        flops = 2.0 * M * N * K
+        cases.append((f"{name}.fwd {M}x{N}x{K}", flops, lambda x=x, w=w: G.linear_fwd(x, w),
+                      lambda x=x, w=w: torch.matmul(x, w.t())))
+        cases.append((f"{name}.dgrad", flops, lambda dy=dy, w=w: G.linear_dgrad(dy, w),
+                      lambda dy=dy, w=w: torch.matmul(dy, w)))
+        cases.append((f"{name}.wgrad", flops, lambda dy=dy, x=x, dw=dw: G.linear_wgrad(dy, x, dw),
+                      lambda dy=dy, x=x: torch.matmul(dy.t(), x)))
+    # grouped experts: T*k rows spread uniformly over E experts, padded to 128
+    per = T * k // E
+    counts = [per] * E
+    offs_l = [0]
+    for c in counts:
+        offs_l.append(offs_l[-1] + (c + 127) // 128 * 128)
+    offs = torch.tensor(offs_l, dtype=torch.int32, device="cuda")
+    R = offs_l[-1]
+    x = bf(R, H)
+    w1 = bf(E, 2 * F, H, std=0.02)
+    w2 = bf(E, H, F, std=0.02)
+    act = bf(R, F)
+    dy2 = bf(R, H)
+    dh = bf(R, 2 * F)
+    dw1 = torch.empty(E, 2 * F, H, device="cuda", dtype=torch.bfloat16)
+    dw2 = torch.empty(E, H, F, device="cuda", dtype=torch.bfloat16)
+    f1 = 2.0 * R * 2 * F * H
+    f2 = 2.0 * R * H * F
+    cases += [
+        (f"experts.w1.fwd+swiglu {R}x{2*F}x{H}", f1, lambda: G.grouped_fwd(x, w1, offs, swiglu=True), None),
+        ("experts.w2.fwd", f2, lambda: G.grouped_fwd(act, w2, offs), None),
+        ("experts.w2.dgrad", f2, lambda: G.grouped_dgrad(dy2, w2, offs), None),
+        ("experts.w2.wgrad", f2, lambda: G.grouped_wgrad(dy2, act, offs, dw2), None),
+        ("experts.w1.dgrad", f1, lambda: G.grouped_dgrad(dh, w1, offs), None),
+        ("experts.w1.wgrad", f1, lambda: G.grouped_wgrad(dh, x, offs, dw1), None),
+    ]
+    return cases
+
+
+def run_gemm(iters):
+    pk = peaks()
+    rows = []
+    for name, flops, ours, lib in gemm_cases():
+        t = timeit(ours, iters)
+        row = {"case": name, "ms": round(t, 4), "tflops": round(flops / t / 1e9, 1),
+               "frac_of_peak": round(flops / t / 1e9 / pk["bf16_tflops"], 3)}
+        if lib is not None:
+            tl = timeit(lib, iters)
+            row["cublas_ms"] = round(tl, 4)
+            row["vs_cublas"] = round(tl / t, 3)
+        rows.append(row)
+    return rows
+
+
+def run_attn(iters, B=8, S=2048, Hq=16, Hkv=4, D=64):
+    pk = peaks()
+    T = B * S
+    qkv = bf(T, (Hq + 2 * Hkv) * D)
+    scale = 1 / math.sqrt(D)
+    o, lse = Fn.attention_fwd(qkv, B, S, Hq, Hkv, D, scale)
+    do = bf(T, Hq * D)
+    causal_flops = 4.0 * B * Hq * S * S * D / 2
+    tf = timeit(lambda: Fn.attention_fwd(qkv, B, S, Hq, Hkv, D, scale), iters)
+    tb = timeit(lambda: Fn.attention_bwd(qkv, o, lse, do, B, S, Hq, Hkv, D, scale), iters)
+    return [{"case": f"attn.fwd B{B} S{S} {Hq}q/{Hkv}kv d{D}", "ms": round(tf, 4),
+             "tflops": round(causal_flops / tf / 1e9, 1), "frac_of_peak": round(causal_flops / tf / 1e9 / pk["bf16_tflops"], 3)},
+            {"case": "attn.bwd", "ms": round(tb, 4), "tflops": round(2.5 * causal_flops / tb / 1e9, 1),
+             "frac_of_peak": round(2.5 * causal_flops / tb / 1e9 / pk["bf16_tflops"], 3)}]
+
+
+def run_mem(iters, T=16384, H=1024):
+    pk = peaks()
+    rows = []
+    x, d = bf(T, H), bf(T, H)
+    w = bf(H)
+    y, rstd, h = Fn.rmsnorm_fwd(x, w, 1e-6, d)
+    dw = torch.zeros(H, device="cuda")
+    t = timeit(lambda: Fn.rmsnorm_fwd(x, w, 1e-6, d), iters)
+    nbytes = T * H * 2 * 4
+    rows.append({"case": "add_rmsnorm.fwd", "ms": round(t, 4), "gbs": round(nbytes / t / 1e6, 1),
+                 "frac_of_peak": round(nbytes / t / 1e6 / pk["hbm_gbs"], 3)})
+    t = timeit(lambda: Fn.rmsnorm_bwd(y, h, rstd, w, 1e-6, dw, dres=d), iters)
+    nbytes = T * H * 2 * 4
+    rows.append({"case": "rmsnorm.bwd", "ms": round(t, 4), "gbs": round(nbytes / t / 1e6, 1),
+                 "frac_of_peak": round(nbytes / t / 1e6 / pk["hbm_gbs"], 3)})
+    n = 124_000_000
+    master = torch.randn(n, device="cuda")
+    m = torch.zeros(n, device="cuda")
+    v = torch.zeros(n, device="cuda")
+    g = bf(n)
+    outs = [torch.empty_like(master) for _ in range(3)]
+    pb = torch.empty(n, device="cuda", dtype=torch.bfloat16)
+    t = timeit(lambda: Fn.adamw_step(master, m, v, [g], *outs, pb, 1e-4, 0.9, 0.999, 1e-8, 0.01, 3, 1.0), iters)
+    nbytes = n * (2 + 12 + 12 + 2)
+    rows.append({"case": f"adamw {n}", "ms": round(t, 4), "gbs": round(nbytes / t / 1e6, 1),
+                 "frac_of_peak": round(nbytes / t / 1e6 / pk["hbm_gbs"], 3)})
+    logits = bf(T, 32768)
+    labels = torch.randint(0, 32768, (T,), device="cuda", dtype=torch.int32)
+    t = timeit(lambda: Fn.xent_fwd_bwd(logits, labels, 1.0 / T), iters)
+    nbytes = T * 32768 * 2 * 2
+    rows.append({"case": "xent fwd+bwd", "ms": round(t, 4), "gbs": round(nbytes / t / 1e6, 1),
+                 "frac_of_peak": round(nbytes / t / 1e6 / pk["hbm_gbs"], 3)})
+    return rows
+
+
+def main():
+    p = argparse.ArgumentParser()
+    p.add_argument("--ops", default="gemm,attn,mem")
+    p.add_argument("--iters", type=int, default=20)
+    args = p.parse_args()
+    torch.manual_seed(0)
+    out = {"peaks": peaks()}
+    ops = args.ops.split(",")
+    if "gemm" in ops:
+        out["gemm"] = run_gemm(args.iters)
+    if "attn" in ops:
+        out["attn"] = run_attn(args.iters)
+    if "mem" in ops:
+        out["mem"] = run_mem(args.iters)
+    for k, v in out.items():
+        if isinstance(v, list):
+            for r in v:
+                print(json.dumps(r))
+    print(json.dumps({"peaks": out["peaks"]}))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,379 @@
+"""Fault-tolerant per-rank trainer (one process per rank of one DP replica).
+
+    python -m shift_b200.ft.train --session S --replica R --generation G \
+        --lighthouse 127.0.0.1:PORT --root RESULTS [--model tiny|bench] [--device cpu|cuda] ...
+
+Each step: quorum (heal from a live peer if this replica is behind) ->
+synthetic microbatches -> forward/backward -> cross-replica gradient average
+(participants only; a healing replica contributes zeros) -> non-finite check
+-> commit vote -> AdamW into the next state generation -> commit flips it.
+Events go to ``<root>/<session>/events_g<generation>_r<rank>.jsonl`` with the
+reference worker's kinds (ready, phase, begin, commit, skipped, snapshot,
+state_loaded, restored, recovery_request, transport_send/recv,
+checkpoint_saved/loaded/resumed, standby_ready/activated, stopped) --
+shift_full/train.py:124-627.  Marker files in the session directory: START
+(begin training), STOP (optionally holding a step bound), ACTIVATE (leave
+standby).
+
+Gradient path: ``--reduce fused`` (CUDA) runs the cross-replica reduction
+inside the fused AdamW kernel over peer memory; ``--reduce group`` averages
+the flat gradient with the Manager's process group first (gloo on CPU, NCCL on
+GPU) -- the baseline.
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import random
+import time
+from datetime import timedelta
+from pathlib import Path
+
+_MODULE_STARTED = time.monotonic()
+
+import torch  # noqa: E402
+
+from ..engine import Engine, rng_state, set_rng_state, synthetic_batch  # noqa: E402
+from ..models.qwen_moe import MoEConfig  # noqa: E402
+from ..utils.digest import cpu_tree, digest, tensor_count  # noqa: E402
+from ..utils.events import EventLog  # noqa: E402
+from .manager import Manager, WorldSizeMode  # noqa: E402
+from .process_group import ReconfigurableGroup  # noqa: E402
+from .transport import PackedTransport  # noqa: E402
+
+
+def parse_args(argv=None):
+    p = argparse.ArgumentParser()
+    p.add_argument("--session", required=True)
+    p.add_argument("--replica", type=int, required=True)
+    p.add_argument("--generation", type=int, default=0)
+    p.add_argument("--host-ip", default="127.0.0.1")
+    p.add_argument("--lighthouse", required=True)
+    p.add_argument("--root", default="results")
+    p.add_argument("--max-seconds", type=int, default=900)
+    p.add_argument("--model", choices=["tiny", "bench"], default="tiny")
+    p.add_argument("--device", choices=["cpu", "cuda"], default="cpu")
+    p.add_argument("--backend", choices=["gloo", "nccl"], default=None)
+    p.add_argument("--reduce", choices=["group", "fused"], default="group")
+    p.add_argument("--steps", "--target-steps", dest="steps", type=int, default=1_000_000)
+    p.add_argument("--seq-len", type=int, default=128)
+    p.add_argument("--batch", type=int, default=4, help="sequences per microbatch")
+    p.add_argument("--microbatches", type=int, default=1)
+    p.add_argument("--hash-every", type=int, default=0)
+    p.add_argument("--audit-state", action="store_true")
+    p.add_argument("--fixed-batch", action="store_true")
+    p.add_argument("--data", choices=["pattern", "random"], default="random")
+    p.add_argument("--data-seed", type=int, default=0, help="uniform random ids from seed data_seed*1e6+sample")
+    p.add_argument("--lr", type=float, default=1e-4)
+    p.add_argument("--min-replicas", type=int, default=1)
+    p.add_argument("--world-size-mode", choices=["dynamic", "fixed_with_spares"], default="dynamic")
+    p.add_argument("--communication-timeout", type=float, default=30)
+    p.add_argument("--checkpoint-step", type=int, default=0)
+    p.add_argument("--checkpoint-cold", action="store_true")
+    p.add_argument("--resume-checkpoint", action="store_true")
+    p.add_argument("--standby", choices=("cpu", "gpu"))
+    p.add_argument("--bucket-size", type=int, default=64 * 1024 * 1024)
+    p.add_argument("--inject", default="", help="test fault: nonfinite@STEP | exit@STEP | slow@MS")
+    p.add_argument("--seed", type=int, default=2026)
+    return p.parse_args(argv)
+
+
+class Worker:
+    def __init__(self, args):
+        self.args = args
+        self.rank = int(os.environ.get("LOCAL_RANK", "0"))
+        self.local_world = int(os.environ.get("LOCAL_WORLD_SIZE", os.environ.get("WORLD_SIZE", "1")))
+        self.out = Path(os.environ.get("SHIFT_RESULT_DIR", str(Path(args.root) / args.session)))
+        self.out.mkdir(parents=True, exist_ok=True)
+        self.event = EventLog(self.out / f"events_g{args.generation}_r{self.rank}.jsonl", rid=args.replica,
+                              rank=self.rank, generation=args.generation,
+                              physical_node=os.environ.get("SHIFT_PHYSICAL_NODE", args.host_ip), host_ip=args.host_ip)
+        self.event.keep = False
+        if args.device == "cuda":
+            dev_index = int(os.environ.get("SHIFT_CUDA_DEVICE", self.rank))
+            torch.cuda.set_device(dev_index)
+            self.device = torch.device("cuda", dev_index)
+        else:
+            self.device = torch.device("cpu")
+        self.progress = {"updates": 0}
+        self.manager = None
+        self.boundary_rng = None
+
+    # ------------------------------------------------------------------ helpers
+    def phase(self, name, started):
+        self.event("phase", name=name, seconds=time.monotonic() - started)
+        return time.monotonic()
+
+    def marker(self, name) -> Path:
+        return self.out / name
+
+    def standby_gate(self, mode):
+        import resource
+        self.event("standby_ready", mode=mode, cpu_maxrss_kib=resource.getrusage(resource.RUSAGE_SELF).ru_maxrss,
+                   cuda_allocated_bytes=torch.cuda.memory_allocated() if self.device.type == "cuda" else 0)
+        until = time.monotonic() + self.args.max_seconds
+        while not self.marker("ACTIVATE").exists():
+            if self.marker("STOP").exists() or time.monotonic() > until:
+                raise RuntimeError("standby stopped or timed out before activation")
+            time.sleep(0.02)
+        self.event("standby_activated", mode=mode)
+
+    def rng_snapshot(self):
+        return rng_state(self.device)
+
+    def current_hashes(self, rng=None):
+        if self.device.type == "cuda":
+            torch.cuda.current_stream().synchronize()
+        rng = rng if rng is not None else self.rng_snapshot()
+        sd = self.engine.state_dict()
+        return dict(model=digest(sd["model"]), optimizer=digest(sd["optimizer"]), scheduler=digest(sd["scheduler"]),
+                    progress=digest(self.progress), cpu_rng=digest(rng["torch_rng"]), cuda_rng=digest(rng["cuda_rng"]),
+                    python_rng=digest(rng["python_rng"]))
+
+    # ------------------------------------------------------------------ state
+    def export_state(self):
+        self.event("snapshot_begin", step=self.progress["updates"])
+        if self.device.type == "cuda":
+            torch.cuda.current_stream().synchronize()
+        step = self.manager.current_step() if self.manager else self.progress["updates"]
+        assert step == self.progress["updates"], (step, self.progress)
+        rng = (self.boundary_rng["rng"] if self.boundary_rng and self.boundary_rng["step"] == step
+               else self.rng_snapshot())
+        sd = self.engine.state_dict()
+        payload = dict(model=sd["model"], optimizer=sd["optimizer"], scheduler=sd["scheduler"],
+                       progress=dict(self.progress), **rng, source_replica=self.args.replica, source_rank=self.rank,
+                       step=step)
+        payload["hashes"] = self.current_hashes(rng) if self.args.audit_state else {}
+        self.event("snapshot", step=step, hashes=payload["hashes"],
+                   optimizer_tensors=tensor_count(payload["optimizer"].get("state", {})))
+        return payload
+
+    def load_state(self, payload):
+        t0 = time.monotonic()
+        assert payload["source_rank"] == self.rank, (payload["source_rank"], self.rank)
+        assert payload["step"] == payload["progress"]["updates"]
+        if self.manager:
+            assert payload["step"] == self.manager.current_step()
+        self.engine.load_state_dict(payload)
+        self.progress.update(payload["progress"])
+        set_rng_state(payload, self.device)
+        if self.device.type == "cuda":
+            torch.cuda.current_stream().synchronize()
+        loaded = time.monotonic()
+        self.event("state_loaded", step=payload["step"], load_seconds=loaded - t0,
+                   source_replica=payload["source_replica"], source_rank=payload["source_rank"])
+        hashes = self.current_hashes() if self.args.audit_state else {}
+        matches = hashes == payload["hashes"]
+        self.event("restored", step=payload["step"], load_seconds=loaded - t0, audit_seconds=time.monotonic() - loaded,
+                   source_replica=payload["source_replica"], source_rank=payload["source_rank"], hashes_match=matches,
+                   expected_hashes=payload["hashes"], actual_hashes=hashes)
+        assert matches, "Restored state differs from source snapshot"
+
+    # ------------------------------------------------------------------ data
+    def batches(self, step):
+        a = self.args
+        data_rank = a.replica
+        out, ids = [], []
+        for micro in range(a.microbatches):
+            sample = step * (a.microbatches * 4) + micro * 4 + data_rank
+            ids.append(sample)
+            data = synthetic_batch(self.cfg, sample, a.batch, a.seq_len, a.data, seed_base=100_000 + a.data_seed * 1_000_000)
+            data = data.to(self.device, non_blocking=True)
+            out.append((data[:, :-1].contiguous(), data[:, 1:].contiguous()))
+        return out, ids
+
+    # ------------------------------------------------------------------ main
+    def run(self):
+        a = self.args
+        if a.standby == "cpu":
+            self.standby_gate("cpu")
+        started = self.phase("python_imports", _MODULE_STARTED)
+        torch.set_num_threads(1)
+        self.cfg = MoEConfig.tiny() if a.model == "tiny" else MoEConfig.bench()
+        self.engine = Engine(self.cfg, self.device, seed=a.seed, bucket_numel=a.bucket_size)
+        self.engine.optim.lr = a.lr
+        self.engine.scheduler.base_lrs = [a.lr]
+        self.engine.scheduler._last_lr = [a.lr]
+        started = self.phase("model_load", started)
+        if a.standby == "gpu":
+            self.standby_gate("gpu")
+        backend = a.backend or ("nccl" if self.device.type == "cuda" else "gloo")
+        pg = ReconfigurableGroup(backend, a.communication_timeout, self.device if backend == "nccl" else None,
+                                 prefix=f"x{self.rank}", event=self.event)
+        transport = PackedTransport(pg, self.device if backend == "nccl" else torch.device("cpu"),
+                                    timedelta(seconds=a.communication_timeout), self.event)
+        store_port = int(os.environ.get("SHIFT_STORE_PORT", "0")) or _free_port()
+        mode = WorldSizeMode.FIXED_WITH_SPARES if a.world_size_mode == "fixed_with_spares" else WorldSizeMode.DYNAMIC
+        self.manager = Manager(pg, self.load_state_for_manager, self.export_state_for_transport, a.min_replicas,
+                               f"shift{a.replica}", a.lighthouse, rank=self.rank, world_size=self.local_world,
+                               store_addr=f"{a.host_ip}:{store_port}", hostname=a.host_ip,
+                               checkpoint_transport=transport, timeout=timedelta(seconds=a.communication_timeout),
+                               world_size_mode=mode, event=self.event)
+        self.transport_on_cpu = backend == "gloo" and self.device.type == "cuda"
+        started = self.phase("manager_init", started)
+        if a.resume_checkpoint:
+            self.resume()
+        self.event("ready", hashes=self.current_hashes() if a.audit_state else {}, model=a.model,
+                   params=self.engine.store.numel, device=str(self.device), backend=backend, reduce=a.reduce,
+                   full_parameters=self.cfg.param_count())
+        deadline = time.monotonic() + a.max_seconds
+        while not self.marker("START").exists():
+            if self.marker("STOP").exists() or time.monotonic() > deadline:
+                raise RuntimeError("Stopped or timed out before START")
+            time.sleep(0.02)
+        self.loop(deadline)
+
+    def load_state_for_manager(self, payload):
+        if self.device.type == "cuda" and getattr(self, "transport_on_cpu", False):
+            payload = _to_device(payload, self.device)
+        self.load_state(payload)
+
+    def export_state_for_transport(self):
+        p = self.export_state()
+        if getattr(self, "transport_on_cpu", False):
+            p = cpu_tree(p)
+        return p
+
+    def requested_stop(self):
+        m = self.marker("STOP")
+        if not m.exists():
+            return False
+        text = m.read_text().strip()
+        return not text or self.progress["updates"] >= int(text)
+
+    def loop(self, deadline):
+        a, eng, mgr = self.args, self.engine, self.manager
+        attempts = 0
+        inject_kind, _, inject_arg = a.inject.partition("@")
+        recovery_requested = False
+        while not self.requested_stop() and time.monotonic() < deadline and self.progress["updates"] < a.steps:
+            it0 = time.monotonic()
+            if self.device.type == "cuda":
+                torch.cuda.current_stream().synchronize()
+            self.boundary_rng = dict(step=self.progress["updates"], rng=self.rng_snapshot())
+            if a.generation > 0 and not recovery_requested:
+                self.event("recovery_request", step=self.progress["updates"])
+                recovery_requested = True
+            q0 = time.monotonic()
+            mgr.start_quorum()
+            step = self.progress["updates"]
+            participants = mgr.num_participants()
+            self.event("begin", step=step, participants=participants, quorum_seconds=time.monotonic() - q0)
+            if inject_kind == "exit" and step == int(inject_arg):
+                self.event("injected_exit", step=step)
+                os._exit(17)
+            batches, sample_ids = self.batches(step)
+            t_compute = time.monotonic()
+            loss = eng.forward_backward(batches, a.batch, a.seq_len)
+            if inject_kind == "slow":
+                time.sleep(float(inject_arg) / 1000.0)
+            if inject_kind == "nonfinite" and step == int(inject_arg):
+                eng.store.grad.view(-1)[0] = float("nan")
+            # cross-replica average (participants only)
+            if a.reduce == "group":
+                g = eng.store.grad
+                if self.transport_on_cpu:
+                    gc = g.float().cpu()
+                    mgr.allreduce(gc).wait()
+                    g.copy_(gc)
+                else:
+                    mgr.allreduce(g).wait()
+                sources, scale = [g], 1.0
+            else:
+                sources, scale = self.fused_sources()
+            nonfinite = eng.optimizer_step(sources, scale)
+            finite = int(nonfinite.item()) == 0
+            if not finite:
+                mgr.report_error(RuntimeError("nonfinite gradients"))
+            t_decide = time.monotonic()
+            commit = mgr.should_commit()
+            attempts += 1
+            if commit:
+                eng.commit()
+                self.progress["updates"] += 1
+                hashes = (self.current_hashes() if (a.hash_every and self.progress["updates"] % a.hash_every == 0)
+                          else {})
+                self.event("commit", step=self.progress["updates"], updates=self.progress["updates"],
+                           participants=mgr.num_participants(), contributed=mgr.is_participating(), hashes=hashes,
+                           model_hash=hashes.get("model"), optimizer_hash=hashes.get("optimizer"),
+                           scheduler_hash=hashes.get("scheduler"), sample_ids=sample_ids, finite_gradients=finite,
+                           loss=float(loss), seconds=time.monotonic() - it0, compute_seconds=t_decide - t_compute,
+                           decision_seconds=time.monotonic() - t_decide,
+                           global_batch=a.batch * a.microbatches * mgr.num_participants())
+            else:
+                self.event("skipped", step=step, error=str(mgr.errored()), finite_gradients=finite)
+            assert mgr.current_step() == self.progress["updates"]
+            if a.checkpoint_step and self.progress["updates"] == a.checkpoint_step and commit:
+                self.save_checkpoint()
+        self.event("stopped", step=self.progress["updates"], attempts=attempts)
+        mgr.shutdown()
+        self.event.close()
+
+    def fused_sources(self):
+        raise RuntimeError("fused cross-replica reduction needs the peer-memory path (parallel.symmetric)")
+
+    # ------------------------------------------------------------------ disk checkpoint baseline
+    def save_checkpoint(self):
+        t0 = time.monotonic()
+        payload = cpu_tree(self.export_state())
+        path = self.out / f"checkpoint_r{self.rank}.pt"
+        torch.save(payload, path)
+        with path.open("rb") as h:
+            os.fsync(h.fileno())
+        self.event("checkpoint_saved", step=self.progress["updates"], seconds=time.monotonic() - t0,
+                   bytes=path.stat().st_size)
+        t1 = time.monotonic()
+        loaded = torch.load(path, weights_only=False)
+        self.engine.load_state_dict(_to_device(loaded, self.device))
+        self.event("checkpoint_loaded", step=self.progress["updates"], seconds=time.monotonic() - t1,
+                   cache="warm_after_save",
+                   hashes_match=not self.args.audit_state or self.current_hashes() == payload.get("hashes"))
+        if self.args.checkpoint_cold:
+            with path.open("rb") as h:
+                os.posix_fadvise(h.fileno(), 0, 0, os.POSIX_FADV_DONTNEED)
+            t2 = time.monotonic()
+            loaded = torch.load(path, weights_only=False)
+            self.engine.load_state_dict(_to_device(loaded, self.device))
+            self.event("checkpoint_loaded_cold", step=self.progress["updates"], seconds=time.monotonic() - t2,
+                       cache="fadvise_dontneed_advisory")
+
+    def resume(self):
+        path = self.out / f"checkpoint_r{self.rank}.pt"
+        t0 = time.monotonic()
+        payload = torch.load(path, weights_only=False)
+        self.engine.load_state_dict(_to_device(payload, self.device))
+        self.progress.update(payload["progress"])
+        set_rng_state(payload, self.device)
+        self.manager.load_state_dict({"step": payload["step"]})
+        self.event("checkpoint_resumed", step=payload["step"], seconds=time.monotonic() - t0)
+
+
+def _to_device(tree, device):
+    if isinstance(tree, torch.Tensor):
+        return tree.to(device) if tree.is_floating_point() or tree.dtype in (torch.int32, torch.int64) else tree
+    if isinstance(tree, dict):
+        return {k: (_to_device(v, device) if k not in ("torch_rng", "cuda_rng") else v) for k, v in tree.items()}
+    if isinstance(tree, list):
+        return [_to_device(v, device) for v in tree]
+    if isinstance(tree, tuple):
+        return tuple(_to_device(v, device) for v in tree)
+    return tree
+
+
+def _free_port() -> int:
+    import socket
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def main(argv=None):
+    args = parse_args(argv)
+    random.seed(args.seed + args.replica)
+    Worker(args).run()
+
+
+if __name__ == "__main__":
+    main()

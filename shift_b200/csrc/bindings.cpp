@@ -48,6 +48,21 @@ std::vector<at::Tensor> attn_fwd(const at::Tensor& qkv, int64_t B, int64_t S, in
 at::Tensor attn_bwd(const at::Tensor& qkv, const at::Tensor& o, const at::Tensor& lse, const at::Tensor& dout,
                     int64_t B, int64_t S, int64_t Hq, int64_t Hkv, double scale);
 }  // namespace attn
+namespace coll {
+at::Tensor sym_alloc(int64_t nbytes, int64_t device);
+at::Tensor ipc_handle(const at::Tensor& t);
+at::Tensor ipc_open(const at::Tensor& handle, int64_t nbytes, int64_t device);
+void fused_reduce_adamw(const std::vector<int64_t>& grad_ptrs, const std::vector<int64_t>& flag_ptrs, int64_t target,
+                        const at::Tensor& master, const at::Tensor& m, const at::Tensor& v, at::Tensor& master_out,
+                        at::Tensor& m_out, at::Tensor& v_out, at::Tensor& param_out, double lr, double beta1,
+                        double beta2, double eps, double wd, int64_t step, double grad_scale,
+                        const at::Tensor& nonfinite, const at::Tensor& status, double timeout_s);
+void flag_set(int64_t flag_ptr, int64_t value);
+void flag_wait(const std::vector<int64_t>& flag_ptrs, int64_t target, const at::Tensor& status, double timeout_s);
+void peer_copy(int64_t src_ptr, int64_t dst_ptr, int64_t nbytes);
+void pair_reduce_scatter(int64_t a_ptr, int64_t b_ptr, at::Tensor& out, const std::vector<int64_t>& flag_ptrs,
+                         int64_t target, const at::Tensor& status, double timeout_s);
+}  // namespace coll
 }  // namespace sb
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -75,4 +90,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("nonfinite_check", &sb::adam::nonfinite_check);
   m.def("attn_fwd", &sb::attn::attn_fwd);
   m.def("attn_bwd", &sb::attn::attn_bwd);
+  m.def("sym_alloc", &sb::coll::sym_alloc);
+  m.def("ipc_handle", &sb::coll::ipc_handle);
+  m.def("ipc_open", &sb::coll::ipc_open);
+  m.def("fused_reduce_adamw", &sb::coll::fused_reduce_adamw, "K1: cross-replica reduce + cast + scale + AdamW");
+  m.def("flag_set", &sb::coll::flag_set);
+  m.def("flag_wait", &sb::coll::flag_wait);
+  m.def("peer_copy", &sb::coll::peer_copy, "K10: SM-driven peer-memory copy");
+  m.def("pair_reduce_scatter", &sb::coll::pair_reduce_scatter);
 }

@@ -1,0 +1,295 @@
+// Peer-memory collectives for one NVLink/NVSwitch box (sm_100a).
+//
+// Symmetric buffers are plain cudaMalloc allocations exported with CUDA IPC;
+// peers map them once per membership (a "reconfigure" re-maps handles, it
+// does not rebuild a communicator).  Synchronisation uses system-scope
+// release/acquire flags in those buffers, and every wait is bounded: on
+// expiry the kernel records kTimeoutPeer in the status word and returns.
+//
+// K1  fused_reduce_adamw: the cross-replica gradient reduction fused with
+//     the bf16->fp32 cast, the participant normalisation and the AdamW step.
+//     Each CTA waits (bounded) until every participant has published the
+//     bucket for this step, then streams the participants' bf16 gradients
+//     straight from their HBM over NVLink (P2P loads, summed in a fixed
+//     replica order so all replicas compute bit-identical updates), applies
+//     AdamW to the fp32 master/moments and writes the next-generation state
+//     and bf16 parameters.  Replaces the reference's per-bucket
+//     manager.allreduce + optimizer.step (shift_full/train.py:420-474,574).
+// K10 peer_copy: SM-driven copy of a peer's state range into local buffers
+//     (live state transfer for heal / handoff).
+// Plus reduce-scatter / all-gather helpers for tensor parallelism.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common.cuh"
+
+namespace sb {
+namespace coll {
+
+constexpr int kMaxSrc = 8;
+
+struct SrcPtrs {
+  const __nv_bfloat16* p[kMaxSrc];
+};
+struct FlagPtrs {
+  const int* p[kMaxSrc];
+};
+
+struct AdamHyper {
+  float lr, beta1, beta2, eps, wd, bc1, bc2_sqrt, grad_scale;
+};
+
+// Wait (one thread per CTA) until every peer flag >= target.
+__device__ bool cta_wait_flags(const FlagPtrs& f, int n, int target, int* status, uint64_t timeout_ns) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    ok = 1;
+    for (int i = 0; i < n; ++i) {
+      if (f.p[i] == nullptr) continue;
+      if (!wait_flag_ge(f.p[i], target, status, timeout_ns)) {
+        ok = 0;
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  return ok != 0;
+}
+
+__global__ void __launch_bounds__(256)
+fused_reduce_adamw_kernel(SrcPtrs src, int n_src, FlagPtrs flags, int n_flags, int target,
+                          const float* __restrict__ master, const float* __restrict__ m_in,
+                          const float* __restrict__ v_in, float* __restrict__ master_out, float* __restrict__ m_out,
+                          float* __restrict__ v_out, __nv_bfloat16* __restrict__ param_out, long n, AdamHyper a,
+                          int* __restrict__ nonfinite, int* __restrict__ status, uint64_t timeout_ns) {
+  if (n_flags > 0 && !cta_wait_flags(flags, n_flags, target, status, timeout_ns)) return;
+  const long stride = static_cast<long>(gridDim.x) * blockDim.x * 8;
+  bool bad = false;
+  for (long i = (static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x) * 8; i < n; i += stride) {
+    if (i + 8 <= n) {
+      float g[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      // issue all peer loads first (they travel over NVLink), then reduce in order
+      bf16x8 raw[kMaxSrc];
+#pragma unroll
+      for (int s = 0; s < kMaxSrc; ++s)
+        if (s < n_src) {
+          const uint4 u = __ldcv(reinterpret_cast<const uint4*>(src.p[s] + i));
+          raw[s].w[0] = u.x; raw[s].w[1] = u.y; raw[s].w[2] = u.z; raw[s].w[3] = u.w;
+        }
+#pragma unroll
+      for (int s = 0; s < kMaxSrc; ++s) {
+        if (s < n_src) {
+          float f[8];
+          bf16x8_to_float(raw[s], f);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) g[q] += f[q];
+        }
+      }
+      float p[8], m[8], v[8];
+      *reinterpret_cast<float4*>(p) = *reinterpret_cast<const float4*>(master + i);
+      *reinterpret_cast<float4*>(p + 4) = *reinterpret_cast<const float4*>(master + i + 4);
+      *reinterpret_cast<float4*>(m) = *reinterpret_cast<const float4*>(m_in + i);
+      *reinterpret_cast<float4*>(m + 4) = *reinterpret_cast<const float4*>(m_in + i + 4);
+      *reinterpret_cast<float4*>(v) = *reinterpret_cast<const float4*>(v_in + i);
+      *reinterpret_cast<float4*>(v + 4) = *reinterpret_cast<const float4*>(v_in + i + 4);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float gq = g[q] * a.grad_scale;
+        bad |= !isfinite(gq);
+        p[q] = p[q] * (1.f - a.lr * a.wd);
+        m[q] = m[q] + (gq - m[q]) * (1.f - a.beta1);
+        v[q] = v[q] * a.beta2 + (1.f - a.beta2) * gq * gq;
+        const float denom = sqrtf(v[q]) / a.bc2_sqrt + a.eps;
+        p[q] = p[q] - (a.lr / a.bc1) * (m[q] / denom);
+      }
+      *reinterpret_cast<float4*>(master_out + i) = *reinterpret_cast<float4*>(p);
+      *reinterpret_cast<float4*>(master_out + i + 4) = *reinterpret_cast<float4*>(p + 4);
+      *reinterpret_cast<float4*>(m_out + i) = *reinterpret_cast<float4*>(m);
+      *reinterpret_cast<float4*>(m_out + i + 4) = *reinterpret_cast<float4*>(m + 4);
+      *reinterpret_cast<float4*>(v_out + i) = *reinterpret_cast<float4*>(v);
+      *reinterpret_cast<float4*>(v_out + i + 4) = *reinterpret_cast<float4*>(v + 4);
+      *reinterpret_cast<bf16x8*>(param_out + i) = float_to_bf16x8(p);
+    } else {
+      for (long j = i; j < n; ++j) {
+        float g = 0.f;
+        for (int s = 0; s < n_src; ++s) g += __bfloat162float(src.p[s][j]);
+        g *= a.grad_scale;
+        bad |= !isfinite(g);
+        float p = master[j] * (1.f - a.lr * a.wd);
+        const float m = m_in[j] + (g - m_in[j]) * (1.f - a.beta1);
+        const float v = v_in[j] * a.beta2 + (1.f - a.beta2) * g * g;
+        p = p - (a.lr / a.bc1) * (m / (sqrtf(v) / a.bc2_sqrt + a.eps));
+        master_out[j] = p;
+        m_out[j] = m;
+        v_out[j] = v;
+        param_out[j] = __float2bfloat16(p);
+      }
+    }
+  }
+  if (bad && nonfinite) atomicOr(nonfinite, 1);
+}
+
+// ---------------------------------------------------------------------------
+__global__ void flag_set_kernel(int* flag, int value) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) {
+    __threadfence_system();
+    st_release_sys(flag, value);
+  }
+}
+
+__global__ void flag_wait_kernel(FlagPtrs f, int n, int target, int* status, uint64_t timeout_ns) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) {
+    for (int i = 0; i < n; ++i) {
+      if (f.p[i] == nullptr) continue;
+      if (!wait_flag_ge(f.p[i], target, status, timeout_ns)) break;
+    }
+  }
+}
+
+// out[i] = src[i] for a peer (or local) range, 16-byte vectors.  K10.
+__global__ void peer_copy_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst, long n16) {
+  const long stride = static_cast<long>(gridDim.x) * blockDim.x;
+  for (long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n16; i += stride) dst[i] = src[i];
+}
+
+// Two-rank reduce-scatter of bf16 rows over peer memory: out = mine[half] + peer[half]
+// (fixed order: rank-0 operand first), optional flag wait on the peer.
+__global__ void pair_reduce_scatter_kernel(const __nv_bfloat16* __restrict__ a, const __nv_bfloat16* __restrict__ b,
+                                           __nv_bfloat16* __restrict__ out, long n8, FlagPtrs f, int n_flags,
+                                           int target, int* status, uint64_t timeout_ns) {
+  if (n_flags > 0 && !cta_wait_flags(f, n_flags, target, status, timeout_ns)) return;
+  const long stride = static_cast<long>(gridDim.x) * blockDim.x;
+  for (long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8; i += stride) {
+    float x[8], y[8];
+    bf16x8_to_float(reinterpret_cast<const bf16x8*>(a)[i], x);
+    const uint4 u = __ldcv(reinterpret_cast<const uint4*>(b) + i);
+    bf16x8 bv;
+    bv.w[0] = u.x; bv.w[1] = u.y; bv.w[2] = u.z; bv.w[3] = u.w;
+    bf16x8_to_float(bv, y);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) x[q] += y[q];
+    reinterpret_cast<bf16x8*>(out)[i] = float_to_bf16x8(x);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+static int sm_count() {
+  int dev, n;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n;
+}
+
+// Symmetric (IPC-exportable) allocation owned by the caller's tensor.
+at::Tensor sym_alloc(int64_t nbytes, int64_t device) {
+  c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  void* ptr = nullptr;
+  C10_CUDA_CHECK(cudaMalloc(&ptr, static_cast<size_t>(nbytes)));
+  C10_CUDA_CHECK(cudaMemset(ptr, 0, static_cast<size_t>(nbytes)));
+  auto opts = at::TensorOptions().dtype(at::kByte).device(at::kCUDA, static_cast<c10::DeviceIndex>(device));
+  return at::from_blob(ptr, {nbytes}, [](void* p) { cudaFree(p); }, opts);
+}
+
+// 64-byte IPC handle of the allocation that starts at t.data_ptr().
+at::Tensor ipc_handle(const at::Tensor& t) {
+  cudaIpcMemHandle_t h;
+  C10_CUDA_CHECK(cudaIpcGetMemHandle(&h, t.data_ptr()));
+  auto out = at::empty({static_cast<long>(sizeof(h))}, at::TensorOptions().dtype(at::kByte));
+  std::memcpy(out.data_ptr(), &h, sizeof(h));
+  return out;
+}
+
+// Map a peer allocation on the current device; unmapped when the tensor dies.
+at::Tensor ipc_open(const at::Tensor& handle, int64_t nbytes, int64_t device) {
+  c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  cudaIpcMemHandle_t h;
+  TORCH_CHECK(handle.numel() == static_cast<long>(sizeof(h)), "ipc_open: bad handle size");
+  std::memcpy(&h, handle.data_ptr(), sizeof(h));
+  void* ptr = nullptr;
+  C10_CUDA_CHECK(cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess));
+  auto opts = at::TensorOptions().dtype(at::kByte).device(at::kCUDA, static_cast<c10::DeviceIndex>(device));
+  return at::from_blob(ptr, {nbytes}, [](void* p) { cudaIpcCloseMemHandle(p); }, opts);
+}
+
+static FlagPtrs make_flags(const std::vector<int64_t>& ptrs) {
+  TORCH_CHECK(ptrs.size() <= static_cast<size_t>(kMaxSrc), "at most 8 peer flags");
+  FlagPtrs f{};
+  for (size_t i = 0; i < ptrs.size(); ++i) f.p[i] = reinterpret_cast<const int*>(ptrs[i]);
+  return f;
+}
+
+// K1.  grad_ptrs: device addresses (local or IPC-mapped) of the bucket's
+// gradient in each participant, in replica order.  flag_ptrs: addresses of
+// the participants' ready flags for this bucket; target: the step tag.
+void fused_reduce_adamw(const std::vector<int64_t>& grad_ptrs, const std::vector<int64_t>& flag_ptrs, int64_t target,
+                        const at::Tensor& master, const at::Tensor& m, const at::Tensor& v, at::Tensor& master_out,
+                        at::Tensor& m_out, at::Tensor& v_out, at::Tensor& param_out, double lr, double beta1,
+                        double beta2, double eps, double wd, int64_t step, double grad_scale,
+                        const at::Tensor& nonfinite, const at::Tensor& status, double timeout_s) {
+  TORCH_CHECK(!grad_ptrs.empty() && grad_ptrs.size() <= static_cast<size_t>(kMaxSrc), "1..8 gradient sources");
+  const at::cuda::CUDAGuard guard(master.device());
+  SrcPtrs src{};
+  for (size_t i = 0; i < grad_ptrs.size(); ++i) src.p[i] = reinterpret_cast<const __nv_bfloat16*>(grad_ptrs[i]);
+  FlagPtrs f = make_flags(flag_ptrs);
+  AdamHyper a;
+  a.lr = static_cast<float>(lr);
+  a.beta1 = static_cast<float>(beta1);
+  a.beta2 = static_cast<float>(beta2);
+  a.eps = static_cast<float>(eps);
+  a.wd = static_cast<float>(wd);
+  a.bc1 = static_cast<float>(1.0 - std::pow(beta1, static_cast<double>(step)));
+  a.bc2_sqrt = static_cast<float>(std::sqrt(1.0 - std::pow(beta2, static_cast<double>(step))));
+  a.grad_scale = static_cast<float>(grad_scale);
+  const long n = master.numel();
+  if (n == 0) return;
+  const long blocks = std::min<long>((n / 8 + 255) / 256 + 1, static_cast<long>(sm_count()) * 8);
+  fused_reduce_adamw_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      src, static_cast<int>(grad_ptrs.size()), f, static_cast<int>(flag_ptrs.size()), static_cast<int>(target),
+      master.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), master_out.data_ptr<float>(),
+      m_out.data_ptr<float>(), v_out.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(param_out.data_ptr()), n, a,
+      nonfinite.data_ptr<int>(), status.data_ptr<int>(), static_cast<uint64_t>(timeout_s * 1e9));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void flag_set(int64_t flag_ptr, int64_t value) {
+  flag_set_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(reinterpret_cast<int*>(flag_ptr),
+                                                                   static_cast<int>(value));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void flag_wait(const std::vector<int64_t>& flag_ptrs, int64_t target, const at::Tensor& status, double timeout_s) {
+  if (flag_ptrs.empty()) return;
+  flag_wait_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(
+      make_flags(flag_ptrs), static_cast<int>(flag_ptrs.size()), static_cast<int>(target), status.data_ptr<int>(),
+      static_cast<uint64_t>(timeout_s * 1e9));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void peer_copy(int64_t src_ptr, int64_t dst_ptr, int64_t nbytes) {
+  TORCH_CHECK(nbytes % 16 == 0 && src_ptr % 16 == 0 && dst_ptr % 16 == 0, "peer_copy: 16-byte aligned ranges");
+  const long n16 = nbytes / 16;
+  if (n16 == 0) return;
+  const long blocks = std::min<long>((n16 + 255) / 256, static_cast<long>(sm_count()) * 4);
+  peer_copy_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(reinterpret_cast<const uint4*>(src_ptr),
+                                                                          reinterpret_cast<uint4*>(dst_ptr), n16);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void pair_reduce_scatter(int64_t a_ptr, int64_t b_ptr, at::Tensor& out, const std::vector<int64_t>& flag_ptrs,
+                         int64_t target, const at::Tensor& status, double timeout_s) {
+  const long n = out.numel();
+  TORCH_CHECK(n % 8 == 0, "pair_reduce_scatter: numel % 8");
+  const long blocks = std::min<long>((n / 8 + 255) / 256, static_cast<long>(sm_count()) * 4);
+  pair_reduce_scatter_kernel<<<std::max<long>(1, blocks), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(a_ptr), reinterpret_cast<const __nv_bfloat16*>(b_ptr),
+      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), n / 8, make_flags(flag_ptrs),
+      static_cast<int>(flag_ptrs.size()), static_cast<int>(target), status.data_ptr<int>(),
+      static_cast<uint64_t>(timeout_s * 1e9));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace coll
+}  // namespace sb

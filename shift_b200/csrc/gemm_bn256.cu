@@ -1,0 +1,16 @@
+// tcgen05 GEMM instantiations for tile width 256 (see gemm_sm100.cu).
+#include "gemm_kernel.cuh"
+
+namespace sb {
+namespace gemm {
+
+void dispatch_bn256(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int hint,
+                    cudaStream_t stream) {
+  if (!a_mn && !b_mn) launch<256, false, false>(ta, tb, p, hint, stream);
+  else if (!a_mn && b_mn) launch<256, false, true>(ta, tb, p, hint, stream);
+  else if (a_mn && b_mn) launch<256, true, true>(ta, tb, p, hint, stream);
+  else TORCH_CHECK(false, "gemm: unsupported major combination (A MN-major, B K-major)");
+}
+
+}  // namespace gemm
+}  // namespace sb

@@ -100,11 +100,16 @@ class Engine:
         self.store.zero_grad()
         total = None
         self.model._accumulate = False
+        hook = self.model.layer_done_hook
         for mb, (tok, lab) in enumerate(batches):
             _, loss = self.model.forward(tok, None, lab, B, S, loss_scale=1.0 / n_tok)
+            # bucket-completion hooks fire only while the last microbatch's
+            # backward writes the final gradients
+            self.model.layer_done_hook = hook if mb == len(batches) - 1 else None
             self.model.backward()
             self.model._accumulate = True
             total = loss if total is None else total + loss
+        self.model.layer_done_hook = hook
         self.model._accumulate = False
         return total / n_tok
 

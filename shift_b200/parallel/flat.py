@@ -154,6 +154,20 @@ class FlatParams:
     def zero_grad(self):
         self.grad.zero_()
 
+    def set_grad_buffers(self, bufs: list):
+        """Use externally owned flat gradient buffers (e.g. IPC-exported), one
+        per step parity; ``select_grad`` picks the active one."""
+        for b in bufs:
+            if b.numel() != self.numel or b.dtype != self.compute_dtype:
+                raise ValueError("gradient buffer does not match the flat layout")
+        self._grad_bufs = list(bufs)
+        self._grad_views = [self._make_views(b) for b in self._grad_bufs]
+        self.select_grad(0)
+
+    def select_grad(self, i: int):
+        self.grad = self._grad_bufs[i]
+        self._gviews = self._grad_views[i]
+
     # ------------------------------------------------------------------ state
     def state_tensors(self) -> dict:
         """Current-generation tensors (views) keyed like a state dict."""

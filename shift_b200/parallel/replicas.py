@@ -1,0 +1,110 @@
+"""Multi-GPU runners on one box (one process per GPU, torchrun-launched).
+
+Data-parallel replicas reduce gradients with the fused cross-replica kernel
+(K1) over NVLink peer memory, overlapped with backward bucket by bucket; the
+optional fault-tolerance Manager takes a quorum every step and votes on the
+commit (the SHIFT step of shift_full/train.py:506-627).  Each replica
+processes its share of the fixed global batch.
+"""
+from __future__ import annotations
+
+import os
+
+import torch
+import torch.distributed as dist
+
+from ..engine import Engine, synthetic_batch
+from ..models.qwen_moe import MoEConfig
+from ..ops._ext import check_status
+from .symmetric import CrossReplicaFused, SymmetricHeap
+
+
+def _order(layer: int, layers: int) -> int:
+    if layer == -1:
+        return 0
+    if layer == -2:
+        return layers + 1
+    return layers - layer
+
+
+class ReplicaDPRunner:
+    """R replicas x 1 GPU; rank r is replica r."""
+
+    def __init__(self, cfg: MoEConfig, n_gpus: int, rank: int, local_rank: int, batch: int, seq: int,
+                 with_manager: bool = False):
+        if batch % n_gpus:
+            raise ValueError(f"global batch {batch} is not divisible by {n_gpus} replicas")
+        self.layout = f"dp{n_gpus} (replicas x 1 GPU, fused NVLink reduce+AdamW)"
+        self.cfg = cfg
+        self.rank, self.world = rank, n_gpus
+        self.device = torch.device("cuda", local_rank)
+        self.B, self.S = batch // n_gpus, seq
+        self.engine = Engine(cfg, self.device)
+        store = dist.distributed_c10d._get_default_store()
+        self.heap = SymmetricHeap(store, f"r{rank}", self.device)
+        self.fused = CrossReplicaFused(self.engine, self.heap)
+        dist.barrier()
+        self.fused.configure([f"r{i}" for i in range(n_gpus)])
+        layers = cfg.layers
+        self.engine.model.layer_done_hook = lambda layer: self.fused.on_layer_done(_order(layer, layers))
+        sl = slice(rank * self.B, (rank + 1) * self.B)
+        self.dev_batches = [synthetic_batch(cfg, i, batch, seq)[sl].to(self.device) for i in range(4)]
+        self.host = synthetic_batch(cfg, 10_000, batch, seq)[sl].contiguous().pin_memory()
+        self.manager = None
+        self.step_no = 0
+        if with_manager:
+            self._init_manager(store)
+        dist.barrier()
+
+    def _init_manager(self, store):
+        from ..ft.manager import Manager
+        from ..ft.native import LighthouseServer
+        if self.rank == 0:
+            self._lh = LighthouseServer("127.0.0.1:0", min_replicas=1, join_timeout_ms=500,
+                                        heartbeat_timeout_ms=2000, quorum_tick_ms=20)
+            store.set("bench/lighthouse", self._lh.address)
+        addr = store.get("bench/lighthouse").decode()
+        self.manager = Manager(None, None, None, 1, f"shift{self.rank}", addr, rank=0, world_size=1, store=store,
+                               local_prefix=f"/bench{self.rank}")
+
+    def _train(self, data):
+        tok, lab = data[:, :-1], data[:, 1:]
+        if self.manager is not None:
+            self.manager.start_quorum()
+        self.engine.nonfinite.zero_()
+        self.fused.begin_step(self.step_no)
+        loss = self.engine.forward_backward([(tok, lab)], self.B, self.S)
+        self.fused.finish_step()
+        commit = True
+        if self.manager is not None:
+            commit = self.manager.should_commit()
+        if commit:
+            self.engine.commit()
+        self.step_no += 1
+        return loss
+
+    def step(self, i: int):
+        return self._train(self.dev_batches[i % len(self.dev_batches)])
+
+    def step_e2e(self, i: int):
+        data = self.host.to(self.device, non_blocking=True)
+        loss = self._train(data)
+        val = loss.item()
+        return val, self.host.numel() * self.host.element_size(), 4
+
+    def close(self):
+        torch.cuda.synchronize()
+        check_status(self.device)
+        if self.manager is not None:
+            self.manager.shutdown()
+        dist.barrier()
+        self.heap.close_peers()
+
+
+def make_parallel_runner(n_gpus: int, rank: int, local_rank: int, batch: int, seq: int, cfg: MoEConfig):
+    layout = os.environ.get("SHIFT_LAYOUT", "dp")
+    if layout == "dp":
+        return ReplicaDPRunner(cfg, n_gpus, rank, local_rank, batch, seq,
+                               with_manager=os.environ.get("SHIFT_BENCH_FT", "1") == "1")
+    from .tp_pp import make_model_parallel_runner
+    return make_model_parallel_runner(layout, cfg, n_gpus, rank, local_rank, batch, seq)

@@ -1,0 +1,166 @@
+"""Symmetric peer memory over CUDA IPC, and the cross-replica fused optimizer.
+
+``SymmetricHeap``: named, IPC-exportable allocations per rank; handles are
+published in a ``torch.distributed`` store under ``sym/<owner>/<name>`` and
+peers map them once (re-mapping for a new membership is a store lookup plus
+``cudaIpcOpenMemHandle``, not a communicator rebuild).
+
+``CrossReplicaFused``: the K1 path.  Each rank keeps two IPC-exported bf16
+gradient buffers (alternating by step, so a peer can still be reading step
+s-1 while this rank writes step s) and a flag block
+``[ready[n_buckets], done[2]]``.  During backward, when a bucket's last layer
+has written its gradient, the rank publishes ``ready[b] = tag(step)`` on the
+compute stream and launches the fused reduce + AdamW for that bucket on a
+side stream; the kernel waits (bounded) for every participant's
+``ready[b]``, reads their gradients over NVLink in replica order, and writes
+the next state generation.  After the last bucket the rank publishes
+``done[parity]``; the next use of that gradient buffer first waits for
+every peer's ``done`` of two steps back.  All waits are bounded and report
+through the kernel status word.
+"""
+from __future__ import annotations
+
+import torch
+
+from ..ops._ext import ext, status_word
+
+
+class SymmetricHeap:
+    def __init__(self, store, owner: str, device: torch.device):
+        self.store = store
+        self.owner = owner
+        self.device = torch.device(device)
+        self.local: dict[str, torch.Tensor] = {}
+        self.peers: dict[tuple, torch.Tensor] = {}
+
+    def alloc(self, name: str, nbytes: int) -> torch.Tensor:
+        t = ext().sym_alloc(int(nbytes), self.device.index)
+        self.local[name] = t
+        h = ext().ipc_handle(t)
+        self.store.set(f"sym/{self.owner}/{name}", bytes(h.numpy().tobytes()) + int(nbytes).to_bytes(8, "little"))
+        return t
+
+    def open(self, owner: str, name: str) -> torch.Tensor:
+        key = (owner, name)
+        if owner == self.owner:
+            return self.local[name]
+        t = self.peers.get(key)
+        if t is None:
+            raw = self.store.get(f"sym/{owner}/{name}")
+            h = torch.frombuffer(bytearray(raw[:64]), dtype=torch.uint8)
+            nbytes = int.from_bytes(raw[64:72], "little")
+            t = ext().ipc_open(h, nbytes, self.device.index)
+            self.peers[key] = t
+        return t
+
+    def close_peers(self):
+        self.peers.clear()
+
+
+def _tag(step: int) -> int:
+    return step + 1
+
+
+class CrossReplicaFused:
+    """K1 for one rank: fused cross-replica gradient reduction + AdamW."""
+
+    def __init__(self, engine, heap: SymmetricHeap, timeout_s: float = 30.0):
+        self.engine = engine
+        self.heap = heap
+        self.timeout = timeout_s
+        st = engine.store
+        self.numel = st.numel
+        nbytes = self.numel * 2
+        self.gbuf = [heap.alloc(f"grad{i}", nbytes).view(torch.bfloat16)[: self.numel] for i in range(2)]
+        self.nb = len(st.buckets)
+        self.flags = heap.alloc("flags", 4 * (self.nb + 2) + 64).view(torch.int32)
+        st.set_grad_buffers(self.gbuf)
+        self.side = torch.cuda.Stream(device=heap.device)
+        self.peer_owners: list[str] = [heap.owner]
+        self.scale = 1.0
+        self.status = status_word(heap.device)
+        # bucket completion order (backward order: head, layers high->low, embed)
+        layers = engine.cfg.layers
+        order_of = {}
+        for s in st.specs:
+            if s.layer >= 0:
+                order_of[s.name] = layers - s.layer
+            elif s.name.startswith("embed"):
+                order_of[s.name] = layers + 1
+            else:
+                order_of[s.name] = 0
+        self.bucket_done_at = [max(order_of[n] for n in b.names) for b in st.buckets]
+        self.step = 0
+        self.launched: set[int] = set()
+        self.active = False
+
+    # ------------------------------------------------------------------ membership
+    def configure(self, owners_in_replica_order: list[str], participating: list[bool] | None = None):
+        """owners of the same shard in every replica of the quorum (replica order).
+        ``participating[i]`` False -> that replica contributes zeros (healing/spare)."""
+        self.peer_owners = list(owners_in_replica_order)
+        part = participating or [True] * len(owners_in_replica_order)
+        self.sources = [o for o, p in zip(self.peer_owners, part) if p]
+        if not 1 <= len(self.sources) <= 8:
+            raise ValueError("1..8 participating replicas supported by the fused path")
+        self.scale = 1.0 / len(self.sources)
+        self.grad_maps = {o: [self.heap.open(o, f"grad{i}").view(torch.bfloat16)[: self.numel] for i in range(2)]
+                          for o in self.peer_owners}
+        self.flag_maps = {o: self.heap.open(o, "flags").view(torch.int32) for o in self.peer_owners}
+
+    # ------------------------------------------------------------------ per step
+    def begin_step(self, step: int):
+        """Select this step's gradient buffer; make sure every peer finished
+        reading it two steps ago; zero it."""
+        self.step = step
+        par = step % 2
+        self.engine.store.select_grad(par)
+        if step >= 2:
+            ptrs = [self.flag_maps[o][self.nb + par].data_ptr() for o in self.peer_owners if o != self.heap.owner]
+            ext().flag_wait(ptrs, _tag(step - 2), self.status, self.timeout)
+        self.launched = set()
+        self.active = True
+        self.progress = -1
+
+    def on_layer_done(self, order: int):
+        """Called from the model's backward (last microbatch) as layers finish."""
+        if not self.active:
+            return
+        self.progress = max(self.progress, order)
+        for b in range(self.nb):
+            if b not in self.launched and self.bucket_done_at[b] <= self.progress:
+                self._launch(b)
+
+    def _launch(self, b: int):
+        st = self.engine.store
+        bk = st.buckets[b]
+        par = self.step % 2
+        tag = _tag(self.step)
+        my_flags = self.flags
+        ext().flag_set(my_flags[b].data_ptr(), tag)   # compute stream: grads of bucket b are written
+        ev = torch.cuda.Event()
+        ev.record()
+        with torch.cuda.stream(self.side):
+            self.side.wait_event(ev)
+            sl = slice(bk.start, bk.end)
+            grad_ptrs = [self.grad_maps[o][par][sl].data_ptr() for o in self.sources]
+            flag_ptrs = [self.flag_maps[o][b].data_ptr() for o in self.sources if o != self.heap.owner]
+            c, n = st.cur, st.nxt
+            o = self.engine.optim
+            ext().fused_reduce_adamw(grad_ptrs, flag_ptrs, tag, st.master[c][sl], st.exp_avg[c][sl],
+                                     st.exp_avg_sq[c][sl], st.master[n][sl], st.exp_avg[n][sl], st.exp_avg_sq[n][sl],
+                                     st.param[n][sl], self.engine.scheduler.get_lr(), o.beta1, o.beta2, o.eps,
+                                     o.weight_decay, st.step + 1, self.scale, self.engine.nonfinite, self.status,
+                                     self.timeout)
+        self.launched.add(b)
+
+    def finish_step(self):
+        """After backward: launch what is left, publish done, join streams."""
+        for b in range(self.nb):
+            if b not in self.launched:
+                self._launch(b)
+        cur = torch.cuda.current_stream()
+        cur.wait_stream(self.side)
+        ext().flag_set(self.flags[self.nb + self.step % 2].data_ptr(), _tag(self.step))
+        self.active = False
+        return self.engine.nonfinite

@@ -1,0 +1,159 @@
+"""Peer-memory collectives: K1 (fused cross-replica reduce + AdamW), bounded
+flag waits, K10 peer copy.  Multi-GPU cases run as child processes."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from shift_b200.ops import reference as ref
+from shift_b200.ops._ext import ext, status_word
+
+pytestmark = pytest.mark.gpu
+
+
+def test_fused_reduce_adamw_local_sources_matches_reference():
+    torch.manual_seed(0)
+    n = 100_003
+    dev = torch.device("cuda", 0)
+    master = torch.randn(n, device=dev)
+    m = torch.randn(n, device=dev) * 0.01
+    v = torch.rand(n, device=dev) * 1e-3
+    gs = [(torch.randn(n, device=dev)).to(torch.bfloat16) for _ in range(3)]
+    outs = [torch.empty_like(master) for _ in range(3)]
+    pb = torch.empty(n, device=dev, dtype=torch.bfloat16)
+    flag = torch.zeros(1, dtype=torch.int32, device=dev)
+    st = status_word(dev)
+    st.zero_()
+    ext().fused_reduce_adamw([g.data_ptr() for g in gs], [], 1, master, m, v, *outs, pb, 1e-3, 0.9, 0.999, 1e-8,
+                             0.01, 5, 1 / 3, flag, st, 5.0)
+    torch.cuda.synchronize()
+    g = (gs[0].float() + gs[1].float() + gs[2].float()) / 3
+    em, emm, ev = ref.adamw(master, m, v, g, 1e-3, 0.9, 0.999, 1e-8, 0.01, 5)
+    assert torch.allclose(outs[0], em, atol=1e-6, rtol=1e-5)
+    assert torch.allclose(outs[1], emm, atol=1e-7, rtol=1e-5)
+    assert torch.allclose(outs[2], ev, atol=1e-9, rtol=1e-4)
+    assert torch.equal(pb, outs[0].to(torch.bfloat16))
+    assert int(st[0]) == 0 and int(flag) == 0
+
+
+def test_flag_wait_times_out_with_status_and_context_survives():
+    dev = torch.device("cuda", 0)
+    flags = ext().sym_alloc(64, 0).view(torch.int32)
+    st = status_word(dev)
+    st.zero_()
+    # nothing ever sets this flag: the bounded wait must give up and report
+    ext().flag_wait([flags[0].data_ptr()], 1, st, 0.2)
+    torch.cuda.synchronize()
+    assert int(st[0]) == 2
+    st.zero_()
+    ext().flag_set(flags[0].data_ptr(), 7)
+    ext().flag_wait([flags[0].data_ptr()], 7, st, 0.2)
+    torch.cuda.synchronize()
+    assert int(st[0]) == 0
+    # K1 with an unset peer flag: records the timeout and writes nothing
+    n = 4096
+    master = torch.randn(n, device=dev)
+    out = torch.full_like(master, 123.0)
+    g = torch.randn(n, device=dev).to(torch.bfloat16)
+    nf = torch.zeros(1, dtype=torch.int32, device=dev)
+    ext().fused_reduce_adamw([g.data_ptr()], [flags[1].data_ptr()], 5, master, master, master, out, out.clone(),
+                             out.clone(), torch.empty(n, device=dev, dtype=torch.bfloat16), 1e-3, 0.9, 0.999, 1e-8,
+                             0.0, 1, 1.0, nf, st, 0.2)
+    torch.cuda.synchronize()
+    assert int(st[0]) == 2
+    assert torch.all(out == 123.0)
+    st.zero_()
+
+
+def test_peer_copy_local():
+    a = torch.randn(1 << 20, device="cuda")
+    b = torch.empty_like(a)
+    ext().peer_copy(a.data_ptr(), b.data_ptr(), a.numel() * 4)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _k1_worker(rank, world, port, q):
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from shift_b200.engine import Engine, synthetic_batch
+    from shift_b200.models.qwen_moe import MoEConfig
+    from shift_b200.parallel.replicas import _order
+    from shift_b200.parallel.symmetric import CrossReplicaFused, SymmetricHeap
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60), device_id=dev)
+    try:
+        cfg = MoEConfig.tiny()
+        B, S = 2, 128
+        eng = Engine(cfg, dev, bucket_numel=1 << 18)
+        heap = SymmetricHeap(dist.distributed_c10d._get_default_store(), f"r{rank}", dev)
+        fused = CrossReplicaFused(eng, heap, timeout_s=20)
+        dist.barrier()
+        fused.configure([f"r{i}" for i in range(world)])
+        eng.model.layer_done_hook = lambda layer: fused.on_layer_done(_order(layer, cfg.layers))
+        for step in range(3):
+            data = synthetic_batch(cfg, 100 * step + rank, B, S).to(dev)
+            eng.nonfinite.zero_()
+            fused.begin_step(step)
+            eng.forward_backward([(data[:, :-1], data[:, 1:])], B, S)
+            fused.finish_step()
+            eng.commit()
+        torch.cuda.synchronize()
+        st = int(status_word(dev)[0])
+        master = eng.store.state_tensors()["master"].cpu()
+        if rank == 0:
+            # single-process reference of the same three averaged steps
+            r = Engine(cfg, dev, bucket_numel=1 << 18)
+            grads = []
+            for step in range(3):
+                gl = []
+                for src in range(world):
+                    data = synthetic_batch(cfg, 100 * step + src, B, S).to(dev)
+                    r.forward_backward([(data[:, :-1], data[:, 1:])], B, S)
+                    gl.append(r.store.grad.clone())
+                r.optimizer_step(gl, 1.0 / world)
+                r.commit()
+                grads.append(gl)
+            q.put(("ref", r.store.state_tensors()["master"].cpu()))
+        q.put((rank, master, st))
+        dist.barrier()
+        heap.close_peers()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.multigpu
+def test_fused_cross_replica_two_gpus_bit_identical_and_matches_reference():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_k1_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = {}
+    for _ in range(world + 1):
+        item = q.get(timeout=300)
+        got[item[0]] = item
+    for p in procs:
+        p.join(60)
+        assert p.exitcode == 0
+    m0, m1 = got[0][1], got[1][1]
+    assert got[0][2] == 0 and got[1][2] == 0
+    assert torch.equal(m0, m1), "replicas diverged"
+    refm = got["ref"][1]
+    assert torch.allclose(m0, refm, atol=1e-6, rtol=1e-5)

@@ -177,6 +177,17 @@ class ManagerServer {
     if (p < 0) return p;
     maddr_ = advertise_host + ":" + std::to_string(p);
     running_ = true;
+    // First heartbeat is synchronous: once start() returns, the lighthouse
+    // counts this replica as alive, so a peer's quorum cannot form without it.
+    {
+      std::string host;
+      int port;
+      if (parse_hostport(lighthouse_, host, port)) {
+        LineClient c;
+        std::string out;
+        if (c.connect(host, port, 5000)) c.request("HB " + rid_, out, 2000);
+      }
+    }
     hb_thread_ = std::thread([this] { heartbeat_loop(); });
     return p;
   }
@@ -194,11 +205,12 @@ class ManagerServer {
     std::string host;
     int port;
     if (!parse_hostport(lighthouse_, host, port)) return;
+    c.connect(host, port, 1000);
     while (running_) {
       if (!killed_) {
         std::string out;
         if (!c.request("HB " + rid_, out, 1000)) {
-          c.connect(host, port, 200);
+          if (c.connect(host, port, 200)) c.request("HB " + rid_, out, 1000);
         }
       }
       for (int i = 0; i < hb_ms_ / 10 && running_; ++i) std::this_thread::sleep_for(std::chrono::milliseconds(10));

@@ -175,6 +175,9 @@ class Manager:
         self._quorum_id = q.quorum_id
         self._healing = False
         if heal:
+            if self._transport is None or self._load_state_dict is None:
+                raise RuntimeError(f"replica {self._replica_id} is behind (step {self._step} < {q.max_step}) "
+                                   "but has no checkpoint transport to heal with")
             self._healing = True
             self._emit("recovery_request", step=self._step, max_step=q.max_step,
                        source_replica_rank=q.recover_src_replica_rank)

@@ -60,12 +60,13 @@ class ReplicaDPRunner:
         from ..ft.manager import Manager
         from ..ft.native import LighthouseServer
         if self.rank == 0:
-            self._lh = LighthouseServer("127.0.0.1:0", min_replicas=1, join_timeout_ms=500,
+            self._lh = LighthouseServer("127.0.0.1:0", min_replicas=self.world, join_timeout_ms=500,
                                         heartbeat_timeout_ms=2000, quorum_tick_ms=20)
             store.set("bench/lighthouse", self._lh.address)
         addr = store.get("bench/lighthouse").decode()
-        self.manager = Manager(None, None, None, 1, f"shift{self.rank}", addr, rank=0, world_size=1, store=store,
-                               local_prefix=f"/bench{self.rank}")
+        # every replica must take part in every step of the benchmark
+        self.manager = Manager(None, None, None, self.world, f"shift{self.rank}", addr, rank=0, world_size=1,
+                               store=store, local_prefix=f"/bench{self.rank}")
 
     def _train(self, data):
         tok, lab = data[:, :-1], data[:, 1:]

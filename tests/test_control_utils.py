@@ -1,0 +1,103 @@
+"""Event reader (incremental, partial-line safe), subreaper orphan reaping,
+supervisor config validation and marker-driven controller helpers."""
+import json
+import os
+import subprocess
+import sys
+import textwrap
+import time
+
+import pytest
+
+from shift_b200.control.event_reader import IncrementalReader, merge, read_increment, remote_code
+from shift_b200.control.supervisor import load_config
+
+
+def test_incremental_partial_lines_and_generation_switch(tmp_path):
+    ev = tmp_path / "events_g0_r0.jsonl"
+    sup = tmp_path / "supervisor_r0.jsonl"
+    ready = b'{"kind":"ready","time":1}\n'
+    ev.write_bytes(ready)
+    sup.write_bytes(b'{"kind":"injected","time":2}\n')
+    first = read_increment(tmp_path, 0)
+    assert first["rows"][ev.name][0]["kind"] == "ready"
+    assert first["rows"][sup.name][0]["kind"] == "injected"
+    assert first["offsets"][ev.name] == len(ready)
+    restored = b'{"kind":"restored","time":3}\n'
+    with ev.open("ab") as f:
+        f.write(restored + b'{"kind":"commit","time":4')
+    second = read_increment(tmp_path, 0, first["offsets"])
+    assert [r["kind"] for r in second["rows"][ev.name]] == ["restored"]
+    assert second["offsets"][ev.name] == len(ready) + len(restored)
+    with ev.open("ab") as f:
+        f.write(b',"step":4}\n')
+    third = read_increment(tmp_path, 0, second["offsets"])
+    assert third["rows"][ev.name] == [{"kind": "commit", "time": 4, "step": 4}]
+    nxt = tmp_path / "events_g1_r0.jsonl"
+    nxt.write_bytes(b'{"kind":"ready","time":5}\n')
+    sw = read_increment(tmp_path, 1, third["offsets"])
+    assert sw["rows"][nxt.name][0]["time"] == 5
+    assert ev.name not in sw["rows"] and ev.name not in sw["offsets"]
+    # the same reader shipped as a stdlib-only program (for ssh-reached hosts)
+    out = subprocess.run([sys.executable, "-c", remote_code(tmp_path, 1, third["offsets"])], check=True,
+                         capture_output=True, text=True).stdout
+    assert json.loads(out)["rows"][nxt.name][0]["kind"] == "ready"
+
+
+def test_merge_bounds_each_kind():
+    name = "events_g0_r0.jsonl"
+    rows = [{"kind": "ready", "time": 0}] + [{"kind": "commit", "time": i + 1, "step": i} for i in range(30)]
+    cache = merge({}, {"rows": {name: rows}})
+    kinds = [r["kind"] for r in cache[name]]
+    assert kinds.count("ready") == 1 and kinds.count("commit") == 12
+    assert cache[name][-1]["step"] == 29
+
+
+def test_incremental_reader_accumulates_all_rows(tmp_path):
+    p = tmp_path / "events_g0_r0.jsonl"
+    p.write_text('{"kind":"ready","rid":0}\n{"kind":"commit","rid":0,"step":1}\n{"kind":"comm')
+    r = IncrementalReader(tmp_path)
+    assert r.poll() == 2
+    with p.open("a") as f:
+        f.write('it","rid":0,"step":2}\n')
+    assert r.poll() == 1
+    assert [x["step"] for x in r.rows("commit", rid=0)] == [1, 2]
+
+
+@pytest.mark.skipif(not sys.platform.startswith("linux"), reason="Linux subreaper")
+def test_subreaper_reaps_orphan_without_stealing_popen_status(tmp_path):
+    code = textwrap.dedent(f"""
+        import os, subprocess, sys, time
+        sys.path.insert(0, {os.getcwd()!r})
+        from shift_b200.control import process_tree as pt
+        pt.enable_subreaper()
+        assert pt.is_subreaper()
+        protected = subprocess.Popen([sys.executable, "-c", "import time; time.sleep(0.3)"])
+        # a child that forks a grandchild and exits: the grandchild is adopted by us
+        mid = subprocess.Popen([sys.executable, "-c",
+            "import os,time\\nif os.fork()==0:\\n    time.sleep(0.2); os._exit(0)\\nos._exit(0)"])
+        mid.wait()
+        time.sleep(0.6)
+        reaped = pt.reap_orphans(exclude_pids=[protected.pid], timeout=2.0)
+        assert len(reaped) == 1, reaped
+        assert protected.wait() == 0   # its status was not consumed by the reaper
+        print("ok")
+    """)
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=30)
+    assert out.returncode == 0, out.stderr
+    assert out.stdout.strip() == "ok"
+
+
+def test_supervisor_config_validation(tmp_path):
+    good = tmp_path / "g.json"
+    good.write_text(json.dumps({"train_args": ["--model", "tiny"], "nproc_per_node": 2}))
+    cfg = load_config(good)
+    assert cfg["nproc_per_node"] == 2 and cfg["entry_module"] == "shift_b200.ft.train"
+    bad = tmp_path / "b.json"
+    bad.write_text(json.dumps({"train_args": "not-a-list"}))
+    with pytest.raises(ValueError):
+        load_config(bad)
+    unknown = tmp_path / "u.json"
+    unknown.write_text(json.dumps({"train_args": [], "bogus": 1}))
+    with pytest.raises(ValueError, match="unknown config keys"):
+        load_config(unknown)

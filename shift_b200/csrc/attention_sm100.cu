@@ -1,0 +1,772 @@
+// Causal flash attention on the 5th-generation tensor cores (sm_100a).
+//
+// Layout: q/k/v are read straight from the fused QKV projection
+// [T, (Hq + 2 Hkv) * 64] with TMA (one 2D map over the whole activation), the
+// output O is written as [T, Hq * 64].  head_dim = 64, tiles of 128 queries x
+// 128 keys, GQA by mapping query head h to kv head h / (Hq / Hkv).  The
+// softmax runs in base 2 on scores pre-multiplied by scale*log2(e); the
+// per-row log-sum-exp (base 2) is saved for the backward.
+//
+// Forward (one CTA per 128 queries of one head):
+//   warp 0   TMA: Q once, then K_j / V_j into a 2-stage ring
+//   warp 1   TMEM allocation + single-thread tcgen05.mma issue:
+//              S_j = Q K_j^T   (128x128x64, TMEM, double-buffered)
+//              O_j = P_j V_j   (128x64x128, TMEM, double-buffered, fresh per block)
+//   warps 2-5 softmax, one thread per query row (= TMEM lane): reads S_j with
+//              tcgen05.ld, online max / sum, writes P_j (bf16) into 128B-swizzled
+//              shared memory for the next MMA, and folds O_{j-1} into a register
+//              accumulator with the running rescale (no TMEM read-modify-write).
+// Backward (deterministic, no atomics):
+//   dkdv kernel: one CTA per 128 keys of one KV head, looping over every
+//              query head of the group and every query block at or after the
+//              diagonal: S^T = K Q^T, dP^T = V dO^T (TMEM); P^T and
+//              dS^T = P^T (dP^T - delta) go to shared memory; dV += P^T dO,
+//              dK += dS^T Q accumulate in TMEM for the whole loop.
+//   dq kernel:   one CTA per 128 queries of one head, looping over key blocks:
+//              S = Q K^T, dP = dO V^T, dS -> shared memory, dQ += dS K in TMEM.
+//   The same 128B-swizzled tile of Q, dO or K serves both as a K-major and as
+//   an MN-major MMA operand, so each is loaded once.
+// Every mbarrier wait is bounded; on expiry the kernel records a status code
+// and winds down (waits for its own MMAs, frees TMEM) instead of hanging.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace sb {
+namespace fa {
+
+constexpr int D = 64;
+constexpr int BM = 128;
+constexpr int BN = 128;
+constexpr int kThreads = 192;
+constexpr int kTile = 128 * 128;   // bytes of one 128 x 64 bf16 tile
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct Params {
+  int B, S, Hq, Hkv;
+  float scale_log2, scale;
+  __nv_bfloat16* o;
+  float* lse;
+  const float* delta;
+  __nv_bfloat16* dqkv;
+  int dqkv_stride;
+  int o_stride;
+  int* status;
+};
+
+SB_DEVICE float ex2(float x) {
+  float y;
+  asm volatile("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// 16-byte chunk c (0..15) of row r of a [128 x 128] bf16 operand stored as two
+// K-major 128B-swizzled halves of 64 columns (16 KB each).
+SB_DEVICE uint8_t* swz_chunk(uint8_t* base, int r, int c) {
+  return base + (c >> 3) * kTile + r * 128 + (((c & 7) ^ (r & 7)) << 4);
+}
+
+SB_DEVICE uint64_t kdesc(uint32_t addr) { return make_sw128_desc(addr, 16, 1024); }
+SB_DEVICE uint64_t mndesc(uint32_t addr) { return make_sw128_desc(addr, 8192, 1024); }
+
+SB_DEVICE void named_bar(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+
+// ============================ forward ============================
+constexpr int kFwdStages = 2;
+constexpr int kFwdSmem = 1024 + kTile /*Q*/ + 2 * kFwdStages * kTile /*K,V*/ + 2 * 2 * kTile /*P x2*/ + 256;
+
+__global__ void __launch_bounds__(kThreads, 1)
+fwd_kernel(const __grid_constant__ CUtensorMap tm, Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* sm = smem_raw + (((raw + 1023) & ~1023u) - raw);
+  uint8_t* sQ = sm;
+  uint8_t* sK = sQ + kTile;
+  uint8_t* sV = sK + kFwdStages * kTile;
+  uint8_t* sP = sV + kFwdStages * kTile;      // 2 buffers x 32 KB
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sP + 4 * kTile);
+  uint64_t* q_full = bar;
+  uint64_t* kv_full = bar + 1;
+  uint64_t* kv_empty = kv_full + kFwdStages;
+  uint64_t* s_full = kv_empty + kFwdStages;
+  uint64_t* p_full = s_full + 2;
+  uint64_t* o_full = p_full + 2;
+  uint64_t* drain = o_full + 2;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(drain + 1);
+
+  const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int kvh = h / (p.Hq / p.Hkv);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int q0 = qb * BM;
+  const int tok0 = b * p.S;
+  const int n_kv = qb + 1;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < kFwdStages; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&o_full[i], 1);
+    }
+    mbar_init(drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tslot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tslot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tm);
+      mbar_arrive_expect_tx(q_full, kTile);
+      tma_load_2d(sQ, &tm, q_full, h * D, tok0 + q0);
+      for (int j = 0; j < n_kv; ++j) {
+        const int st = j % kFwdStages;
+        if (!mbar_wait(&kv_empty[st], ((j / kFwdStages) & 1) ^ 1, p.status)) break;
+        mbar_arrive_expect_tx(&kv_full[st], 2 * kTile);
+        tma_load_2d(sK + st * kTile, &tm, &kv_full[st], (p.Hq + kvh) * D, tok0 + j * BN);
+        tma_load_2d(sV + st * kTile, &tm, &kv_full[st], (p.Hq + p.Hkv + kvh) * D, tok0 + j * BN);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idS = make_idesc_bf16(BM, BN, 0, 0);
+      constexpr uint32_t idO = make_idesc_bf16(BM, D, 0, 1);
+      const uint32_t qa = smem_u32(sQ);
+      bool ok = mbar_wait(q_full, 0, p.status);
+      auto issue_s = [&](int j) -> bool {
+        const int st = j % kFwdStages;
+        if (!mbar_wait(&kv_full[st], (j / kFwdStages) & 1, p.status)) return false;
+        tc_fence_after();
+        const uint32_t ka = smem_u32(sK + st * kTile);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          umma_f16(tbase + (j & 1) * BN, kdesc(qa + kk * 32), kdesc(ka + kk * 32), idS, kk > 0);
+        umma_commit(&s_full[j & 1]);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int j = 0; j < n_kv && ok; ++j) {
+        if (j + 1 < n_kv && !issue_s(j + 1)) break;
+        if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1, p.status)) break;
+        tc_fence_after();
+        const int st = j % kFwdStages;
+        const uint32_t pa = smem_u32(sP + (j & 1) * 2 * kTile);
+        const uint32_t va = smem_u32(sV + st * kTile);
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk)
+          umma_f16(tbase + 256 + (j & 1) * D, kdesc(pa + (kk >> 2) * kTile + (kk & 3) * 32), mndesc(va + kk * 2048),
+                   idO, kk > 0);
+        umma_commit(&o_full[j & 1]);
+        umma_commit(&kv_empty[st]);
+      }
+      umma_commit(drain);
+      mbar_wait(drain, 0, p.status);
+    }
+  } else {
+    // ----------------------------- softmax -----------------------------
+    const int quarter = warp % 4;
+    const int row = quarter * 32 + lane;
+    const int q = q0 + row;
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    float m_run = -INFINITY, l_run = 0.f, m_fold = -INFINITY;
+    float o_acc[D];
+#pragma unroll
+    for (int i = 0; i < D; ++i) o_acc[i] = 0.f;
+    bool ok = true;
+    auto fold = [&](int i, float m_i) -> bool {
+      if (!mbar_wait(&o_full[i & 1], (i >> 1) & 1, p.status)) return false;
+      tc_fence_after();
+      const float a = (m_fold == -INFINITY) ? 0.f : ex2(m_fold - m_i);
+      uint32_t v[32];
+#pragma unroll
+      for (int c = 0; c < D; c += 32) {
+        tmem_ld_32x32b_x32(tbase + 256 + (i & 1) * D + c + lane_off, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int t = 0; t < 32; ++t) o_acc[c + t] = o_acc[c + t] * a + __uint_as_float(v[t]);
+      }
+      m_fold = m_i;
+      return true;
+    };
+    for (int j = 0; j < n_kv && ok; ++j) {
+      if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1, p.status)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t ts = tbase + (j & 1) * BN + lane_off;
+      const bool diag = (j == qb);
+      // pass 1: row max
+      float mx = m_run;
+      uint32_t v[32];
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        tmem_ld_32x32b_x32(ts + c, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int t = 0; t < 32; ++t) {
+          const int key = j * BN + c + t;
+          const float s = (diag && key > q) ? -INFINITY : __uint_as_float(v[t]) * p.scale_log2;
+          mx = fmaxf(mx, s);
+        }
+      }
+      const float m_prev = m_run;
+      l_run = (m_prev == -INFINITY) ? 0.f : l_run * ex2(m_prev - mx);
+      m_run = mx;
+      // pass 2: probabilities -> shared memory (bf16, swizzled)
+      uint8_t* pbuf = sP + (j & 1) * 2 * kTile;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        tmem_ld_32x32b_x32(ts + c, v);
+        tmem_wait_ld();
+        float pr[32];
+#pragma unroll
+        for (int t = 0; t < 32; ++t) {
+          const int key = j * BN + c + t;
+          const float s = __uint_as_float(v[t]) * p.scale_log2;
+          pr[t] = (diag && key > q) ? 0.f : ex2(s - mx);
+          l_run += pr[t];
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          bf16x8 pk = float_to_bf16x8(pr + 8 * u);
+          *reinterpret_cast<uint4*>(swz_chunk(pbuf, row, (c >> 3) + u)) =
+              make_uint4(pk.w[0], pk.w[1], pk.w[2], pk.w[3]);
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&p_full[j & 1]);
+      if (j >= 1 && !fold(j - 1, m_prev)) {
+        ok = false;
+        break;
+      }
+    }
+    if (ok) ok = fold(n_kv - 1, m_run);
+    if (ok) {
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      __nv_bfloat16* orow = p.o + static_cast<long>(tok0 + q) * p.o_stride + h * D;
+#pragma unroll
+      for (int c = 0; c < D; c += 8) {
+        float t8[8];
+#pragma unroll
+        for (int t = 0; t < 8; ++t) t8[t] = o_acc[c + t] * inv;
+        *reinterpret_cast<bf16x8*>(orow + c) = float_to_bf16x8(t8);
+      }
+      p.lse[(static_cast<long>(b) * p.Hq + h) * p.S + q] = m_run + log2f(l_run);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tbase, 512);
+}
+
+// ============================ backward: dK, dV ============================
+constexpr int kBwdStages = 2;
+constexpr int kDkdvSmem = 1024 + 2 * kTile /*K,V*/ + 2 * kBwdStages * kTile /*Q,dO*/ + 4 * kTile /*P^T,dS^T*/ +
+                          2 * BM * 4 * 2 /*lse,delta*/ + 256;
+
+__global__ void __launch_bounds__(kThreads, 1)
+dkdv_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtensorMap tmo, Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* sm = smem_raw + (((raw + 1023) & ~1023u) - raw);
+  uint8_t* sK = sm;
+  uint8_t* sV = sK + kTile;
+  uint8_t* sQ = sV + kTile;                       // stages x kTile
+  uint8_t* sO = sQ + kBwdStages * kTile;          // dO, stages x kTile
+  uint8_t* sP = sO + kBwdStages * kTile;          // P^T  (2 halves)
+  uint8_t* sS = sP + 2 * kTile;                   // dS^T (2 halves)
+  float* s_lse = reinterpret_cast<float*>(sS + 2 * kTile);
+  float* s_del = s_lse + BM;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(s_del + BM);
+  uint64_t* kv_full = bar;
+  uint64_t* qo_full = bar + 1;
+  uint64_t* qo_empty = qo_full + kBwdStages;
+  uint64_t* sdp_full = qo_empty + kBwdStages;
+  uint64_t* ds_full = sdp_full + 1;
+  uint64_t* pds_empty = ds_full + 1;
+  uint64_t* acc_done = pds_empty + 1;
+  uint64_t* drain = acc_done + 1;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(drain + 1);
+
+  const int kb = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int group = p.Hq / p.Hkv;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int k0 = kb * BN;
+  const int tok0 = b * p.S;
+  const int n_q = p.S / BM;
+  const int per_head = n_q - kb;
+  const int n_it = group * per_head;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int s = 0; s < kBwdStages; ++s) {
+      mbar_init(&qo_full[s], 1);
+      mbar_init(&qo_empty[s], 1);
+    }
+    mbar_init(sdp_full, 1);
+    mbar_init(ds_full, 128);
+    mbar_init(pds_empty, 1);
+    mbar_init(acc_done, 1);
+    mbar_init(drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tslot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tslot;
+  const uint32_t tS = tbase, tdP = tbase + 128, tdV = tbase + 256, tdK = tbase + 320;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tm);
+      tma_prefetch_desc(&tmo);
+      mbar_arrive_expect_tx(kv_full, 2 * kTile);
+      tma_load_2d(sK, &tm, kv_full, (p.Hq + kvh) * D, tok0 + k0);
+      tma_load_2d(sV, &tm, kv_full, (p.Hq + p.Hkv + kvh) * D, tok0 + k0);
+      for (int it = 0; it < n_it; ++it) {
+        const int h = kvh * group + it / per_head;
+        const int qb = kb + it % per_head;
+        const int st = it % kBwdStages;
+        if (!mbar_wait(&qo_empty[st], ((it / kBwdStages) & 1) ^ 1, p.status)) break;
+        mbar_arrive_expect_tx(&qo_full[st], 2 * kTile);
+        tma_load_2d(sQ + st * kTile, &tm, &qo_full[st], h * D, tok0 + qb * BM);
+        tma_load_2d(sO + st * kTile, &tmo, &qo_full[st], h * D, tok0 + qb * BM);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idS = make_idesc_bf16(BN, BM, 0, 0);   // [keys x queries], K = d
+      constexpr uint32_t idG = make_idesc_bf16(BN, D, 0, 1);    // [keys x d], K = queries
+      const uint32_t ka = smem_u32(sK), va = smem_u32(sV);
+      const uint32_t pa = smem_u32(sP), da = smem_u32(sS);
+      bool ok = mbar_wait(kv_full, 0, p.status);
+      for (int it = 0; it < n_it && ok; ++it) {
+        const int st = it % kBwdStages;
+        if (!mbar_wait(&qo_full[st], (it / kBwdStages) & 1, p.status)) break;
+        tc_fence_after();
+        const uint32_t qa = smem_u32(sQ + st * kTile), oa = smem_u32(sO + st * kTile);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          umma_f16(tS, kdesc(ka + kk * 32), kdesc(qa + kk * 32), idS, kk > 0);
+          umma_f16(tdP, kdesc(va + kk * 32), kdesc(oa + kk * 32), idS, kk > 0);
+        }
+        umma_commit(sdp_full);
+        if (!mbar_wait(ds_full, it & 1, p.status)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BM / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * kTile + (kk & 3) * 32;
+          umma_f16(tdV, kdesc(pa + off), mndesc(oa + kk * 2048), idG, (it > 0 || kk > 0) ? 1u : 0u);
+          umma_f16(tdK, kdesc(da + off), mndesc(qa + kk * 2048), idG, (it > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&qo_empty[st]);
+        umma_commit(pds_empty);
+      }
+      umma_commit(acc_done);
+      umma_commit(drain);
+      mbar_wait(drain, 0, p.status);
+    }
+  } else {
+    const int quarter = warp % 4;
+    const int row = quarter * 32 + lane;     // key row within the block
+    const int key = k0 + row;
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const int sm_tid = threadIdx.x - 64;     // 0..127
+    bool ok = true;
+    for (int it = 0; it < n_it; ++it) {
+      const int h = kvh * group + it / per_head;
+      const int qb = kb + it % per_head;
+      const int q0 = qb * BM;
+      // stage this block's lse / delta (one value per thread), then wait for S^T / dP^T
+      named_bar(1, 128);  // previous iteration finished reading s_lse / s_del
+      const long li = (static_cast<long>(b) * p.Hq + h) * p.S + q0 + sm_tid;
+      s_lse[sm_tid] = p.lse[li];
+      s_del[sm_tid] = p.delta[li];
+      named_bar(1, 128);
+      if (!mbar_wait(sdp_full, it & 1, p.status)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      if (it > 0 && !mbar_wait(pds_empty, (it - 1) & 1, p.status)) {
+        ok = false;
+        break;
+      }
+      const bool diag = (qb == kb);
+      uint32_t vs[32], vd[32];
+#pragma unroll 1
+      for (int c = 0; c < BM; c += 32) {
+        tmem_ld_32x32b_x32(tS + c + lane_off, vs);
+        tmem_ld_32x32b_x32(tdP + c + lane_off, vd);
+        tmem_wait_ld();
+        float pt[32], dst[32];
+#pragma unroll
+        for (int t = 0; t < 32; ++t) {
+          const int qq = q0 + c + t;
+          float pv = ex2(__uint_as_float(vs[t]) * p.scale_log2 - s_lse[c + t]);
+          if (diag && key > qq) pv = 0.f;
+          pt[t] = pv;
+          dst[t] = pv * (__uint_as_float(vd[t]) - s_del[c + t]);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          bf16x8 a = float_to_bf16x8(pt + 8 * u);
+          bf16x8 d = float_to_bf16x8(dst + 8 * u);
+          *reinterpret_cast<uint4*>(swz_chunk(sP, row, (c >> 3) + u)) = make_uint4(a.w[0], a.w[1], a.w[2], a.w[3]);
+          *reinterpret_cast<uint4*>(swz_chunk(sS, row, (c >> 3) + u)) = make_uint4(d.w[0], d.w[1], d.w[2], d.w[3]);
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(ds_full);
+    }
+    if (ok && mbar_wait(acc_done, 0, p.status)) {
+      tc_fence_after();
+      uint32_t v[32];
+      __nv_bfloat16* krow = p.dqkv + static_cast<long>(tok0 + key) * p.dqkv_stride + (p.Hq + kvh) * D;
+      __nv_bfloat16* vrow = p.dqkv + static_cast<long>(tok0 + key) * p.dqkv_stride + (p.Hq + p.Hkv + kvh) * D;
+#pragma unroll
+      for (int c = 0; c < D; c += 32) {
+        float f[32];
+        tmem_ld_32x32b_x32(tdK + c + lane_off, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int t = 0; t < 32; ++t) f[t] = __uint_as_float(v[t]) * p.scale;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) reinterpret_cast<bf16x8*>(krow + c)[u] = float_to_bf16x8(f + 8 * u);
+        tmem_ld_32x32b_x32(tdV + c + lane_off, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int t = 0; t < 32; ++t) f[t] = __uint_as_float(v[t]);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) reinterpret_cast<bf16x8*>(vrow + c)[u] = float_to_bf16x8(f + 8 * u);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tbase, 512);
+}
+
+// ============================ backward: dQ ============================
+constexpr int kDqSmem = 1024 + 2 * kTile /*Q,dO*/ + 2 * kBwdStages * kTile /*K,V*/ + 2 * kTile /*dS*/ + 256;
+
+__global__ void __launch_bounds__(kThreads, 1)
+dq_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtensorMap tmo, Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* sm = smem_raw + (((raw + 1023) & ~1023u) - raw);
+  uint8_t* sQ = sm;
+  uint8_t* sO = sQ + kTile;
+  uint8_t* sK = sO + kTile;
+  uint8_t* sV = sK + kBwdStages * kTile;
+  uint8_t* sS = sV + kBwdStages * kTile;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sS + 2 * kTile);
+  uint64_t* q_full = bar;
+  uint64_t* kv_full = bar + 1;
+  uint64_t* kv_empty = kv_full + kBwdStages;
+  uint64_t* sdp_full = kv_empty + kBwdStages;
+  uint64_t* ds_full = sdp_full + 1;
+  uint64_t* ds_empty = ds_full + 1;
+  uint64_t* acc_done = ds_empty + 1;
+  uint64_t* drain = acc_done + 1;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(drain + 1);
+
+  const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int kvh = h / (p.Hq / p.Hkv);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int q0 = qb * BM;
+  const int tok0 = b * p.S;
+  const int n_kv = qb + 1;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < kBwdStages; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    mbar_init(sdp_full, 1);
+    mbar_init(ds_full, 128);
+    mbar_init(ds_empty, 1);
+    mbar_init(acc_done, 1);
+    mbar_init(drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tslot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tslot;
+  const uint32_t tS = tbase, tdP = tbase + 128, tdQ = tbase + 256;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tm);
+      tma_prefetch_desc(&tmo);
+      mbar_arrive_expect_tx(q_full, 2 * kTile);
+      tma_load_2d(sQ, &tm, q_full, h * D, tok0 + q0);
+      tma_load_2d(sO, &tmo, q_full, h * D, tok0 + q0);
+      for (int j = 0; j < n_kv; ++j) {
+        const int st = j % kBwdStages;
+        if (!mbar_wait(&kv_empty[st], ((j / kBwdStages) & 1) ^ 1, p.status)) break;
+        mbar_arrive_expect_tx(&kv_full[st], 2 * kTile);
+        tma_load_2d(sK + st * kTile, &tm, &kv_full[st], (p.Hq + kvh) * D, tok0 + j * BN);
+        tma_load_2d(sV + st * kTile, &tm, &kv_full[st], (p.Hq + p.Hkv + kvh) * D, tok0 + j * BN);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idS = make_idesc_bf16(BM, BN, 0, 0);
+      constexpr uint32_t idG = make_idesc_bf16(BM, D, 0, 1);
+      const uint32_t qa = smem_u32(sQ), oa = smem_u32(sO), da = smem_u32(sS);
+      bool ok = mbar_wait(q_full, 0, p.status);
+      for (int j = 0; j < n_kv && ok; ++j) {
+        const int st = j % kBwdStages;
+        if (!mbar_wait(&kv_full[st], (j / kBwdStages) & 1, p.status)) break;
+        tc_fence_after();
+        const uint32_t ka = smem_u32(sK + st * kTile), va = smem_u32(sV + st * kTile);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          umma_f16(tS, kdesc(qa + kk * 32), kdesc(ka + kk * 32), idS, kk > 0);
+          umma_f16(tdP, kdesc(oa + kk * 32), kdesc(va + kk * 32), idS, kk > 0);
+        }
+        umma_commit(sdp_full);
+        if (!mbar_wait(ds_full, j & 1, p.status)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk)
+          umma_f16(tdQ, kdesc(da + (kk >> 2) * kTile + (kk & 3) * 32), mndesc(ka + kk * 2048), idG,
+                   (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&kv_empty[st]);
+        umma_commit(ds_empty);
+      }
+      umma_commit(acc_done);
+      umma_commit(drain);
+      mbar_wait(drain, 0, p.status);
+    }
+  } else {
+    const int quarter = warp % 4;
+    const int row = quarter * 32 + lane;
+    const int q = q0 + row;
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const long li = (static_cast<long>(b) * p.Hq + h) * p.S + q;
+    const float lse = p.lse[li];
+    const float del = p.delta[li];
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      if (!mbar_wait(sdp_full, j & 1, p.status)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      if (j > 0 && !mbar_wait(ds_empty, (j - 1) & 1, p.status)) {
+        ok = false;
+        break;
+      }
+      const bool diag = (j == qb);
+      uint32_t vs[32], vd[32];
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        tmem_ld_32x32b_x32(tS + c + lane_off, vs);
+        tmem_ld_32x32b_x32(tdP + c + lane_off, vd);
+        tmem_wait_ld();
+        float ds[32];
+#pragma unroll
+        for (int t = 0; t < 32; ++t) {
+          const int key = j * BN + c + t;
+          float pv = ex2(__uint_as_float(vs[t]) * p.scale_log2 - lse);
+          if (diag && key > q) pv = 0.f;
+          ds[t] = pv * (__uint_as_float(vd[t]) - del);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          bf16x8 d = float_to_bf16x8(ds + 8 * u);
+          *reinterpret_cast<uint4*>(swz_chunk(sS, row, (c >> 3) + u)) = make_uint4(d.w[0], d.w[1], d.w[2], d.w[3]);
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(ds_full);
+    }
+    if (ok && mbar_wait(acc_done, 0, p.status)) {
+      tc_fence_after();
+      uint32_t v[32];
+      __nv_bfloat16* qrow = p.dqkv + static_cast<long>(tok0 + q) * p.dqkv_stride + h * D;
+#pragma unroll
+      for (int c = 0; c < D; c += 32) {
+        float f[32];
+        tmem_ld_32x32b_x32(tdQ + c + lane_off, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int t = 0; t < 32; ++t) f[t] = __uint_as_float(v[t]) * p.scale;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) reinterpret_cast<bf16x8*>(qrow + c)[u] = float_to_bf16x8(f + 8 * u);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tbase, 512);
+}
+
+// delta[b,h,q] = sum_d dO * O
+__global__ void delta_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout,
+                             float* __restrict__ delta, int B, int S, int Hq) {
+  const long i = static_cast<long>(blockIdx.x) * (blockDim.x / 8) + threadIdx.x / 8;
+  const int sub = threadIdx.x % 8;
+  const long n = static_cast<long>(B) * S * Hq;
+  if (i >= n) return;
+  const long tok = i / Hq;
+  const int h = static_cast<int>(i % Hq);
+  const long off = tok * Hq * D + h * D + sub * 8;
+  float a[8], g[8];
+  bf16x8_to_float(*reinterpret_cast<const bf16x8*>(o + off), a);
+  bf16x8_to_float(*reinterpret_cast<const bf16x8*>(dout + off), g);
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) s += a[j] * g[j];
+  s += __shfl_xor_sync(0xffffffffu, s, 1);
+  s += __shfl_xor_sync(0xffffffffu, s, 2);
+  s += __shfl_xor_sync(0xffffffffu, s, 4);
+  if (sub == 0) {
+    const long bb = tok / S, q = tok % S;
+    delta[(bb * Hq + h) * S + q] = s;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeFn encode_fn() {
+  static EncodeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q);
+    TORCH_CHECK(e == cudaSuccess && q == cudaDriverEntryPointSuccess && ptr, "cannot resolve cuTensorMapEncodeTiled");
+    fn = reinterpret_cast<EncodeFn>(ptr);
+  });
+  return fn;
+}
+
+// [rows, cols] bf16 row-major with row stride ld; box 64 x 128, 128B swizzle.
+static CUtensorMap tile_map(const void* base, int64_t rows, int64_t cols, int64_t ld) {
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0 && (ld * 2) % 16 == 0, "attention: TMA alignment");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
+  cuuint32_t box[2] = {64, 128};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "attention: cuTensorMapEncodeTiled failed ", static_cast<int>(r));
+  return m;
+}
+
+static Params base_params(const at::Tensor& qkv, int64_t B, int64_t S, int64_t Hq, int64_t Hkv, double scale,
+                          const at::Tensor& status) {
+  TORCH_CHECK(qkv.scalar_type() == at::kBFloat16 && qkv.stride(-1) == 1, "attention: bf16 qkv");
+  TORCH_CHECK(qkv.size(-1) == (Hq + 2 * Hkv) * D, "attention: qkv width must be (Hq + 2 Hkv) * 64");
+  TORCH_CHECK(Hq % Hkv == 0, "attention: Hq % Hkv");
+  TORCH_CHECK(S % 128 == 0, "attention: sequence length must be a multiple of 128");
+  TORCH_CHECK(qkv.numel() / qkv.size(-1) == B * S, "attention: token count");
+  Params p{};
+  p.B = static_cast<int>(B);
+  p.S = static_cast<int>(S);
+  p.Hq = static_cast<int>(Hq);
+  p.Hkv = static_cast<int>(Hkv);
+  p.scale = static_cast<float>(scale);
+  p.scale_log2 = static_cast<float>(scale) * kLog2e;
+  p.status = status.data_ptr<int>();
+  return p;
+}
+
+std::vector<at::Tensor> fwd(const at::Tensor& qkv, int64_t B, int64_t S, int64_t Hq, int64_t Hkv, double scale,
+                            const at::Tensor& status) {
+  const at::cuda::CUDAGuard guard(qkv.device());
+  Params p = base_params(qkv, B, S, Hq, Hkv, scale, status);
+  auto o = at::empty({B * S, Hq * D}, qkv.options());
+  auto lse = at::empty({B, Hq, S}, qkv.options().dtype(at::kFloat));
+  p.o = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
+  p.o_stride = static_cast<int>(Hq * D);
+  p.lse = lse.data_ptr<float>();
+  CUtensorMap tm = tile_map(qkv.data_ptr(), B * S, qkv.size(-1), qkv.stride(-2));
+  static bool cfg = false;
+  if (!cfg) {
+    cudaFuncSetAttribute(fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem);
+    cfg = true;
+  }
+  dim3 grid(static_cast<unsigned>(S / BM), static_cast<unsigned>(Hq), static_cast<unsigned>(B));
+  fwd_kernel<<<grid, kThreads, kFwdSmem, at::cuda::getCurrentCUDAStream()>>>(tm, p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {o, lse};
+}
+
+at::Tensor bwd(const at::Tensor& qkv, const at::Tensor& o, const at::Tensor& lse, const at::Tensor& dout, int64_t B,
+               int64_t S, int64_t Hq, int64_t Hkv, double scale, const at::Tensor& status) {
+  const at::cuda::CUDAGuard guard(qkv.device());
+  TORCH_CHECK(dout.is_contiguous() && o.is_contiguous(), "attention bwd: contiguous O / dO");
+  Params p = base_params(qkv, B, S, Hq, Hkv, scale, status);
+  auto dqkv = at::empty({B * S, (Hq + 2 * Hkv) * D}, qkv.options());
+  auto delta = at::empty({B, Hq, S}, qkv.options().dtype(at::kFloat));
+  p.lse = const_cast<float*>(lse.data_ptr<float>());
+  p.delta = delta.data_ptr<float>();
+  p.dqkv = reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr());
+  p.dqkv_stride = static_cast<int>(dqkv.stride(-2));
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const long n = B * S * Hq;
+  delta_kernel<<<(n + 31) / 32, 256, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(o.data_ptr()),
+                                                  reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()),
+                                                  delta.data_ptr<float>(), (int)B, (int)S, (int)Hq);
+  CUtensorMap tm = tile_map(qkv.data_ptr(), B * S, qkv.size(-1), qkv.stride(-2));
+  CUtensorMap tmo = tile_map(dout.data_ptr(), B * S, dout.size(-1), dout.stride(-2));
+  static bool cfg = false;
+  if (!cfg) {
+    cudaFuncSetAttribute(dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDkdvSmem);
+    cudaFuncSetAttribute(dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDqSmem);
+    cfg = true;
+  }
+  dim3 g1(static_cast<unsigned>(S / BN), static_cast<unsigned>(Hkv), static_cast<unsigned>(B));
+  dkdv_kernel<<<g1, kThreads, kDkdvSmem, stream>>>(tm, tmo, p);
+  dim3 g2(static_cast<unsigned>(S / BM), static_cast<unsigned>(Hq), static_cast<unsigned>(B));
+  dq_kernel<<<g2, kThreads, kDqSmem, stream>>>(tm, tmo, p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return dqkv;
+}
+
+}  // namespace fa
+}  // namespace sb

@@ -43,11 +43,12 @@ void adamw_step(const at::Tensor& master, const at::Tensor& m, const at::Tensor&
                 const c10::optional<at::Tensor>& nonfinite);
 void nonfinite_check(const at::Tensor& x, at::Tensor& flag);
 }  // namespace adam
-namespace attn {
-std::vector<at::Tensor> attn_fwd(const at::Tensor& qkv, int64_t B, int64_t S, int64_t Hq, int64_t Hkv, double scale);
-at::Tensor attn_bwd(const at::Tensor& qkv, const at::Tensor& o, const at::Tensor& lse, const at::Tensor& dout,
-                    int64_t B, int64_t S, int64_t Hq, int64_t Hkv, double scale);
-}  // namespace attn
+namespace fa {
+std::vector<at::Tensor> fwd(const at::Tensor& qkv, int64_t B, int64_t S, int64_t Hq, int64_t Hkv, double scale,
+                            const at::Tensor& status);
+at::Tensor bwd(const at::Tensor& qkv, const at::Tensor& o, const at::Tensor& lse, const at::Tensor& dout, int64_t B,
+               int64_t S, int64_t Hq, int64_t Hkv, double scale, const at::Tensor& status);
+}  // namespace fa
 namespace coll {
 at::Tensor sym_alloc(int64_t nbytes, int64_t device);
 at::Tensor ipc_handle(const at::Tensor& t);
@@ -88,8 +89,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("xent_fwd_bwd", &sb::xent::xent_fwd_bwd);
   m.def("adamw_step", &sb::adam::adamw_step);
   m.def("nonfinite_check", &sb::adam::nonfinite_check);
-  m.def("attn_fwd", &sb::attn::attn_fwd);
-  m.def("attn_bwd", &sb::attn::attn_bwd);
+  m.def("attn_fwd", &sb::fa::fwd, "tcgen05 causal flash attention forward");
+  m.def("attn_bwd", &sb::fa::bwd, "tcgen05 causal flash attention backward (dK/dV + dQ kernels)");
   m.def("sym_alloc", &sb::coll::sym_alloc);
   m.def("ipc_handle", &sb::coll::ipc_handle);
   m.def("ipc_open", &sb::coll::ipc_open);

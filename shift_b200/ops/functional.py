@@ -9,7 +9,7 @@ from __future__ import annotations
 import torch
 
 from . import reference as ref
-from ._ext import ext
+from ._ext import ext, status_word
 
 
 # ----------------------------------------------------------------------------- RMSNorm
@@ -57,7 +57,7 @@ def rope_(qkv, cos, sin, S, n_rot_heads, head_dim, inverse=False):
 def attention_fwd(qkv, B, S, Hq, Hkv, D, scale):
     """Returns (o [T, Hq*D], lse)."""
     if qkv.is_cuda:
-        o, lse = ext().attn_fwd(qkv, B, S, Hq, Hkv, scale)
+        o, lse = ext().attn_fwd(qkv, B, S, Hq, Hkv, scale, status_word(qkv.device))
         return o, lse
     T = qkv.shape[0]
     q = qkv[:, : Hq * D].view(T, Hq, D)
@@ -68,7 +68,7 @@ def attention_fwd(qkv, B, S, Hq, Hkv, D, scale):
 
 def attention_bwd(qkv, o, lse, do, B, S, Hq, Hkv, D, scale):
     if qkv.is_cuda:
-        return ext().attn_bwd(qkv, o, lse, do, B, S, Hq, Hkv, scale)
+        return ext().attn_bwd(qkv, o, lse, do, B, S, Hq, Hkv, scale, status_word(qkv.device))
     T = qkv.shape[0]
 
     def f(x):

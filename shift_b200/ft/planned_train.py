@@ -1,0 +1,243 @@
+"""Role-aware trainer for planned handoff (roles A, B, C; variants p1f, p2).
+
+    python -m shift_b200.ft.planned_train --planned-role A|B|C --planned-variant p1f|p2 \
+        --coord HOST:PORT --lighthouse-host HOST --lighthouse-port L [trainer flags]
+
+Epoch e uses the lighthouse at ``L + 10*e`` (``L + 10*e + 1`` for the A+B
+fallback epoch of a rejected P2 relay) and Manager stores on their own ports,
+as the reference moves to 31410 / 31411 (shift_full/planned_handoff.py:192,
+shift_full/overlap_handoff.py:184-199).  A keeps logical replica id 0; B and
+its replacement C both carry logical id 1, so C consumes exactly the data
+B would have consumed (fixed batch).  Commit events carry the epoch and the
+physical members.  Mirrors shift_full/planned_train.py.
+"""
+from __future__ import annotations
+
+import os
+import time
+from datetime import timedelta
+
+import torch
+
+from ..engine import rng_state, set_rng_state
+from .handoff import Coordinator, OverlapHandoff, PlannedHandoff
+from .manager import Manager, WorldSizeMode
+from .process_group import ReconfigurableGroup
+from .train import Worker, _free_port, parse_args as base_parse
+from .transport import PackedTransport
+
+
+def parse_args(argv=None):
+    import argparse
+    extra = argparse.ArgumentParser(add_help=False)
+    extra.add_argument("--planned-role", choices=["A", "B", "C"], required=True)
+    extra.add_argument("--planned-variant", choices=["p0", "p1", "p1d", "p1f", "p2", "steady"], default="p1f")
+    extra.add_argument("--planned-source", choices=["A", "B"], default="B")
+    extra.add_argument("--planned-inject", default="healthy",
+                       choices=["healthy", "prepare-fail", "ready-timeout", "stale-state", "relay-reject",
+                                "slow-compute"])
+    extra.add_argument("--planned-slow-ms", type=float, default=250)
+    extra.add_argument("--planned-round", type=int, default=0)
+    extra.add_argument("--coord", required=True)
+    extra.add_argument("--lighthouse-host", default="127.0.0.1")
+    extra.add_argument("--lighthouse-port", type=int, required=True)
+    extra.add_argument("--mover", choices=["auto", "ipc", "packed"], default="auto")
+    known, rest = extra.parse_known_args(argv)
+    args = base_parse(rest + ["--lighthouse", f"{known.lighthouse_host}:{known.lighthouse_port}"])
+    for k, v in vars(known).items():
+        setattr(args, k, v)
+    return args
+
+
+class PlannedWorker(Worker):
+    def __init__(self, args):
+        super().__init__(args)
+        self.role = args.planned_role
+        self.logical_rid = 0 if self.role == "A" else 1
+        self.forward_calls = 0
+
+    def manifest(self):
+        return {"numel": self.engine.store.numel, "specs": [(s.name, list(s.shape)) for s in self.engine.store.specs],
+                "optimizer_groups": [{"betas": [self.engine.optim.beta1, self.engine.optim.beta2],
+                                      "eps": self.engine.optim.eps, "weight_decay": self.engine.optim.weight_decay}]}
+
+    def rng_tail(self):
+        return dict(rng_state(self.device), progress=dict(self.progress), step=self.progress["updates"],
+                    source_rank=self.rank)
+
+    def apply_tail(self, tail):
+        set_rng_state(tail, self.device)
+        return tail
+
+    # ------------------------------------------------------------------ managers per epoch
+    def make_manager(self, epoch: int, members: str = "AB"):
+        a = self.args
+        port = a.lighthouse_port + 10 * epoch + (1 if members == "AB" and epoch > a.planned_round else 0)
+        backend = a.backend or ("nccl" if self.device.type == "cuda" else "gloo")
+        pg = ReconfigurableGroup(backend, a.communication_timeout, self.device if backend == "nccl" else None,
+                                 prefix=f"x{self.rank}e{epoch}", event=self.event)
+        transport = PackedTransport(pg, self.device if backend == "nccl" else torch.device("cpu"),
+                                    timedelta(seconds=a.communication_timeout), self.event)
+        rid = self.logical_rid
+        store_port = int(os.environ.get("SHIFT_STORE_PORT", "0"))
+        store_port = (store_port + 100 * (epoch + 1) + 7 * (members == "AB")) if store_port else _free_port()
+        m = Manager(pg, self.load_state_for_manager, self.export_state_for_transport, 2, f"shift{rid}",
+                    f"{a.lighthouse_host}:{port}", rank=self.rank, world_size=self.local_world,
+                    store_addr=f"{a.host_ip}:{store_port}", hostname=a.host_ip, checkpoint_transport=transport,
+                    timeout=timedelta(seconds=a.communication_timeout),
+                    world_size_mode=WorldSizeMode.FIXED_WITH_SPARES, event=self.event)
+        m._shift_epoch = epoch
+        m.load_state_dict({"step": self.progress["updates"]})   # a new epoch continues the committed step count
+        return m
+
+    def load_state(self, payload):
+        if payload.get("_inplace"):
+            # the state mover already wrote the flat buffers; apply the rest
+            self.engine.scheduler.load_state_dict(payload["scheduler"])
+            self.engine.store.step = int(payload["step"])
+            self.progress.update(payload["progress"])
+            set_rng_state(payload, self.device)
+            hashes = self.current_hashes() if self.args.audit_state else {}
+            ok = hashes == payload.get("hashes", {})
+            self.event("restored", step=payload["step"], source_replica=payload["source_replica"],
+                       source_rank=payload["source_rank"], hashes_match=ok, expected_hashes=payload.get("hashes"),
+                       actual_hashes=hashes, mode="ipc")
+            assert ok, "Restored state differs from source snapshot"
+            return
+        return super().load_state(payload)
+
+    def batches(self, step):
+        a = self.args
+        out, ids = [], []
+        from ..engine import synthetic_batch
+        for micro in range(a.microbatches):
+            sample = step * (a.microbatches * 4) + micro * 4 + self.logical_rid
+            ids.append(sample)
+            data = synthetic_batch(self.cfg, sample, a.batch, a.seq_len, a.data,
+                                   seed_base=100_000 + a.data_seed * 1_000_000).to(self.device)
+            out.append((data[:, :-1].contiguous(), data[:, 1:].contiguous()))
+        return out, ids
+
+    # ------------------------------------------------------------------ run
+    def run(self):
+        from ..engine import Engine
+        from ..models.qwen_moe import MoEConfig
+        a = self.args
+        torch.set_num_threads(1)
+        self.cfg = MoEConfig.tiny() if a.model == "tiny" else MoEConfig.bench()
+        self.engine = Engine(self.cfg, self.device, seed=a.seed, bucket_numel=a.bucket_size)
+        self.engine.optim.lr = a.lr
+        self.engine.scheduler.base_lrs = [a.lr]
+        self.engine.scheduler._last_lr = [a.lr]
+        prefix = f"round/{a.planned_round}" if a.planned_round else ""
+        self.coord = Coordinator(a.coord, prefix)
+        mover = a.mover if a.mover != "auto" else ("ipc" if self.device.type == "cuda" else "packed")
+        cls = OverlapHandoff if a.planned_variant == "p2" else PlannedHandoff
+        self.handoff = cls(self.role, a.planned_variant, self.rank, self.local_world, self.coord, self.event,
+                           self.export_state, self.load_state, self.progress, self.manifest, self.device, mover,
+                           round_=a.planned_round, source=a.planned_source, inject=a.planned_inject)
+        self.handoff.engine = self.engine
+        self.handoff.rng_tail = self.rng_tail
+        self.transport_on_cpu = False
+        base_epoch = a.planned_round
+        if self.role == "C":
+            self.event("ready", role="C", planned_variant=a.planned_variant)
+            ok = self.handoff.ready_receiver()
+            if not ok:
+                self.event("stopped", step=self.progress["updates"], role="C", cancelled=True)
+                self.event.close()
+                return
+            self.manager = self.make_manager(base_epoch + 1, "AC")
+            self.manager.load_state_dict({"step": self.progress["updates"]})
+            self.event("planned_epoch_activated", step=self.progress["updates"], epoch=base_epoch + 1)
+        else:
+            self.manager = self.make_manager(base_epoch, "AB")
+            self.event("ready", role=self.role, planned_variant=a.planned_variant,
+                       hashes=self.current_hashes() if a.audit_state else {})
+            deadline = time.monotonic() + a.max_seconds
+            while not self.marker("START").exists():
+                if self.marker("STOP").exists() or time.monotonic() > deadline:
+                    raise RuntimeError("Stopped or timed out before START")
+                time.sleep(0.02)
+        self.loop_planned(time.monotonic() + a.max_seconds)
+
+    def requested_stop(self):
+        if super().requested_stop():
+            return True
+        m = self.marker("TRAIN_UNTIL")
+        return m.exists() and self.progress["updates"] >= int(m.read_text().strip() or 0)
+
+    def loop_planned(self, deadline):
+        a, eng = self.args, self.engine
+        attempts = 0
+        while not self.requested_stop() and time.monotonic() < deadline and self.progress["updates"] < a.steps:
+            it0 = time.monotonic()
+            self.boundary_rng = dict(step=self.progress["updates"], rng=self.rng_snapshot())
+            if self.role != "C":
+                mgr, retired = self.handoff.boundary(self.manager)
+                if retired:
+                    self.event("stopped", step=self.progress["updates"], role=self.role, retired=True)
+                    self.event.close()
+                    return
+                if mgr is None:
+                    mgr = self.make_manager(self.handoff.gate.epoch, "AC")
+                    mgr.load_state_dict({"step": self.progress["updates"]})
+                    self.event("planned_epoch_activated", step=self.progress["updates"],
+                               epoch=self.handoff.gate.epoch)
+                self.manager = mgr
+            mgr = self.manager
+            mgr.start_quorum()
+            step = self.progress["updates"]
+            self.event("begin", step=step, participants=mgr.num_participants())
+            batches, sample_ids = self.batches(step)
+            relay = a.planned_variant == "p2" and self.handoff.is_relay_step()
+            t_c = time.monotonic()
+            if relay and self.role == "C":
+                eng.store.zero_grad()
+                loss = torch.zeros(())
+            else:
+                loss = eng.forward_backward(batches, a.batch, a.seq_len)
+                self.forward_calls += 1
+                if a.planned_inject == "slow-compute":
+                    time.sleep(a.planned_slow_ms / 1000.0)
+            if relay:
+                mgr, retired = self.handoff.at_gradient(mgr, eng.store.grad, self.make_manager, sample_ids,
+                                                        self.apply_tail)
+                if retired:
+                    self.event("stopped", step=self.progress["updates"], role=self.role, retired=True)
+                    self.event.close()
+                    return
+                self.manager = mgr
+                self.event("planned_ac_outer_begin", step=step)
+            mgr.allreduce(eng.store.grad).wait()
+            nonfinite = eng.optimizer_step([eng.store.grad], 1.0)
+            if int(nonfinite.item()):
+                mgr.report_error(RuntimeError("nonfinite gradients"))
+            commit = mgr.should_commit()
+            attempts += 1
+            if commit:
+                eng.commit()
+                self.progress["updates"] += 1
+                hashes = self.current_hashes() if (a.hash_every and self.progress["updates"] % a.hash_every == 0) else {}
+                self.event("commit", step=self.progress["updates"], participants=mgr.num_participants(),
+                           contributed=mgr.is_participating(), hashes=hashes, sample_ids=sample_ids,
+                           loss=float(loss), seconds=time.monotonic() - it0, compute_seconds=time.monotonic() - t_c,
+                           forward_calls=self.forward_calls, relay_step=relay,
+                           global_batch=a.batch * a.microbatches * mgr.num_participants(),
+                           **self.handoff.commit_fields(mgr))
+                self.handoff.committed()
+            else:
+                self.event("skipped", step=step, error=str(mgr.errored()))
+        self.event("stopped", step=self.progress["updates"], attempts=attempts, role=self.role)
+        self.handoff.cleanup_cancel.set()
+        self.manager.shutdown()
+        self.event.close()
+
+
+def main(argv=None):
+    args = parse_args(argv)
+    PlannedWorker(args).run()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,50 @@
+"""Planned handoff: EpochGate fencing rules and the P1f / P2 protocols end to
+end on CPU (tiny MoE, gloo, C++ lighthouses, one coordination store)."""
+import pytest
+
+from shift_b200.control.planned import PlannedSession
+from shift_b200.ft.handoff import EpochGate
+
+
+def test_epoch_gate_fence_rules():
+    g = EpochGate()
+    assert g.cancel() == ("A", "B")
+    with pytest.raises(ValueError):
+        g.activate(2, 5, 5, True)          # skipped epoch
+    with pytest.raises(ValueError):
+        g.activate(1, 5, 4, True)          # stale state
+    with pytest.raises(ValueError):
+        g.activate(1, 5, 5, False)         # unready target
+    g.activate(1, 5, 5, True)
+    assert g.members == ("A", "C") and g.epoch == 1
+    g.authorize("A", 1)
+    g.authorize("C", 1)
+    with pytest.raises(ValueError):
+        g.authorize("B", 1)                # retired owner
+    with pytest.raises(ValueError):
+        g.authorize("A", 0)                # old epoch
+    with pytest.raises(ValueError):
+        g.cancel()                         # cannot cancel after activation
+
+
+@pytest.mark.parametrize("variant", ["p1f", "p2"])
+def test_planned_handoff_healthy(tmp_path, variant):
+    s = PlannedSession(tmp_path, variant, variant=variant)
+    res = s.run(post_steps=3)
+    assert res["returncodes"] == {"A": 0, "B": 0, "C": 0}
+    failed = {k: v for k, v in res["checks"].items() if not v["pass"]}
+    assert res["pass"], failed
+    assert res["handoff_interval_s"] > 0
+
+
+def test_p2_relay_rejected_recovers_ab_in_new_epoch(tmp_path):
+    s = PlannedSession(tmp_path, "rej", variant="p2", scenario="relay-reject")
+    res = s.run(post_steps=3)
+    assert res["checks"]["ab_recovered_new_epoch"]["pass"]
+    assert res["checks"]["c_effective_commits_zero"]["pass"]
+
+
+def test_prepare_failure_cancels_and_old_epoch_continues(tmp_path):
+    s = PlannedSession(tmp_path, "pf", variant="p1f", scenario="prepare-fail")
+    res = s.run(post_steps=3)
+    assert res["cancelled"] and res["pass"]

@@ -112,6 +112,7 @@ class Manager:
         self._thread_exc: Optional[BaseException] = None
         self._shift_epoch = 0
         self._server = None
+        self.on_quorum: Optional[Callable] = None
         # replica-local store: rank 0 hosts it unless given
         self._own_store = None
         if store is None:
@@ -174,6 +175,9 @@ class Manager:
                                quorum_id=q.quorum_id)
         self._quorum_id = q.quorum_id
         self._healing = False
+        if self.on_quorum is not None:
+            # e.g. re-map the fused peer-memory reduction to this membership
+            self.on_quorum(q, up, changed)
         if heal:
             if self._transport is None or self._load_state_dict is None:
                 raise RuntimeError(f"replica {self._replica_id} is behind (step {self._step} < {q.max_step}) "

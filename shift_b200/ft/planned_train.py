@@ -73,11 +73,25 @@ class PlannedWorker(Worker):
     def make_manager(self, epoch: int, members: str = "AB"):
         a = self.args
         port = a.lighthouse_port + 10 * epoch + (1 if members == "AB" and epoch > a.planned_round else 0)
-        backend = a.backend or ("nccl" if self.device.type == "cuda" else "gloo")
-        pg = ReconfigurableGroup(backend, a.communication_timeout, self.device if backend == "nccl" else None,
-                                 prefix=f"x{self.rank}e{epoch}", event=self.event)
-        transport = PackedTransport(pg, self.device if backend == "nccl" else torch.device("cpu"),
-                                    timedelta(seconds=a.communication_timeout), self.event)
+        if self.device.type == "cuda":
+            # fused peer-memory reduction + IPC healing: a new epoch only re-maps handles
+            from .fused import PeerStateTransport, QuorumFusedReducer
+            if getattr(self, "reducer", None) is None:
+                self.reducer = QuorumFusedReducer(self.engine, self.device, self.role, a.generation, self.rank,
+                                                  a.communication_timeout)
+                layers = self.cfg.layers
+                from ..parallel.replicas import _order
+                self.engine.model.layer_done_hook = (
+                    lambda layer: self.reducer.fused.on_layer_done(_order(layer, layers)))
+            pg = None
+            transport = PeerStateTransport(self.engine, self.device, self.reducer.owner, self.event,
+                                           lambda: self.manager)
+        else:
+            backend = a.backend or "gloo"
+            pg = ReconfigurableGroup(backend, a.communication_timeout, None, prefix=f"x{self.rank}e{epoch}",
+                                     event=self.event)
+            transport = PackedTransport(pg, torch.device("cpu"), timedelta(seconds=a.communication_timeout),
+                                        self.event)
         rid = self.logical_rid
         store_port = int(os.environ.get("SHIFT_STORE_PORT", "0"))
         store_port = (store_port + 100 * (epoch + 1) + 7 * (members == "AB")) if store_port else _free_port()
@@ -88,6 +102,11 @@ class PlannedWorker(Worker):
                     world_size_mode=WorldSizeMode.FIXED_WITH_SPARES, event=self.event)
         m._shift_epoch = epoch
         m.load_state_dict({"step": self.progress["updates"]})   # a new epoch continues the committed step count
+        if pg is None:
+            m.on_quorum = lambda q, up, changed: (
+                self.reducer.reconfigure(q, up, q.max_step) if changed or self.reducer.quorum_id != q.quorum_id
+                else None)
+            self.manager = m
         return m
 
     def load_state(self, payload):
@@ -191,6 +210,10 @@ class PlannedWorker(Worker):
             self.event("begin", step=step, participants=mgr.num_participants())
             batches, sample_ids = self.batches(step)
             relay = a.planned_variant == "p2" and self.handoff.is_relay_step()
+            fused = getattr(self, "reducer", None) is not None
+            if fused:
+                eng.nonfinite.zero_()
+                self.reducer.fused.begin_step(step, defer=relay)
             t_c = time.monotonic()
             if relay and self.role == "C":
                 eng.store.zero_grad()
@@ -209,8 +232,11 @@ class PlannedWorker(Worker):
                     return
                 self.manager = mgr
                 self.event("planned_ac_outer_begin", step=step)
-            mgr.allreduce(eng.store.grad).wait()
-            nonfinite = eng.optimizer_step([eng.store.grad], 1.0)
+            if fused:
+                nonfinite = self.reducer.fused.finish_step()
+            else:
+                mgr.allreduce(eng.store.grad).wait()
+                nonfinite = eng.optimizer_step([eng.store.grad], 1.0)
             if int(nonfinite.item()):
                 mgr.report_error(RuntimeError("nonfinite gradients"))
             commit = mgr.should_commit()

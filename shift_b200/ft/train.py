@@ -154,7 +154,12 @@ class Worker:
         assert payload["step"] == payload["progress"]["updates"]
         if self.manager:
             assert payload["step"] == self.manager.current_step()
-        self.engine.load_state_dict(payload)
+        if payload.get("_inplace"):
+            # flat buffers were already copied from the donor's HBM; apply the rest
+            self.engine.scheduler.load_state_dict(payload["scheduler"])
+            self.engine.store.step = int(payload["step"])
+        else:
+            self.engine.load_state_dict(payload)
         self.progress.update(payload["progress"])
         set_rng_state(payload, self.device)
         if self.device.type == "cuda":
@@ -198,10 +203,25 @@ class Worker:
         if a.standby == "gpu":
             self.standby_gate("gpu")
         backend = a.backend or ("nccl" if self.device.type == "cuda" else "gloo")
-        pg = ReconfigurableGroup(backend, a.communication_timeout, self.device if backend == "nccl" else None,
-                                 prefix=f"x{self.rank}", event=self.event)
-        transport = PackedTransport(pg, self.device if backend == "nccl" else torch.device("cpu"),
-                                    timedelta(seconds=a.communication_timeout), self.event)
+        self.reducer = None
+        if a.reduce == "fused":
+            if self.device.type != "cuda":
+                raise ValueError("--reduce fused needs a CUDA device")
+            from .fused import PeerStateTransport, QuorumFusedReducer
+            self.reducer = QuorumFusedReducer(self.engine, self.device, f"shift{a.replica}", a.generation, self.rank,
+                                              a.communication_timeout)
+            layers = self.cfg.layers
+            from ..parallel.replicas import _order
+            self.engine.model.layer_done_hook = lambda layer: self.reducer.fused.on_layer_done(_order(layer, layers))
+            pg = None
+            transport = PeerStateTransport(self.engine, self.device, self.reducer.owner, self.event,
+                                           lambda: self.manager)
+            backend = "peer-ipc"
+        else:
+            pg = ReconfigurableGroup(backend, a.communication_timeout, self.device if backend == "nccl" else None,
+                                     prefix=f"x{self.rank}", event=self.event)
+            transport = PackedTransport(pg, self.device if backend == "nccl" else torch.device("cpu"),
+                                        timedelta(seconds=a.communication_timeout), self.event)
         store_port = int(os.environ.get("SHIFT_STORE_PORT", "0")) or _free_port()
         mode = WorldSizeMode.FIXED_WITH_SPARES if a.world_size_mode == "fixed_with_spares" else WorldSizeMode.DYNAMIC
         self.manager = Manager(pg, self.load_state_for_manager, self.export_state_for_transport, a.min_replicas,
@@ -209,6 +229,9 @@ class Worker:
                                store_addr=f"{a.host_ip}:{store_port}", hostname=a.host_ip,
                                checkpoint_transport=transport, timeout=timedelta(seconds=a.communication_timeout),
                                world_size_mode=mode, event=self.event)
+        if self.reducer is not None:
+            self.manager.on_quorum = lambda q, up, changed: (
+                self.reducer.reconfigure(q, up, q.max_step) if changed or self.reducer.quorum_id is None else None)
         self.transport_on_cpu = backend == "gloo" and self.device.type == "cuda"
         started = self.phase("manager_init", started)
         if a.resume_checkpoint:
@@ -264,6 +287,9 @@ class Worker:
                 os._exit(17)
             batches, sample_ids = self.batches(step)
             t_compute = time.monotonic()
+            if self.reducer is not None:
+                eng.nonfinite.zero_()
+                self.reducer.fused.begin_step(step)
             loss = eng.forward_backward(batches, a.batch, a.seq_len)
             if inject_kind == "slow":
                 time.sleep(float(inject_arg) / 1000.0)
@@ -278,13 +304,19 @@ class Worker:
                     g.copy_(gc)
                 else:
                     mgr.allreduce(g).wait()
-                sources, scale = [g], 1.0
+                nonfinite = eng.optimizer_step([g], 1.0)
             else:
-                sources, scale = self.fused_sources()
-            nonfinite = eng.optimizer_step(sources, scale)
+                # reduction + AdamW already ran per bucket inside the fused kernel
+                nonfinite = self.reducer.fused.finish_step()
             finite = int(nonfinite.item()) == 0
             if not finite:
                 mgr.report_error(RuntimeError("nonfinite gradients"))
+            if self.reducer is not None:
+                from ..ops._ext import status_word
+                sw = status_word(self.device)
+                if int(sw[0].item()) != 0:
+                    mgr.report_error(RuntimeError(f"fused path status {int(sw[0].item())}"))
+                    sw.zero_()
             t_decide = time.monotonic()
             commit = mgr.should_commit()
             attempts += 1
@@ -308,9 +340,6 @@ class Worker:
         self.event("stopped", step=self.progress["updates"], attempts=attempts)
         mgr.shutdown()
         self.event.close()
-
-    def fused_sources(self):
-        raise RuntimeError("fused cross-replica reduction needs the peer-memory path (parallel.symmetric)")
 
     # ------------------------------------------------------------------ disk checkpoint baseline
     def save_checkpoint(self):

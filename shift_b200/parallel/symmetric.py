@@ -37,8 +37,17 @@ class SymmetricHeap:
         t = ext().sym_alloc(int(nbytes), self.device.index)
         self.local[name] = t
         h = ext().ipc_handle(t)
-        self.store.set(f"sym/{self.owner}/{name}", bytes(h.numpy().tobytes()) + int(nbytes).to_bytes(8, "little"))
+        self.handles = getattr(self, "handles", {})
+        self.handles[name] = bytes(h.numpy().tobytes()) + int(nbytes).to_bytes(8, "little")
+        if self.store is not None:
+            self.store.set(f"sym/{self.owner}/{name}", self.handles[name])
         return t
+
+    def publish(self, store):
+        """(Re)publish every local handle into ``store`` (e.g. a new quorum's store)."""
+        self.store = store
+        for name, blob in getattr(self, "handles", {}).items():
+            store.set(f"sym/{self.owner}/{name}", blob)
 
     def open(self, owner: str, name: str) -> torch.Tensor:
         key = (owner, name)
@@ -95,31 +104,40 @@ class CrossReplicaFused:
         self.active = False
 
     # ------------------------------------------------------------------ membership
-    def configure(self, owners_in_replica_order: list[str], participating: list[bool] | None = None):
+    def configure(self, owners_in_replica_order: list[str], participating: list[bool] | None = None,
+                  step: int = 0):
         """owners of the same shard in every replica of the quorum (replica order).
-        ``participating[i]`` False -> that replica contributes zeros (healing/spare)."""
+        ``participating[i]`` False -> that replica contributes zeros (healing/spare).
+        ``step``: the step this membership starts at (peers that joined later
+        than two steps ago are not waited on for buffer reuse)."""
         self.peer_owners = list(owners_in_replica_order)
         part = participating or [True] * len(owners_in_replica_order)
         self.sources = [o for o, p in zip(self.peer_owners, part) if p]
         if not 1 <= len(self.sources) <= 8:
             raise ValueError("1..8 participating replicas supported by the fused path")
         self.scale = 1.0 / len(self.sources)
+        since = getattr(self, "member_since", {})
+        self.member_since = {o: since.get(o, step) for o in self.peer_owners}
         self.grad_maps = {o: [self.heap.open(o, f"grad{i}").view(torch.bfloat16)[: self.numel] for i in range(2)]
                           for o in self.peer_owners}
         self.flag_maps = {o: self.heap.open(o, "flags").view(torch.int32) for o in self.peer_owners}
 
     # ------------------------------------------------------------------ per step
-    def begin_step(self, step: int):
+    def begin_step(self, step: int, defer: bool = False):
         """Select this step's gradient buffer; make sure every peer finished
-        reading it two steps ago; zero it."""
+        reading it two steps ago.  ``defer``: launch no bucket during backward
+        (membership may change before the reduction, e.g. a gradient relay);
+        ``finish_step`` then launches every bucket."""
         self.step = step
         par = step % 2
         self.engine.store.select_grad(par)
         if step >= 2:
-            ptrs = [self.flag_maps[o][self.nb + par].data_ptr() for o in self.peer_owners if o != self.heap.owner]
+            since = getattr(self, "member_since", {})
+            ptrs = [self.flag_maps[o][self.nb + par].data_ptr() for o in self.peer_owners
+                    if o != self.heap.owner and since.get(o, 0) <= step - 2]
             ext().flag_wait(ptrs, _tag(step - 2), self.status, self.timeout)
         self.launched = set()
-        self.active = True
+        self.active = not defer
         self.progress = -1
 
     def on_layer_done(self, order: int):

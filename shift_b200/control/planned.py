@@ -271,12 +271,15 @@ def main(argv=None):
     ap.add_argument("--device", default="cpu")
     ap.add_argument("--nproc", type=int, default=1)
     ap.add_argument("--gpus", default="", help="A,B,C device lists, e.g. '0;1;2'")
+    ap.add_argument("--train-args", default="", help="extra trainer flags, e.g. '--seq-len 2048 --batch 4'")
     a = ap.parse_args(argv)
     devices = {}
     if a.gpus:
         for role, lst in zip("ABC", a.gpus.split(";")):
             devices[role] = [int(x) for x in lst.split(",")]
-    s = PlannedSession(a.root, a.name, a.variant, a.scenario, a.model, a.device, a.nproc, devices=devices)
+    import shlex
+    s = PlannedSession(a.root, a.name, a.variant, a.scenario, a.model, a.device, a.nproc, devices=devices,
+                       train_args=shlex.split(a.train_args))
     res = s.run(a.post_steps, a.cancel)
     print(json.dumps({k: v for k, v in res.items() if k != "checks"}, indent=1, default=str))
     print(json.dumps({k: v["pass"] for k, v in res.get("checks", {}).items()}, indent=1))

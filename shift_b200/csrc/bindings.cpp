@@ -61,6 +61,7 @@ void fused_reduce_adamw(const std::vector<int64_t>& grad_ptrs, const std::vector
 void flag_set(int64_t flag_ptr, int64_t value);
 void flag_wait(const std::vector<int64_t>& flag_ptrs, int64_t target, const at::Tensor& status, double timeout_s);
 void peer_copy(int64_t src_ptr, int64_t dst_ptr, int64_t nbytes);
+std::string fingerprint(const at::Tensor& t);
 void pair_reduce_scatter(int64_t a_ptr, int64_t b_ptr, at::Tensor& out, const std::vector<int64_t>& flag_ptrs,
                          int64_t target, const at::Tensor& status, double timeout_s);
 }  // namespace coll
@@ -99,4 +100,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flag_wait", &sb::coll::flag_wait);
   m.def("peer_copy", &sb::coll::peer_copy, "K10: SM-driven peer-memory copy");
   m.def("pair_reduce_scatter", &sb::coll::pair_reduce_scatter);
+  m.def("fingerprint", &sb::coll::fingerprint, "deterministic 64-bit fingerprint of a tensor's bytes");
 }

@@ -174,6 +174,38 @@ __global__ void pair_reduce_scatter_kernel(const __nv_bfloat16* __restrict__ a, 
 }
 
 // ---------------------------------------------------------------------------
+// Deterministic 64-bit fingerprint of a byte range (FNV-1a over 32-bit words):
+// thread t of block b hashes words [chunk*(b*T+t), +chunk); the block folds its
+// threads' hashes in thread order, the host folds block hashes in block order.
+// Equal bytes give equal fingerprints; used for exact-state audits on GPU.
+// ---------------------------------------------------------------------------
+constexpr unsigned long long kFnvOffset = 1469598103934665603ull;
+constexpr unsigned long long kFnvPrime = 1099511628211ull;
+
+__device__ __forceinline__ unsigned long long fnv_word(unsigned long long h, uint32_t w) {
+  return (h ^ w) * kFnvPrime;
+}
+
+__global__ void fingerprint_kernel(const uint32_t* __restrict__ words, long n, long chunk,
+                                   unsigned long long* __restrict__ out) {
+  __shared__ unsigned long long th[256];
+  const long t = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  unsigned long long h = kFnvOffset;
+  const long b0 = t * chunk, b1 = min(n, b0 + chunk);
+  for (long i = b0; i < b1; ++i) h = fnv_word(h, words[i]);
+  th[threadIdx.x] = h;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned long long s = kFnvOffset;
+    for (int i = 0; i < static_cast<int>(blockDim.x); ++i) {
+      s = fnv_word(s, static_cast<uint32_t>(th[i]));
+      s = fnv_word(s, static_cast<uint32_t>(th[i] >> 32));
+    }
+    out[blockIdx.x] = s;
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
 static int sm_count() {
@@ -276,6 +308,36 @@ void peer_copy(int64_t src_ptr, int64_t dst_ptr, int64_t nbytes) {
   peer_copy_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(reinterpret_cast<const uint4*>(src_ptr),
                                                                           reinterpret_cast<uint4*>(dst_ptr), n16);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Fingerprint of a contiguous tensor's bytes (size must be a multiple of 4).
+std::string fingerprint(const at::Tensor& t) {
+  TORCH_CHECK(t.is_contiguous() && t.is_cuda(), "fingerprint: contiguous CUDA tensor");
+  const long nbytes = t.numel() * t.element_size();
+  TORCH_CHECK(nbytes % 4 == 0, "fingerprint: byte size must be a multiple of 4");
+  const at::cuda::CUDAGuard guard(t.device());
+  const long n = nbytes / 4;
+  const int threads = 256;
+  const long total_threads = 148L * 4 * threads;
+  const long chunk = std::max<long>(1, (n + total_threads - 1) / total_threads);
+  const long blocks = std::max<long>(1, (n + chunk * threads - 1) / (chunk * threads));
+  auto part = at::empty({blocks}, t.options().dtype(at::kLong));
+  if (n > 0)
+    fingerprint_kernel<<<blocks, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
+        reinterpret_cast<const uint32_t*>(t.data_ptr()), n, chunk,
+        reinterpret_cast<unsigned long long*>(part.data_ptr()));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  auto host = part.cpu();
+  unsigned long long s = kFnvOffset;
+  const auto* hp = reinterpret_cast<const unsigned long long*>(host.data_ptr());
+  for (long i = 0; i < blocks; ++i) {
+    s = (s ^ static_cast<uint32_t>(hp[i])) * kFnvPrime;
+    s = (s ^ static_cast<uint32_t>(hp[i] >> 32)) * kFnvPrime;
+  }
+  s = (s ^ static_cast<uint32_t>(nbytes)) * kFnvPrime;
+  char buf[32];
+  std::snprintf(buf, sizeof(buf), "%016llx", s);
+  return std::string(buf);
 }
 
 void pair_reduce_scatter(int64_t a_ptr, int64_t b_ptr, at::Tensor& out, const std::vector<int64_t>& flag_ptrs,

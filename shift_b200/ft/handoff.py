@@ -365,9 +365,12 @@ class PlannedHandoff:
         if self.role == self.source:
             payload = self.export()
             payload.update(planned_epoch=self.new_epoch, planned_role=1, manifest=self.manifest())
-            self.mover().send(payload, self.engine, k, "final")
+            # the exported snapshot must outlive the receiver's copy
+            self._sending = self.mover()
+            self._sending.send(payload, self.engine, k, "final")
             self.emit("planned_state_sent", step=k, source=self.source)
         self.coord.wait([f"loaded/{i}" for i in range(self.local_world)], 600)
+        self._sending = None
         if self.role == "B":
             self.retire(manager)
             return None, True
@@ -527,6 +530,7 @@ class OverlapHandoff(PlannedHandoff):
                     payload["planned_epoch"] = self.base_epoch
                 self.emit("planned_precopy_window_open", step=self.cut, seconds=time.monotonic() - t0)
                 mover = self.mover()
+                self._sending = mover   # released once C reports preloaded
                 # committed generation is read-only while step cut+1 runs (the
                 # optimizer writes the other generation), so the send can overlap
                 versions = self._versions()
@@ -696,6 +700,7 @@ class OverlapHandoff(PlannedHandoff):
                 raise RuntimeError("precopy sender timed out")
             self.check()
             self.coord.wait([f"preloaded/{self.rank}"], 600)
+            self._sending = None
             tail = self.tail()
             packet = dict(step=self.cut, sample_step=self.cut + 1, sample_ids=sample_ids, gradients=grad, tail=tail,
                           gradient_hash=_grad_hash(grad))

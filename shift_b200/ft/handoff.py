@@ -123,8 +123,52 @@ class StateMover:
         self.emit = event or (lambda *a, **k: None)
         self.rank = rank
 
+    LIVE = ("param", "master", "exp_avg", "exp_avg_sq")
+
+    def export_live(self, engine):
+        """Donor, during preparation: publish IPC handles of every state buffer
+        (both generations) so the spare can map them ahead of the cut."""
+        import pickle
+
+        from ..ops._ext import ext
+        st = engine.store
+        if not getattr(st, "ipc_state", False):
+            return False
+        handles = {}
+        for name in self.LIVE:
+            for g, t in enumerate(getattr(st, name)):
+                handles[f"{name}{g}"] = (ext().ipc_handle(t).numpy().tobytes(), t.numel() * t.element_size())
+        self.coord.raw.set(f"{self.coord.prefix}/live/{self.rank}", pickle.dumps(handles))
+        return True
+
+    def premap(self, timeout: float = 600.0):
+        """Spare, during preparation: map the donor's live state buffers."""
+        import pickle
+
+        from ..ops._ext import ext
+        key = f"{self.coord.prefix}/live/{self.rank}"
+        end = time.monotonic() + timeout
+        while not self.coord.raw.check([key]):
+            if time.monotonic() > end or self.coord.has("cancel"):
+                return False
+            time.sleep(0.005)
+        handles = pickle.loads(self.coord.raw.get(key))
+        self.mapped = {k: ext().ipc_open(torch.frombuffer(bytearray(h), dtype=torch.uint8), n, self.device.index)
+                       for k, (h, n) in handles.items()}
+        return True
+
     def send(self, payload: dict, engine, step: int, tag: str):
         t0 = time.perf_counter()
+        if self.mode == "ipc" and getattr(engine.store, "ipc_state", False):
+            # live mode: the spare reads this rank's frozen buffers directly
+            import pickle
+            st = engine.store
+            meta = {k: v for k, v in payload.items() if k not in ("model", "optimizer")}
+            blob = pickle.dumps({"live_gen": st.cur, "numel": st.numel, "meta": meta,
+                                 "opt_groups": payload["optimizer"]["param_groups"], "step": step})
+            self.coord.raw.set(f"{self.coord.prefix}/mover/{tag}/{self.rank}", blob)
+            self.emit("transport_send", step=step, seconds=time.perf_counter() - t0, gpu_bytes=0, mode="ipc_live")
+            return
         if self.mode == "ipc":
             from ..ops._ext import ext
             st = engine.store
@@ -168,15 +212,25 @@ class StateMover:
             if info["step"] != step:
                 raise ValueError(f"state mover step mismatch {info['step']} != {step}")
             st = engine.store
-            mapped = []
-            for name in ("param", "master", "exp_avg", "exp_avg_sq"):
-                dst = getattr(st, name)[st.cur]
-                h = torch.frombuffer(bytearray(bytes.fromhex(info["handles"][name])), dtype=torch.uint8)
-                src = ext().ipc_open(h, dst.numel() * dst.element_size(), dst.device.index)
-                ext().peer_copy(src.data_ptr(), dst.data_ptr(), dst.numel() * dst.element_size())
-                mapped.append(src)
-            torch.cuda.current_stream().synchronize()
-            del mapped
+            if "live_gen" in info:
+                if getattr(self, "mapped", None) is None and not self.premap(timeout):
+                    raise TimeoutError("state mover: donor buffers not published")
+                g = info["live_gen"]
+                for name in self.LIVE:
+                    dst = getattr(st, name)[st.cur]
+                    src = self.mapped[f"{name}{g}"]
+                    ext().peer_copy(src.data_ptr(), dst.data_ptr(), dst.numel() * dst.element_size())
+                torch.cuda.current_stream().synchronize()
+            else:
+                mapped = []
+                for name in ("param", "master", "exp_avg", "exp_avg_sq"):
+                    dst = getattr(st, name)[st.cur]
+                    h = torch.frombuffer(bytearray(bytes.fromhex(info["handles"][name])), dtype=torch.uint8)
+                    src = ext().ipc_open(h, dst.numel() * dst.element_size(), dst.device.index)
+                    ext().peer_copy(src.data_ptr(), dst.data_ptr(), dst.numel() * dst.element_size())
+                    mapped.append(src)
+                torch.cuda.current_stream().synchronize()
+                del mapped
             nbytes = sum(getattr(st, n)[st.cur].numel() * getattr(st, n)[st.cur].element_size()
                          for n in ("param", "master", "exp_avg", "exp_avg_sq"))
             self.emit("transport_recv", step=step, seconds=time.perf_counter() - t0, gpu_bytes=nbytes, mode="ipc")
@@ -195,7 +249,7 @@ class PlannedHandoff:
 
     def __init__(self, role: str, variant: str, rank: int, local_world: int, coord: Coordinator, event, export,
                  load, progress: dict, manifest, device, mover_mode: str, round_: int = 0, source: str = "B",
-                 inject: str = "healthy"):
+                 inject: str = "healthy", engine=None, prepare_hooks=()):
         self.role, self.variant, self.rank, self.local_world = role, variant, rank, local_world
         self.coord = coord
         self.emit = event
@@ -222,7 +276,9 @@ class PlannedHandoff:
         self.retired = []
         self.cleanup_thread = None
         self.cleanup_cancel = threading.Event()
-        self.engine = None
+        self.engine = engine
+        self.prepare_hooks = list(prepare_hooks)
+        self._mover = None
         if variant != "steady":
             self.spawn(self.prepare_all)
 
@@ -274,7 +330,16 @@ class PlannedHandoff:
             if not waiter.wait([f"local/C/{self.rank}"], 600, cancel_key="cancel"):
                 return
             self.channels["state"] = self._channel("state")
+            if self.mover_mode == "ipc":
+                # map the donor's live state into the spare ahead of the cut
+                mv = self.mover()
+                if self.role == self.source:
+                    mv.export_live(self.engine)
+                else:
+                    mv.premap()
         self.emit("planned_channel_ready", channel="state")
+        for hook in self.prepare_hooks:
+            hook(self)
 
     def _channel(self, name: str):
         """A 2-member group (donor 0, spare 1) used by the packed transport
@@ -299,9 +364,13 @@ class PlannedHandoff:
         self.channels = {}
 
     def mover(self):
-        return StateMover(self.mover_mode, self.coord, self.channels.get("state"),
-                          self.device if self.mover_mode == "packed" and self.device.type == "cuda" else
-                          torch.device("cpu") if self.mover_mode == "packed" else self.device, self.emit, self.rank)
+        if self._mover is None or self._mover.channel is not self.channels.get("state"):
+            dev = torch.device("cpu") if self.mover_mode == "packed" else self.device
+            mapped = getattr(self._mover, "mapped", None)
+            self._mover = StateMover(self.mover_mode, self.coord, self.channels.get("state"), dev, self.emit,
+                                     self.rank)
+            self._mover.mapped = mapped
+        return self._mover
 
     # ------------------------------------------------------------------ C side
     def ready_receiver(self) -> bool:

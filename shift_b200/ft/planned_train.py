@@ -70,19 +70,60 @@ class PlannedWorker(Worker):
         return tail
 
     # ------------------------------------------------------------------ managers per epoch
-    def make_manager(self, epoch: int, members: str = "AB"):
+    def ensure_reducer(self):
+        if getattr(self, "reducer", None) is None:
+            from .fused import QuorumFusedReducer
+            a = self.args
+            self.reducer = QuorumFusedReducer(self.engine, self.device, self.role, a.generation, self.rank,
+                                              a.communication_timeout)
+            layers = self.cfg.layers
+            from ..parallel.replicas import _order
+            self.engine.model.layer_done_hook = lambda layer: self.reducer.fused.on_layer_done(_order(layer, layers))
+        return self.reducer
+
+    # ------------------------------------------------------------------ preparation hooks (background)
+    def premap_k1(self, handoff):
+        """Exchange the fused-path buffers of the future AC pair now, so the
+        first AC step only finds cached mappings."""
+        if self.device.type != "cuda" or self.role not in ("A", "C"):
+            return
+        red = self.ensure_reducer()
+        raw, pre = handoff.coord.raw, handoff.coord.prefix
+        red.heap.publish(raw)
+        raw.set(f"{pre}/k1owner/{self.role}/{self.rank}", red.owner)
+        other = "C" if self.role == "A" else "A"
+        key = f"{pre}/k1owner/{other}/{self.rank}"
+        end = time.monotonic() + 600
+        while not raw.check([key]):
+            if time.monotonic() > end or handoff.coord.has("cancel"):
+                return
+            time.sleep(0.005)
+        owner = raw.get(key).decode()
+        for name in ("grad0", "grad1", "flags"):
+            red.heap.open(owner, name)
+        self.event("planned_k1_premapped", peer=owner)
+
+    def precreate_manager(self, handoff):
+        if self.role in ("A", "C") and self.args.planned_variant in ("p1f", "p2"):
+            self.next_manager = self.make_manager(handoff.new_epoch, "AC", activate=False)
+            self.event("planned_candidate_manager_ready", epoch=handoff.new_epoch)
+
+    def take_manager(self, epoch: int, members: str):
+        m = getattr(self, "next_manager", None)
+        if m is not None and members == "AC" and m._shift_epoch == epoch:
+            self.next_manager = None
+            m.load_state_dict({"step": self.progress["updates"]})
+            self.manager = m
+            return m
+        return self.make_manager(epoch, members)
+
+    def make_manager(self, epoch: int, members: str = "AB", activate: bool = True):
         a = self.args
         port = a.lighthouse_port + 10 * epoch + (1 if members == "AB" and epoch > a.planned_round else 0)
         if self.device.type == "cuda":
             # fused peer-memory reduction + IPC healing: a new epoch only re-maps handles
-            from .fused import PeerStateTransport, QuorumFusedReducer
-            if getattr(self, "reducer", None) is None:
-                self.reducer = QuorumFusedReducer(self.engine, self.device, self.role, a.generation, self.rank,
-                                                  a.communication_timeout)
-                layers = self.cfg.layers
-                from ..parallel.replicas import _order
-                self.engine.model.layer_done_hook = (
-                    lambda layer: self.reducer.fused.on_layer_done(_order(layer, layers)))
+            from .fused import PeerStateTransport
+            self.ensure_reducer()
             pg = None
             transport = PeerStateTransport(self.engine, self.device, self.reducer.owner, self.event,
                                            lambda: self.manager)
@@ -106,7 +147,8 @@ class PlannedWorker(Worker):
             m.on_quorum = lambda q, up, changed: (
                 self.reducer.reconfigure(q, up, q.max_step) if changed or self.reducer.quorum_id != q.quorum_id
                 else None)
-            self.manager = m
+            if activate:
+                self.manager = m
         return m
 
     def load_state(self, payload):
@@ -144,18 +186,22 @@ class PlannedWorker(Worker):
         a = self.args
         torch.set_num_threads(1)
         self.cfg = MoEConfig.tiny() if a.model == "tiny" else MoEConfig.bench()
-        self.engine = Engine(self.cfg, self.device, seed=a.seed, bucket_numel=a.bucket_size)
+        cuda = self.device.type == "cuda"
+        self.engine = Engine(self.cfg, self.device, seed=a.seed, bucket_numel=a.bucket_size, ipc_state=cuda)
         self.engine.optim.lr = a.lr
         self.engine.scheduler.base_lrs = [a.lr]
         self.engine.scheduler._last_lr = [a.lr]
+        if cuda:
+            self.ensure_reducer()
         prefix = f"round/{a.planned_round}" if a.planned_round else ""
         self.coord = Coordinator(a.coord, prefix)
-        mover = a.mover if a.mover != "auto" else ("ipc" if self.device.type == "cuda" else "packed")
+        mover = a.mover if a.mover != "auto" else ("ipc" if cuda else "packed")
         cls = OverlapHandoff if a.planned_variant == "p2" else PlannedHandoff
+        hooks = [self.premap_k1, self.precreate_manager] if cuda else [self.precreate_manager]
         self.handoff = cls(self.role, a.planned_variant, self.rank, self.local_world, self.coord, self.event,
                            self.export_state, self.load_state, self.progress, self.manifest, self.device, mover,
-                           round_=a.planned_round, source=a.planned_source, inject=a.planned_inject)
-        self.handoff.engine = self.engine
+                           round_=a.planned_round, source=a.planned_source, inject=a.planned_inject,
+                           engine=self.engine, prepare_hooks=hooks)
         self.handoff.rng_tail = self.rng_tail
         self.transport_on_cpu = False
         base_epoch = a.planned_round
@@ -166,7 +212,7 @@ class PlannedWorker(Worker):
                 self.event("stopped", step=self.progress["updates"], role="C", cancelled=True)
                 self.event.close()
                 return
-            self.manager = self.make_manager(base_epoch + 1, "AC")
+            self.manager = self.take_manager(base_epoch + 1, "AC")
             self.manager.load_state_dict({"step": self.progress["updates"]})
             self.event("planned_epoch_activated", step=self.progress["updates"], epoch=base_epoch + 1)
         else:
@@ -199,7 +245,7 @@ class PlannedWorker(Worker):
                     self.event.close()
                     return
                 if mgr is None:
-                    mgr = self.make_manager(self.handoff.gate.epoch, "AC")
+                    mgr = self.take_manager(self.handoff.gate.epoch, "AC")
                     mgr.load_state_dict({"step": self.progress["updates"]})
                     self.event("planned_epoch_activated", step=self.progress["updates"],
                                epoch=self.handoff.gate.epoch)
@@ -224,7 +270,7 @@ class PlannedWorker(Worker):
                 if a.planned_inject == "slow-compute":
                     time.sleep(a.planned_slow_ms / 1000.0)
             if relay:
-                mgr, retired = self.handoff.at_gradient(mgr, eng.store.grad, self.make_manager, sample_ids,
+                mgr, retired = self.handoff.at_gradient(mgr, eng.store.grad, self.take_manager, sample_ids,
                                                         self.apply_tail)
                 if retired:
                     self.event("stopped", step=self.progress["updates"], role=self.role, retired=True)

@@ -48,7 +48,7 @@ class Bucket:
 
 class FlatParams:
     def __init__(self, specs: list[ParamSpec], device, compute_dtype=torch.bfloat16,
-                 bucket_numel: int = 64 * 1024 * 1024, pingpong: bool = True):
+                 bucket_numel: int = 64 * 1024 * 1024, pingpong: bool = True, ipc_state: bool = False):
         self.specs = list(specs)
         self.device = torch.device(device)
         self.compute_dtype = compute_dtype
@@ -62,11 +62,20 @@ class FlatParams:
             off += (n + ALIGN - 1) // ALIGN * ALIGN
         self.numel = off
         gens = 2 if pingpong else 1
-        f32 = dict(dtype=torch.float32, device=self.device)
-        self.master = [torch.zeros(self.numel, **f32) for _ in range(gens)]
-        self.exp_avg = [torch.zeros(self.numel, **f32) for _ in range(gens)]
-        self.exp_avg_sq = [torch.zeros(self.numel, **f32) for _ in range(gens)]
-        self.param = [torch.zeros(self.numel, dtype=compute_dtype, device=self.device) for _ in range(gens)]
+        self.ipc_state = ipc_state and self.device.type == "cuda"
+
+        def buf(dtype):
+            if self.ipc_state:
+                # plain cudaMalloc allocations so that peers can map the live state (CUDA IPC)
+                from ..ops._ext import ext
+                elem = torch.tensor([], dtype=dtype).element_size()
+                return ext().sym_alloc(self.numel * elem, self.device.index).view(dtype)[: self.numel]
+            return torch.zeros(self.numel, dtype=dtype, device=self.device)
+
+        self.master = [buf(torch.float32) for _ in range(gens)]
+        self.exp_avg = [buf(torch.float32) for _ in range(gens)]
+        self.exp_avg_sq = [buf(torch.float32) for _ in range(gens)]
+        self.param = [buf(compute_dtype) for _ in range(gens)]
         self.grad = torch.zeros(self.numel, dtype=compute_dtype, device=self.device)
         self.cur = 0
         self.pingpong = pingpong

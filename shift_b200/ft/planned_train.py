@@ -89,7 +89,7 @@ class PlannedWorker(Worker):
             return
         red = self.ensure_reducer()
         raw, pre = handoff.coord.raw, handoff.coord.prefix
-        red.heap.publish(raw)
+        red.heap.publish(raw, make_default=False)
         raw.set(f"{pre}/k1owner/{self.role}/{self.rank}", red.owner)
         other = "C" if self.role == "A" else "A"
         key = f"{pre}/k1owner/{other}/{self.rank}"
@@ -100,7 +100,7 @@ class PlannedWorker(Worker):
             time.sleep(0.005)
         owner = raw.get(key).decode()
         for name in ("grad0", "grad1", "flags"):
-            red.heap.open(owner, name)
+            red.heap.open(owner, name, store=raw)
         self.event("planned_k1_premapped", peer=owner)
 
     def precreate_manager(self, handoff):

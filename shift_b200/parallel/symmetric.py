@@ -43,19 +43,20 @@ class SymmetricHeap:
             self.store.set(f"sym/{self.owner}/{name}", self.handles[name])
         return t
 
-    def publish(self, store):
+    def publish(self, store, make_default: bool = True):
         """(Re)publish every local handle into ``store`` (e.g. a new quorum's store)."""
-        self.store = store
+        if make_default:
+            self.store = store
         for name, blob in getattr(self, "handles", {}).items():
             store.set(f"sym/{self.owner}/{name}", blob)
 
-    def open(self, owner: str, name: str) -> torch.Tensor:
+    def open(self, owner: str, name: str, store=None) -> torch.Tensor:
         key = (owner, name)
         if owner == self.owner:
             return self.local[name]
         t = self.peers.get(key)
         if t is None:
-            raw = self.store.get(f"sym/{owner}/{name}")
+            raw = (store or self.store).get(f"sym/{owner}/{name}")
             h = torch.frombuffer(bytearray(raw[:64]), dtype=torch.uint8)
             nbytes = int.from_bytes(raw[64:72], "little")
             t = ext().ipc_open(h, nbytes, self.device.index)

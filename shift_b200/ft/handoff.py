@@ -337,6 +337,8 @@ class PlannedHandoff:
                     mv.export_live(self.engine)
                 else:
                     mv.premap()
+                if hasattr(self, "prepare_relay"):
+                    self.prepare_relay()
         self.emit("planned_channel_ready", channel="state")
         for hook in self.prepare_hooks:
             hook(self)
@@ -676,15 +678,40 @@ class OverlapHandoff(PlannedHandoff):
     def is_relay_step(self) -> bool:
         return self.cut is not None and self.progress["updates"] == self.cut and not self.relay_done
 
+    def prepare_relay(self):
+        """P2 preparation on a GPU box: B allocates and exports the relay
+        buffer, C maps it -- at the relay step only a local copy (B) and one
+        NVLink copy (C) remain."""
+        import pickle
+
+        from ..ops._ext import ext
+        n = self.engine.store.numel
+        key = f"{self.coord.prefix}/relaybuf/{self.rank}"
+        if self.role == "B":
+            self._relay_buf = ext().sym_alloc(n * 2, self.device.index)
+            self.coord.raw.set(key, pickle.dumps((ext().ipc_handle(self._relay_buf).numpy().tobytes(), n)))
+        elif self.role == "C":
+            end = time.monotonic() + 600
+            while not self.coord.raw.check([key]):
+                if time.monotonic() > end or self.coord.has("cancel"):
+                    return
+                time.sleep(0.005)
+            h, n2 = pickle.loads(self.coord.raw.get(key))
+            self._relay_src = ext().ipc_open(torch.frombuffer(bytearray(h), dtype=torch.uint8), n2 * 2,
+                                             self.device.index)
+
     def _send_relay(self, packet):
         import pickle
         if self.mover_mode == "ipc":
             from ..ops._ext import ext
             g = packet["gradients"]
-            sym = ext().sym_alloc(g.numel() * g.element_size(), g.device.index)
-            ext().peer_copy(g.data_ptr(), sym.data_ptr(), g.numel() * g.element_size())
+            nbytes = g.numel() * g.element_size()
+            sym = getattr(self, "_relay_buf", None)
+            if sym is None or sym.numel() != nbytes:
+                sym = ext().sym_alloc(nbytes, g.device.index)
+                self._relay_buf = sym
+            ext().peer_copy(g.data_ptr(), sym.data_ptr(), nbytes)
             torch.cuda.current_stream().synchronize()
-            self._relay_buf = sym
             meta = dict(packet, gradients=None, handle=ext().ipc_handle(sym).numpy().tobytes().hex(),
                         numel=g.numel(), dtype=str(g.dtype))
             self.coord.raw.set(f"{self.coord.prefix}/relay/{self.rank}", pickle.dumps(meta))
@@ -707,8 +734,10 @@ class OverlapHandoff(PlannedHandoff):
             meta = pickle.loads(self.coord.raw.get(key))
             dev = self.device
             n = meta["numel"]
-            h = torch.frombuffer(bytearray(bytes.fromhex(meta["handle"])), dtype=torch.uint8)
-            src = ext().ipc_open(h, n * 2, dev.index)
+            src = getattr(self, "_relay_src", None)
+            if src is None or src.numel() != n * 2:
+                h = torch.frombuffer(bytearray(bytes.fromhex(meta["handle"])), dtype=torch.uint8)
+                src = ext().ipc_open(h, n * 2, dev.index)
             g = torch.empty(n, dtype=torch.bfloat16, device=dev)
             ext().peer_copy(src.data_ptr(), g.data_ptr(), n * 2)
             torch.cuda.current_stream().synchronize()
@@ -861,4 +890,10 @@ class OverlapHandoff(PlannedHandoff):
 
 
 def _grad_hash(g: torch.Tensor) -> str:
+    """Exact-equality hash of a gradient: the reference digest for host
+    tensors, the deterministic GPU fingerprint for device tensors (hashing a
+    1 GB gradient through host SHA-256 would dominate the relay)."""
+    if g.is_cuda:
+        from ..ops._ext import ext
+        return "fp:" + ext().fingerprint(g.detach().contiguous())
     return digest(g.detach())

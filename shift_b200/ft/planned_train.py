@@ -103,6 +103,20 @@ class PlannedWorker(Worker):
             red.heap.open(owner, name, store=raw)
         self.event("planned_k1_premapped", peer=owner)
 
+    def warmup_spare(self, handoff):
+        """C: one forward/backward on a throw-away batch while A and B train,
+        so the first real step pays no lazy initialisation (GPU standby).
+        Touches only activations and the gradient buffer, never the state."""
+        if self.role != "C":
+            return
+        from ..engine import synthetic_batch
+        a = self.args
+        data = synthetic_batch(self.cfg, 0, a.batch, a.seq_len, "pattern").to(self.device)
+        self.engine.forward_backward([(data[:, :-1].contiguous(), data[:, 1:].contiguous())], a.batch, a.seq_len)
+        self.engine.store.zero_grad()
+        torch.cuda.synchronize(self.device)
+        self.event("planned_spare_warm", seconds=0.0)
+
     def precreate_manager(self, handoff):
         if self.role in ("A", "C") and self.args.planned_variant in ("p1f", "p2"):
             self.next_manager = self.make_manager(handoff.new_epoch, "AC", activate=False)
@@ -197,7 +211,7 @@ class PlannedWorker(Worker):
         self.coord = Coordinator(a.coord, prefix)
         mover = a.mover if a.mover != "auto" else ("ipc" if cuda else "packed")
         cls = OverlapHandoff if a.planned_variant == "p2" else PlannedHandoff
-        hooks = [self.premap_k1, self.precreate_manager] if cuda else [self.precreate_manager]
+        hooks = [self.premap_k1, self.warmup_spare, self.precreate_manager] if cuda else [self.precreate_manager]
         self.handoff = cls(self.role, a.planned_variant, self.rank, self.local_world, self.coord, self.event,
                            self.export_state, self.load_state, self.progress, self.manifest, self.device, mover,
                            round_=a.planned_round, source=a.planned_source, inject=a.planned_inject,

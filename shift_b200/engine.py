@@ -79,17 +79,17 @@ def synthetic_batch(cfg: MoEConfig, sample: int, B: int, S: int, mode: str = "ra
 class Engine:
     def __init__(self, cfg: MoEConfig, device, part: Partition | None = None, optim: OptimConfig | None = None,
                  seed: int = 2026, bucket_numel: int = 64 * 1024 * 1024, compute_dtype=None,
-                 ipc_state: bool = False):
+                 ipc_state: bool = False, tp=None, specs=None, seed_of=None):
         self.cfg = cfg
         self.device = torch.device(device)
         self.part = part or Partition()
         self.optim = optim or OptimConfig()
         if compute_dtype is None:
             compute_dtype = torch.bfloat16 if self.device.type == "cuda" else torch.float32
-        self.store = FlatParams(param_specs(cfg, self.part), self.device, compute_dtype, bucket_numel,
-                                ipc_state=ipc_state)
-        self.store.init_(cfg.init_std, torch.Generator().manual_seed(seed))
-        self.model = QwenMoE(cfg, self.store, self.part)
+        self.store = FlatParams(specs if specs is not None else param_specs(cfg, self.part), self.device,
+                                compute_dtype, bucket_numel, ipc_state=ipc_state)
+        self.store.init_(cfg.init_std, torch.Generator().manual_seed(seed), seed_of=seed_of)
+        self.model = QwenMoE(cfg, self.store, self.part, tp=tp)
         self.scheduler = StepLR(self.optim.lr, self.optim.step_size, self.optim.gamma)
         self.nonfinite = torch.zeros(1, dtype=torch.int32, device=self.device)
 

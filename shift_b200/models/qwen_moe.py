@@ -79,6 +79,12 @@ class Partition:
     has_head: bool = True
     expert_lo: int = 0
     expert_hi: int = -1          # exclusive; -1 = all
+    tp_size: int = 1             # attention heads split over this many ranks
+
+
+# parameters split over the TP pair (the rest are replicated and their
+# gradients summed over the pair)
+TP_SHARDED = ("attn.qkv", "attn.o", "mlp.w1", "mlp.w2")
 
 
 def param_specs(cfg: MoEConfig, part: Partition) -> list[ParamSpec]:
@@ -86,6 +92,8 @@ def param_specs(cfg: MoEConfig, part: Partition) -> list[ParamSpec]:
     hi = cfg.layers if part.layer_hi < 0 else part.layer_hi
     e_hi = cfg.experts if part.expert_hi < 0 else part.expert_hi
     e_n = e_hi - part.expert_lo
+    tp = part.tp_size
+    hq, hkv = cfg.heads // tp, cfg.kv_heads // tp
     specs = []
     if part.has_embed:
         specs.append(ParamSpec("embed.weight", (cfg.vocab, H)))
@@ -93,8 +101,8 @@ def param_specs(cfg: MoEConfig, part: Partition) -> list[ParamSpec]:
         p = f"layers.{i}."
         specs += [
             ParamSpec(p + "ln1.weight", (H,), init="ones", layer=i),
-            ParamSpec(p + "attn.qkv", ((cfg.heads + 2 * cfg.kv_heads) * D, H), layer=i),
-            ParamSpec(p + "attn.o", (H, cfg.heads * D), layer=i),
+            ParamSpec(p + "attn.qkv", ((hq + 2 * hkv) * D, H), layer=i),
+            ParamSpec(p + "attn.o", (H, hq * D), layer=i),
             ParamSpec(p + "ln2.weight", (H,), init="ones", layer=i),
             ParamSpec(p + "mlp.router", (cfg.experts, H), layer=i),
             ParamSpec(p + "mlp.w1", (e_n, 2 * cfg.expert_ffn, H), kind="expert", layer=i),
@@ -115,10 +123,13 @@ class StepStats:
 class QwenMoE:
     """One pipeline stage (or the whole model) of the MoE, bound to a FlatParams."""
 
-    def __init__(self, cfg: MoEConfig, store: FlatParams, part: Partition | None = None):
+    def __init__(self, cfg: MoEConfig, store: FlatParams, part: Partition | None = None, tp=None):
         self.cfg = cfg
         self.store = store
         self.part = part or Partition()
+        self.tp = tp if (tp is not None and tp.size > 1) else None
+        self.hq = cfg.heads // self.part.tp_size
+        self.hkv = cfg.kv_heads // self.part.tp_size
         self.layer_hi = cfg.layers if self.part.layer_hi < 0 else self.part.layer_hi
         self.e_lo = self.part.expert_lo
         self.e_hi = cfg.experts if self.part.expert_hi < 0 else self.part.expert_hi
@@ -144,6 +155,8 @@ class QwenMoE:
         saved = {"B": B, "S": S, "layers": [], "loss_scale": loss_scale}
         if self.part.has_embed:
             tok = tokens.reshape(-1).to(torch.int32)
+            if self.tp is not None:
+                tok = self.tp.local_rows(tok).contiguous()   # sequence-parallel token split
             saved["tokens"] = tok
             resid = Fn.embedding_fwd(st.w("embed.weight"), tok)
             delta = None
@@ -157,6 +170,8 @@ class QwenMoE:
             y, rstd, h = Fn.rmsnorm_fwd(resid, st.w("norm.weight"), cfg.eps, delta)
             logits = G.linear_fwd(y, st.w("lm_head.weight"))
             lab = labels.reshape(-1).to(torch.int32)
+            if self.tp is not None:
+                lab = self.tp.local_rows(lab).contiguous()
             per_tok = Fn.xent_fwd_bwd(logits, lab, loss_scale)   # logits now hold dlogits
             loss_sum = per_tok.sum()
             saved.update(final_h=h, final_rstd=rstd, final_y=y, dlogits=logits)
@@ -166,18 +181,28 @@ class QwenMoE:
         self._saved.append(saved)
         return out, loss_sum
 
+    def _ag(self, x):
+        return self.tp.all_gather(x) if self.tp is not None else x
+
+    def _rs(self, x):
+        return self.tp.reduce_scatter(x) if self.tp is not None else x
+
     def _layer_fwd(self, i, resid, delta, B, S):
+        """resid / delta / outputs are this rank's token rows (all rows without TP)."""
         cfg, st = self.cfg, self.store
         p = f"layers.{i}."
-        Hq, Hkv, D = cfg.heads, cfg.kv_heads, cfg.head_dim
+        Hq, Hkv, D = self.hq, self.hkv, cfg.head_dim
         T = B * S
-        a_in, rstd1, h = Fn.rmsnorm_fwd(resid, st.w(p + "ln1.weight"), cfg.eps, delta)
-        qkv = G.linear_fwd(a_in, st.w(p + "attn.qkv"))
+        a_loc, rstd1, h = Fn.rmsnorm_fwd(resid, st.w(p + "ln1.weight"), cfg.eps, delta)
+        a_in = self._ag(a_loc)                                  # [T, H]
+        qkv = G.linear_fwd(a_in, st.w(p + "attn.qkv"))          # column parallel: local heads
         Fn.rope_(qkv, self.cos, self.sin, S, Hq + Hkv, D)
         o, lse = Fn.attention_fwd(qkv, B, S, Hq, Hkv, D, self.scale)
-        attn_out = G.linear_fwd(o, st.w(p + "attn.o"))
-        m_in, rstd2, h2 = Fn.rmsnorm_fwd(h, st.w(p + "ln2.weight"), cfg.eps, attn_out)
-        moe_out, mctx = self._moe_fwd(p, m_in, T)
+        attn_out = self._rs(G.linear_fwd(o, st.w(p + "attn.o")))  # row parallel partial -> token rows
+        m_loc, rstd2, h2 = Fn.rmsnorm_fwd(h, st.w(p + "ln2.weight"), cfg.eps, attn_out)
+        m_in = self._ag(m_loc)
+        moe_partial, mctx = self._moe_fwd(p, m_in, T)
+        moe_out = self._rs(moe_partial)
         ctx = dict(h=h, rstd1=rstd1, a_in=a_in, qkv=qkv, o=o, lse=lse, h2=h2, rstd2=rstd2, m_in=m_in, **mctx)
         return h2, moe_out, ctx
 
@@ -245,19 +270,20 @@ class QwenMoE:
         """dout: gradient w.r.t. the layer output h_out = h2 + moe_out."""
         cfg, st = self.cfg, self.store
         p = f"layers.{i}."
-        Hq, Hkv, D = cfg.heads, cfg.kv_heads, cfg.head_dim
+        Hq, Hkv, D = self.hq, self.hkv, cfg.head_dim
         T = B * S
-        # ---- MoE ----
-        dm_in = self._moe_bwd(p, c, dout, T, accumulate)
+        # ---- MoE (the gradient of a reduce-scatter is an all-gather and vice versa) ----
+        dm_in = self._rs(self._moe_bwd(p, c, self._ag(dout), T, accumulate))
         dh2 = Fn.rmsnorm_bwd(dm_in, c["h2"], c["rstd2"], st.w(p + "ln2.weight"), cfg.eps, st.g(p + "ln2.weight"),
                              dout, accumulate)
         # ---- attention ----
-        G.linear_wgrad(dh2, c["o"], st.g(p + "attn.o"), accumulate)
-        d_o = G.linear_dgrad(dh2, st.w(p + "attn.o"))
+        dattn = self._ag(dh2)
+        G.linear_wgrad(dattn, c["o"], st.g(p + "attn.o"), accumulate)
+        d_o = G.linear_dgrad(dattn, st.w(p + "attn.o"))
         dqkv = Fn.attention_bwd(c["qkv"], c["o"], c["lse"], d_o, B, S, Hq, Hkv, D, self.scale)
         Fn.rope_(dqkv, self.cos, self.sin, S, Hq + Hkv, D, inverse=True)
         G.linear_wgrad(dqkv, c["a_in"], st.g(p + "attn.qkv"), accumulate)
-        da = G.linear_dgrad(dqkv, st.w(p + "attn.qkv"))
+        da = self._rs(G.linear_dgrad(dqkv, st.w(p + "attn.qkv")))
         dh = Fn.rmsnorm_bwd(da, c["h"], c["rstd1"], st.w(p + "ln1.weight"), cfg.eps, st.g(p + "ln1.weight"), dh2,
                             accumulate)
         return dh
@@ -275,14 +301,16 @@ class QwenMoE:
         dx = torch.empty_like(c["m_in"])
         Fn.scatter_back(dxp, c["pos"], dx, False)
         aux_grad = None
-        if cfg.aux_coef > 0:
+        # the auxiliary loss is added once per replica: on TP rank 0 only (both TP
+        # ranks route the same tokens, and the reduce-scatter sums their partials)
+        if cfg.aux_coef > 0 and (self.tp is None or self.tp.rank == 0):
             # switch loss coef * E * sum_e f_e * mean_t p_te ; d/dp_te = coef * E * f_e / T
-            f = c["counts"].float() / float(T * cfg.top_k)
+            if self.e_hi - self.e_lo == cfg.experts:
+                counts = c["counts"].float()
+            else:
+                counts = torch.bincount(c["idx"].reshape(-1).long(), minlength=cfg.experts).float()
+            f = counts / float(T * cfg.top_k)
             aux_grad = (f * (cfg.aux_coef * cfg.experts / float(T))).contiguous()
-            if self.e_hi - self.e_lo != cfg.experts:
-                full = torch.zeros(cfg.experts, dtype=torch.float32, device=dx.device)
-                full[self.e_lo:self.e_hi] = aux_grad
-                aux_grad = full
         Fn.router_bwd(c["m_in"], st.w(p + "mlp.router"), c["probs"], c["idx"], c["w"], dw_topk.contiguous(),
                       aux_grad, cfg.norm_topk, dx, st.g(p + "mlp.router"), accumulate)
         return dx

@@ -117,8 +117,12 @@ class FlatParams:
         self.step += 1
 
     # ------------------------------------------------------------------ init
-    def init_(self, std: float, generator: torch.Generator | None = None):
-        """N(0, std) for matrices, ones for norm weights; master = param (fp32)."""
+    def init_(self, std: float, generator: torch.Generator | None = None, seed_of=None):
+        """N(0, std) for matrices, ones for norm weights; master = param (fp32).
+
+        ``seed_of(spec) -> int`` seeds each parameter independently (so that a
+        parameter replicated on several ranks gets identical values whatever
+        else those ranks hold); otherwise one generator runs over all specs."""
         m = self.master[self.cur]
         for s in self.specs:
             v = self.view_of(m, s.name)
@@ -128,7 +132,8 @@ class FlatParams:
                 v.zero_()
             else:
                 cpu = torch.empty(v.shape, dtype=torch.float32)
-                cpu.normal_(0.0, std, generator=generator)
+                g = torch.Generator().manual_seed(seed_of(s)) if seed_of is not None else generator
+                cpu.normal_(0.0, std, generator=g)
                 v.copy_(cpu)
         self.param[self.cur].copy_(m)
         # params are rounded to the compute dtype; keep master consistent with them

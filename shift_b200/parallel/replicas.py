@@ -103,7 +103,9 @@ class ReplicaDPRunner:
 
 
 def make_parallel_runner(n_gpus: int, rank: int, local_rank: int, batch: int, seq: int, cfg: MoEConfig):
-    layout = os.environ.get("SHIFT_LAYOUT", "dp")
+    """Default layouts: 2 GPUs -> 2 replicas x 1; 4 -> 2 replicas x TP2;
+    8 -> 2 replicas x (TP2 x PP2).  SHIFT_LAYOUT=dp|tp|tppp overrides."""
+    layout = os.environ.get("SHIFT_LAYOUT") or {2: "dp", 4: "tp", 8: "tppp"}.get(n_gpus, "dp")
     if layout == "dp":
         return ReplicaDPRunner(cfg, n_gpus, rank, local_rank, batch, seq,
                                with_manager=os.environ.get("SHIFT_BENCH_FT", "1") == "1")

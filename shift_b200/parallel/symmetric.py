@@ -122,6 +122,22 @@ class CrossReplicaFused:
         self.grad_maps = {o: [self.heap.open(o, f"grad{i}").view(torch.bfloat16)[: self.numel] for i in range(2)]
                           for o in self.peer_owners}
         self.flag_maps = {o: self.heap.open(o, "flags").view(torch.int32) for o in self.peer_owners}
+        self.segments = [(0, self.numel, self.sources, self.scale)]
+
+    def configure_segments(self, owners: list[str], segments: list, step: int = 0):
+        """Different flat ranges reduced over different source sets.
+        segments: [(lo, hi, source_owners_in_fixed_order, scale)].  With tensor
+        parallelism the TP-replicated parameters are summed over the TP pair
+        and averaged over replicas, the TP-sharded ones only averaged over
+        replicas."""
+        self.configure(owners, None, step)
+        for lo, hi, srcs, _ in segments:
+            if not 1 <= len(srcs) <= 8:
+                raise ValueError("1..8 gradient sources per segment")
+            for o in srcs:
+                if o not in self.peer_owners:
+                    raise ValueError(f"segment source {o} is not a member")
+        self.segments = list(segments)
 
     # ------------------------------------------------------------------ per step
     def begin_step(self, step: int, defer: bool = False):
@@ -161,16 +177,20 @@ class CrossReplicaFused:
         ev.record()
         with torch.cuda.stream(self.side):
             self.side.wait_event(ev)
-            sl = slice(bk.start, bk.end)
-            grad_ptrs = [self.grad_maps[o][par][sl].data_ptr() for o in self.sources]
-            flag_ptrs = [self.flag_maps[o][b].data_ptr() for o in self.sources if o != self.heap.owner]
             c, n = st.cur, st.nxt
             o = self.engine.optim
-            ext().fused_reduce_adamw(grad_ptrs, flag_ptrs, tag, st.master[c][sl], st.exp_avg[c][sl],
-                                     st.exp_avg_sq[c][sl], st.master[n][sl], st.exp_avg[n][sl], st.exp_avg_sq[n][sl],
-                                     st.param[n][sl], self.engine.scheduler.get_lr(), o.beta1, o.beta2, o.eps,
-                                     o.weight_decay, st.step + 1, self.scale, self.engine.nonfinite, self.status,
-                                     self.timeout)
+            for lo, hi, srcs, scale in self.segments:
+                s0, s1 = max(bk.start, lo), min(bk.end, hi)
+                if s0 >= s1:
+                    continue
+                sl = slice(s0, s1)
+                grad_ptrs = [self.grad_maps[w][par][sl].data_ptr() for w in srcs]
+                flag_ptrs = [self.flag_maps[w][b].data_ptr() for w in srcs if w != self.heap.owner]
+                ext().fused_reduce_adamw(grad_ptrs, flag_ptrs, tag, st.master[c][sl], st.exp_avg[c][sl],
+                                         st.exp_avg_sq[c][sl], st.master[n][sl], st.exp_avg[n][sl],
+                                         st.exp_avg_sq[n][sl], st.param[n][sl], self.engine.scheduler.get_lr(),
+                                         o.beta1, o.beta2, o.eps, o.weight_decay, st.step + 1, scale,
+                                         self.engine.nonfinite, self.status, self.timeout)
         self.launched.add(b)
 
     def finish_step(self):

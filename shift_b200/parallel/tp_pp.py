@@ -1,0 +1,200 @@
+"""Replicas of TP x PP GPUs on one box (the 2 replicas x 4 GPU layout).
+
+Global rank = replica * (tp*pp) + stage * tp + tp_rank.  Inside a replica:
+tensor parallelism with sequence parallelism and experts split over the TP
+pair (``parallel.tp``), pipeline parallelism with a 1F1B schedule over
+microbatches of one sequence (activations and gradients travel on NCCL p2p,
+batched send/recv pairs in steady state -- the reference keeps PP on NCCL
+p2p too, shift_full/train.py:552).  Across replicas: the fused peer-memory
+reduce + AdamW (K1) per bucket, overlapped with the last microbatch's
+backward; TP-replicated parameters are summed over the TP pair and averaged
+over replicas inside the same kernel.
+"""
+from __future__ import annotations
+
+import zlib
+
+import torch
+import torch.distributed as dist
+
+from ..engine import Engine, synthetic_batch
+from ..models.qwen_moe import TP_SHARDED, MoEConfig, Partition, param_specs
+from ..ops._ext import check_status
+from .replicas import _order
+from .symmetric import CrossReplicaFused, SymmetricHeap
+from .tp import TPComm
+
+
+def _is_sharded(name: str) -> bool:
+    return any(name.endswith(s) for s in TP_SHARDED)
+
+
+class ModelParallelRunner:
+    def __init__(self, cfg: MoEConfig, n_gpus: int, rank: int, local_rank: int, batch: int, seq: int,
+                 replicas: int, tp: int, pp: int, microbatch: int = 1):
+        if replicas * tp * pp != n_gpus:
+            raise ValueError(f"{replicas} x tp{tp} x pp{pp} != {n_gpus} GPUs")
+        if batch % (replicas * microbatch):
+            raise ValueError("global batch must split evenly over replicas and microbatches")
+        if cfg.layers % pp or cfg.experts % tp or cfg.heads % tp or cfg.kv_heads % tp:
+            raise ValueError("layers / experts / heads must divide by pp / tp")
+        self.layout = f"{replicas}x(tp{tp},pp{pp}) sp+ep-over-tp, 1F1B, fused NVLink reduce+AdamW"
+        self.cfg, self.rank = cfg, rank
+        per = tp * pp
+        self.r, rem = divmod(rank, per)
+        self.s, self.t = divmod(rem, tp)
+        self.R, self.TP, self.PP = replicas, tp, pp
+        self.device = torch.device("cuda", local_rank)
+        self.S = seq
+        self.mb = microbatch
+        self.M = batch // replicas // microbatch
+        # ---- process groups (every rank creates every group, in the same order) ----
+        self.tp_group = None
+        for r in range(replicas):
+            for s in range(pp):
+                g = dist.new_group([r * per + s * tp + t for t in range(tp)])
+                if r == self.r and s == self.s:
+                    self.tp_group = g
+        self.pp_ranks = [self.r * per + s * tp + self.t for s in range(pp)]
+        self.pp_group = None
+        for r in range(replicas):
+            for t in range(tp):
+                g = dist.new_group([r * per + s * tp + t for s in range(pp)])
+                if r == self.r and t == self.t:
+                    self.pp_group = g
+        # ---- model partition ----
+        lps = cfg.layers // pp
+        e_per = cfg.experts // tp
+        part = Partition(layer_lo=self.s * lps, layer_hi=(self.s + 1) * lps, has_embed=self.s == 0,
+                         has_head=self.s == pp - 1, expert_lo=self.t * e_per, expert_hi=(self.t + 1) * e_per,
+                         tp_size=tp)
+        specs = param_specs(cfg, part)
+        rep = [s for s in specs if not _is_sharded(s.name)]
+        shard = [s for s in specs if _is_sharded(s.name)]
+        t_rank = self.t
+
+        def seed_of(spec):
+            salt = f"/tp{t_rank}" if _is_sharded(spec.name) else ""
+            return 2026 + zlib.crc32((spec.name + salt).encode())
+
+        self.comm = TPComm(self.tp_group, self.t, tp, self.device)
+        self.engine = Engine(cfg, self.device, part=part, specs=rep + shard, seed_of=seed_of, tp=self.comm)
+        st = self.engine.store
+        self.rep_end = st.offsets[shard[0].name][0] if shard else st.numel
+        # ---- fused cross-replica (and cross-TP for replicated params) reduction ----
+        store = dist.distributed_c10d._get_default_store()
+        self.heap = SymmetricHeap(store, f"r{self.r}s{self.s}t{self.t}", self.device)
+        self.fused = CrossReplicaFused(self.engine, self.heap)
+        dist.barrier()
+        rep_src = [f"r{r}s{self.s}t{t}" for r in range(replicas) for t in range(tp)]
+        shard_src = [f"r{r}s{self.s}t{self.t}" for r in range(replicas)]
+        owners = sorted(set(rep_src) | set(shard_src))
+        self.fused.configure_segments(owners, [(0, self.rep_end, rep_src, 1.0 / replicas),
+                                               (self.rep_end, st.numel, shard_src, 1.0 / replicas)])
+        layers = cfg.layers
+        self._hook = lambda layer: self.fused.on_layer_done(_order(layer, layers))
+        # ---- data: replica r takes sequences [r*B/R, (r+1)*B/R) of the global batch ----
+        b_per = batch // replicas
+        sl = slice(self.r * b_per, (self.r + 1) * b_per)
+        self.dev_batches = [synthetic_batch(cfg, i, batch, seq)[sl].to(self.device) for i in range(2)]
+        self.host = synthetic_batch(cfg, 10_000, batch, seq)[sl].contiguous().pin_memory()
+        self.step_no = 0
+        self.tok_loc = self.mb * seq // tp
+        dist.barrier()
+
+    # ------------------------------------------------------------------ pipeline p2p
+    def _p2p(self, send=None, send_to=None, recv_from=None):
+        ops, buf = [], None
+        if send is not None:
+            ops.append(dist.P2POp(dist.isend, send.contiguous(), self.pp_ranks[send_to], group=self.pp_group))
+        if recv_from is not None:
+            buf = torch.empty(self._act_shape(), dtype=torch.bfloat16, device=self.device)
+            ops.append(dist.P2POp(dist.irecv, buf, self.pp_ranks[recv_from], group=self.pp_group))
+        if ops:
+            for w in dist.batch_isend_irecv(ops):
+                w.wait()
+        return buf
+
+    def _act_shape(self):
+        return (2, self.tok_loc, self.cfg.hidden)
+
+    # ------------------------------------------------------------------ one step (1F1B)
+    def _fwd(self, i, data, hidden):
+        model = self.engine.model
+        tok = data[i * self.mb:(i + 1) * self.mb]
+        out, loss = model.forward(tok[:, :-1] if self.s == 0 else None,
+                                  None if self.s == 0 else (hidden[0], hidden[1]),
+                                  tok[:, 1:] if self.s == self.PP - 1 else None, self.mb, self.S,
+                                  loss_scale=1.0 / (self.M * self.mb * self.S))
+        if loss is not None:
+            self._loss = loss if self._loss is None else self._loss + loss
+        return None if out is None else torch.stack([out[0], out[1]])
+
+    def _bwd(self, i, dout):
+        model = self.engine.model
+        model._accumulate = i > 0
+        model.layer_done_hook = self._hook if i == self.M - 1 else None
+        d = model.backward(None if dout is None else dout[0])
+        model.layer_done_hook = None
+        return None if d is None else torch.stack([d, d])
+
+    def _train(self, data):
+        eng = self.engine
+        eng.nonfinite.zero_()
+        self.fused.begin_step(self.step_no)
+        eng.store.zero_grad()
+        self._loss = None
+        M, s, pp = self.M, self.s, self.PP
+        first, last = s == 0, s == pp - 1
+        n_warm = min(pp - s - 1, M)
+        n_rem = M - n_warm
+        for i in range(n_warm):
+            x = None if first else self._p2p(recv_from=s - 1)
+            y = self._fwd(i, data, x)
+            self._p2p(send=y, send_to=s + 1)
+        x = None if (first or n_rem == 0) else self._p2p(recv_from=s - 1)
+        for j in range(n_rem):
+            i = n_warm + j
+            y = self._fwd(i, data, x)
+            dy = None if last else self._p2p(send=y, send_to=s + 1, recv_from=s + 1)
+            dx = self._bwd(j, dy)
+            if j == n_rem - 1:
+                if not first:
+                    self._p2p(send=dx, send_to=s - 1)
+            else:
+                x = None if first else self._p2p(send=dx, send_to=s - 1, recv_from=s - 1)
+        for j in range(n_rem, M):
+            dy = None if last else self._p2p(recv_from=s + 1)
+            dx = self._bwd(j, dy)
+            if not first:
+                self._p2p(send=dx, send_to=s - 1)
+        eng.model._accumulate = False
+        self.fused.finish_step()
+        eng.commit()
+        self.step_no += 1
+        return self._loss if self._loss is not None else torch.zeros((), device=self.device)
+
+    def step(self, i: int):
+        return self._train(self.dev_batches[i % len(self.dev_batches)])
+
+    def step_e2e(self, i: int):
+        data = self.host.to(self.device, non_blocking=True)
+        loss = self._train(data)
+        val = loss.item()
+        return val, self.host.numel() * self.host.element_size(), 4
+
+    def close(self):
+        torch.cuda.synchronize()
+        check_status(self.device)
+        dist.barrier()
+        self.heap.close_peers()
+
+
+def make_model_parallel_runner(layout: str, cfg, n_gpus, rank, local_rank, batch, seq):
+    """layout: 'tp' (replicas x TP2) or 'tppp' (replicas x TP2 x PP2) or 'auto'."""
+    if layout == "auto":
+        layout = {4: "tp", 8: "tppp"}.get(n_gpus, "tp")
+    tp = 2
+    pp = 2 if layout == "tppp" else 1
+    replicas = n_gpus // (tp * pp)
+    return ModelParallelRunner(cfg, n_gpus, rank, local_rank, batch, seq, replicas, tp, pp)

@@ -59,6 +59,9 @@ void fused_reduce_adamw(const std::vector<int64_t>& grad_ptrs, const std::vector
                         double beta2, double eps, double wd, int64_t step, double grad_scale,
                         const at::Tensor& nonfinite, const at::Tensor& status, double timeout_s);
 void flag_set(int64_t flag_ptr, int64_t value);
+void reduce_slice_scatter(const std::vector<int64_t>& src_ptrs, const std::vector<int64_t>& dst_ptrs, int64_t lo,
+                          int64_t hi, const std::vector<int64_t>& flag_ptrs, int64_t target, double scale,
+                          const at::Tensor& status, double timeout_s);
 void flag_wait(const std::vector<int64_t>& flag_ptrs, int64_t target, const at::Tensor& status, double timeout_s);
 void peer_copy(int64_t src_ptr, int64_t dst_ptr, int64_t nbytes);
 std::string fingerprint(const at::Tensor& t);
@@ -97,6 +100,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_open", &sb::coll::ipc_open);
   m.def("fused_reduce_adamw", &sb::coll::fused_reduce_adamw, "K1: cross-replica reduce + cast + scale + AdamW");
   m.def("flag_set", &sb::coll::flag_set);
+  m.def("reduce_slice_scatter", &sb::coll::reduce_slice_scatter, "K1 phase A: reduce-scatter + all-gather via P2P");
   m.def("flag_wait", &sb::coll::flag_wait);
   m.def("peer_copy", &sb::coll::peer_copy, "K10: SM-driven peer-memory copy");
   m.def("pair_reduce_scatter", &sb::coll::pair_reduce_scatter);

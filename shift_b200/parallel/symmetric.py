@@ -74,7 +74,7 @@ def _tag(step: int) -> int:
 class CrossReplicaFused:
     """K1 for one rank: fused cross-replica gradient reduction + AdamW."""
 
-    def __init__(self, engine, heap: SymmetricHeap, timeout_s: float = 30.0):
+    def __init__(self, engine, heap: SymmetricHeap, timeout_s: float = 30.0, two_phase: bool = True):
         self.engine = engine
         self.heap = heap
         self.timeout = timeout_s
@@ -83,7 +83,12 @@ class CrossReplicaFused:
         nbytes = self.numel * 2
         self.gbuf = [heap.alloc(f"grad{i}", nbytes).view(torch.bfloat16)[: self.numel] for i in range(2)]
         self.nb = len(st.buckets)
-        self.flags = heap.alloc("flags", 4 * (self.nb + 2) + 64).view(torch.int32)
+        # flags: ready[nb] | done[2] | slice[nb]
+        self.flags = heap.alloc("flags", 4 * (2 * self.nb + 2) + 64).view(torch.int32)
+        # reduced gradient written by every member's slice (two-phase K1)
+        self.two_phase = two_phase
+        if two_phase:
+            self.red = heap.alloc("red", nbytes).view(torch.bfloat16)[: self.numel]
         st.set_grad_buffers(self.gbuf)
         self.side = torch.cuda.Stream(device=heap.device)
         self.peer_owners: list[str] = [heap.owner]
@@ -122,7 +127,9 @@ class CrossReplicaFused:
         self.grad_maps = {o: [self.heap.open(o, f"grad{i}").view(torch.bfloat16)[: self.numel] for i in range(2)]
                           for o in self.peer_owners}
         self.flag_maps = {o: self.heap.open(o, "flags").view(torch.int32) for o in self.peer_owners}
-        self.segments = [(0, self.numel, self.sources, self.scale)]
+        if self.two_phase:
+            self.red_maps = {o: self.heap.open(o, "red").view(torch.bfloat16)[: self.numel] for o in self.peer_owners}
+        self.segments = [(0, self.numel, self.sources, self.scale, list(self.peer_owners))]
 
     def configure_segments(self, owners: list[str], segments: list, step: int = 0):
         """Different flat ranges reduced over different source sets.
@@ -179,7 +186,12 @@ class CrossReplicaFused:
             self.side.wait_event(ev)
             c, n = st.cur, st.nxt
             o = self.engine.optim
-            for lo, hi, srcs, scale in self.segments:
+            if self.two_phase:
+                self._two_phase(b, bk, par, tag, c, n, o)
+                self.launched.add(b)
+                return
+            for seg in self.segments:
+                lo, hi, srcs, scale = seg[:4]
                 s0, s1 = max(bk.start, lo), min(bk.end, hi)
                 if s0 >= s1:
                     continue
@@ -192,6 +204,41 @@ class CrossReplicaFused:
                                          o.beta1, o.beta2, o.eps, o.weight_decay, st.step + 1, scale,
                                          self.engine.nonfinite, self.status, self.timeout)
         self.launched.add(b)
+
+    def _two_phase(self, b, bk, par, tag, c, n, o):
+        """Phase A: reduce this rank's slice of every segment and store it into
+        every member's reduced buffer; publish slice[b].  Phase B: AdamW from
+        the local reduced gradient once every source's slice has landed."""
+        st = self.engine.store
+        me = self.heap.owner
+        slice_flag = self.nb + 2 + b
+        parts = []
+        for seg in self.segments:
+            lo, hi, srcs, scale = seg[:4]
+            # receivers: the sources plus, for the whole-model segment of a
+            # quorum, members that do not contribute (healing / spare)
+            members = seg[4] if len(seg) > 4 else list(srcs)
+            s0, s1 = max(bk.start, lo), min(bk.end, hi)
+            if s0 >= s1:
+                continue
+            parts.append((s0, s1, srcs))
+            if me not in srcs:
+                continue           # a non-participating member only receives
+            k, ns = srcs.index(me), len(srcs)
+            cuts = [s0 + ((s1 - s0) * j // ns) // 8 * 8 for j in range(ns)] + [s1]
+            ext().reduce_slice_scatter([self.grad_maps[w][par].data_ptr() for w in srcs],
+                                       [self.red_maps[w].data_ptr() for w in members], cuts[k], cuts[k + 1],
+                                       [self.flag_maps[w][b].data_ptr() for w in srcs if w != me], tag, scale,
+                                       self.status, self.timeout)
+        ext().flag_set(self.flags[slice_flag].data_ptr(), tag)
+        for s0, s1, srcs in parts:
+            sl = slice(s0, s1)
+            ext().fused_reduce_adamw([self.red[sl].data_ptr()],
+                                     [self.flag_maps[w][slice_flag].data_ptr() for w in srcs if w != me], tag,
+                                     st.master[c][sl], st.exp_avg[c][sl], st.exp_avg_sq[c][sl], st.master[n][sl],
+                                     st.exp_avg[n][sl], st.exp_avg_sq[n][sl], st.param[n][sl],
+                                     self.engine.scheduler.get_lr(), o.beta1, o.beta2, o.eps, o.weight_decay,
+                                     st.step + 1, 1.0, self.engine.nonfinite, self.status, self.timeout)
 
     def finish_step(self):
         """After backward: launch what is left, publish done, join streams."""

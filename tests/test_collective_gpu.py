@@ -156,4 +156,6 @@ def test_fused_cross_replica_two_gpus_bit_identical_and_matches_reference():
     assert got[0][2] == 0 and got[1][2] == 0
     assert torch.equal(m0, m1), "replicas diverged"
     refm = got["ref"][1]
-    assert torch.allclose(m0, refm, atol=1e-6, rtol=1e-5)
+    # the two-phase reduction rounds the averaged gradient to bf16 before AdamW
+    # (as a bf16 all-reduce would); the reference sums in fp32
+    assert torch.allclose(m0, refm, atol=2e-5, rtol=1e-4)

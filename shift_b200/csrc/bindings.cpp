@@ -40,7 +40,7 @@ namespace adam {
 void adamw_step(const at::Tensor& master, const at::Tensor& m, const at::Tensor& v, const std::vector<at::Tensor>& grads,
                 at::Tensor& master_out, at::Tensor& m_out, at::Tensor& v_out, at::Tensor& param_out, double lr,
                 double beta1, double beta2, double eps, double wd, int64_t step, double grad_scale,
-                const c10::optional<at::Tensor>& nonfinite);
+                const c10::optional<at::Tensor>& nonfinite, const c10::optional<at::Tensor>& step_dev);
 void nonfinite_check(const at::Tensor& x, at::Tensor& flag);
 }  // namespace adam
 namespace fa {
@@ -53,16 +53,17 @@ namespace coll {
 at::Tensor sym_alloc(int64_t nbytes, int64_t device);
 at::Tensor ipc_handle(const at::Tensor& t);
 at::Tensor ipc_open(const at::Tensor& handle, int64_t nbytes, int64_t device);
-void fused_reduce_adamw(const std::vector<int64_t>& grad_ptrs, const std::vector<int64_t>& flag_ptrs, int64_t target,
-                        const at::Tensor& master, const at::Tensor& m, const at::Tensor& v, at::Tensor& master_out,
-                        at::Tensor& m_out, at::Tensor& v_out, at::Tensor& param_out, double lr, double beta1,
-                        double beta2, double eps, double wd, int64_t step, double grad_scale,
+void fused_reduce_adamw(const std::vector<int64_t>& grad_ptrs, const std::vector<int64_t>& flag_ptrs,
+                        const at::Tensor& step_dev, const at::Tensor& master, const at::Tensor& m, const at::Tensor& v,
+                        at::Tensor& master_out, at::Tensor& m_out, at::Tensor& v_out, at::Tensor& param_out,
+                        double beta1, double beta2, double eps, double wd, double grad_scale,
                         const at::Tensor& nonfinite, const at::Tensor& status, double timeout_s);
-void flag_set(int64_t flag_ptr, int64_t value);
+void flag_set(int64_t flag_ptr, const at::Tensor& step_dev, int64_t delta);
 void reduce_slice_scatter(const std::vector<int64_t>& src_ptrs, const std::vector<int64_t>& dst_ptrs, int64_t lo,
-                          int64_t hi, const std::vector<int64_t>& flag_ptrs, int64_t target, double scale,
-                          const at::Tensor& status, double timeout_s);
-void flag_wait(const std::vector<int64_t>& flag_ptrs, int64_t target, const at::Tensor& status, double timeout_s);
+                          int64_t hi, const std::vector<int64_t>& flag_ptrs, const at::Tensor& step_dev,
+                          double scale, const at::Tensor& status, double timeout_s);
+void flag_wait(const std::vector<int64_t>& flag_ptrs, const at::Tensor& step_dev, int64_t delta,
+               const at::Tensor& status, double timeout_s);
 void peer_copy(int64_t src_ptr, int64_t dst_ptr, int64_t nbytes);
 std::string fingerprint(const at::Tensor& t);
 void pair_reduce_scatter(int64_t a_ptr, int64_t b_ptr, at::Tensor& out, const std::vector<int64_t>& flag_ptrs,
@@ -91,7 +92,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("swiglu_fwd", &sb::moe::swiglu_fwd);
   m.def("swiglu_bwd", &sb::moe::swiglu_bwd);
   m.def("xent_fwd_bwd", &sb::xent::xent_fwd_bwd);
-  m.def("adamw_step", &sb::adam::adamw_step);
+  m.def("adamw_step", &sb::adam::adamw_step, py::arg("master"), py::arg("m"), py::arg("v"), py::arg("grads"),
+        py::arg("master_out"), py::arg("m_out"), py::arg("v_out"), py::arg("param_out"), py::arg("lr"), py::arg("beta1"),
+        py::arg("beta2"), py::arg("eps"), py::arg("wd"), py::arg("step"), py::arg("grad_scale"),
+        py::arg("nonfinite") = py::none(), py::arg("step_dev") = py::none());
   m.def("nonfinite_check", &sb::adam::nonfinite_check);
   m.def("attn_fwd", &sb::fa::fwd, "tcgen05 causal flash attention forward");
   m.def("attn_bwd", &sb::fa::bwd, "tcgen05 causal flash attention backward (dK/dV + dQ kernels)");

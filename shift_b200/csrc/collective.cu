@@ -57,12 +57,24 @@ __device__ bool cta_wait_flags(const FlagPtrs& f, int n, int target, int* status
   return ok != 0;
 }
 
+// Per-step scalars live in device memory so that a captured CUDA graph replays
+// correctly every step: sdev[0] = step tag (int), sdev[1..3] = lr, 1 - beta1^t,
+// sqrt(1 - beta2^t) (float bits).
+SB_DEVICE void load_step(const int* sdev, int& tag, AdamHyper& a) {
+  tag = sdev[0];
+  a.lr = __int_as_float(sdev[1]);
+  a.bc1 = __int_as_float(sdev[2]);
+  a.bc2_sqrt = __int_as_float(sdev[3]);
+}
+
 __global__ void __launch_bounds__(256)
-fused_reduce_adamw_kernel(SrcPtrs src, int n_src, FlagPtrs flags, int n_flags, int target,
+fused_reduce_adamw_kernel(SrcPtrs src, int n_src, FlagPtrs flags, int n_flags, const int* __restrict__ sdev,
                           const float* __restrict__ master, const float* __restrict__ m_in,
                           const float* __restrict__ v_in, float* __restrict__ master_out, float* __restrict__ m_out,
                           float* __restrict__ v_out, __nv_bfloat16* __restrict__ param_out, long n, AdamHyper a,
                           int* __restrict__ nonfinite, int* __restrict__ status, uint64_t timeout_ns) {
+  int target;
+  load_step(sdev, target, a);
   if (n_flags > 0 && !cta_wait_flags(flags, n_flags, target, status, timeout_ns)) return;
   const long stride = static_cast<long>(gridDim.x) * blockDim.x * 8;
   bool bad = false;
@@ -146,7 +158,9 @@ struct DstPtrs {
 
 __global__ void __launch_bounds__(256)
 reduce_slice_scatter_kernel(SrcPtrs src, int n_src, DstPtrs dst, int n_dst, long lo, long hi, FlagPtrs flags,
-                            int n_flags, int target, float scale, int* __restrict__ status, uint64_t timeout_ns) {
+                            int n_flags, const int* __restrict__ sdev, float scale, int* __restrict__ status,
+                            uint64_t timeout_ns) {
+  const int target = sdev[0];
   if (n_flags > 0 && !cta_wait_flags(flags, n_flags, target, status, timeout_ns)) return;
   const long stride = static_cast<long>(gridDim.x) * blockDim.x * 8;
   for (long i = lo + (static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x) * 8; i < hi; i += stride) {
@@ -186,14 +200,18 @@ reduce_slice_scatter_kernel(SrcPtrs src, int n_src, DstPtrs dst, int n_dst, long
 }
 
 // ---------------------------------------------------------------------------
-__global__ void flag_set_kernel(int* flag, int value) {
+// flag = step tag + delta
+__global__ void flag_set_kernel(int* flag, const int* __restrict__ sdev, int delta) {
   if (threadIdx.x == 0 && blockIdx.x == 0) {
     __threadfence_system();
-    st_release_sys(flag, value);
+    st_release_sys(flag, sdev[0] + delta);
   }
 }
 
-__global__ void flag_wait_kernel(FlagPtrs f, int n, int target, int* status, uint64_t timeout_ns) {
+// wait until every flag >= step tag + delta
+__global__ void flag_wait_kernel(FlagPtrs f, int n, const int* __restrict__ sdev, int delta, int* status,
+                                 uint64_t timeout_ns) {
+  const int target = sdev[0] + delta;
   if (threadIdx.x == 0 && blockIdx.x == 0) {
     for (int i = 0; i < n; ++i) {
       if (f.p[i] == nullptr) continue;
@@ -308,33 +326,40 @@ static FlagPtrs make_flags(const std::vector<int64_t>& ptrs) {
   return f;
 }
 
+void check_step_dev(const at::Tensor& step_dev, const at::Tensor& like) {
+  TORCH_CHECK(step_dev.is_cuda() && step_dev.scalar_type() == at::kInt && step_dev.numel() >= 4 &&
+                  step_dev.device() == like.device(),
+              "step_dev: int32[>=4] on the parameter's device");
+}
+
 // K1.  grad_ptrs: device addresses (local or IPC-mapped) of the bucket's
 // gradient in each participant, in replica order.  flag_ptrs: addresses of
 // the participants' ready flags for this bucket; target: the step tag.
-void fused_reduce_adamw(const std::vector<int64_t>& grad_ptrs, const std::vector<int64_t>& flag_ptrs, int64_t target,
-                        const at::Tensor& master, const at::Tensor& m, const at::Tensor& v, at::Tensor& master_out,
-                        at::Tensor& m_out, at::Tensor& v_out, at::Tensor& param_out, double lr, double beta1,
-                        double beta2, double eps, double wd, int64_t step, double grad_scale,
+void fused_reduce_adamw(const std::vector<int64_t>& grad_ptrs, const std::vector<int64_t>& flag_ptrs,
+                        const at::Tensor& step_dev, const at::Tensor& master, const at::Tensor& m, const at::Tensor& v,
+                        at::Tensor& master_out, at::Tensor& m_out, at::Tensor& v_out, at::Tensor& param_out,
+                        double beta1, double beta2, double eps, double wd, double grad_scale,
                         const at::Tensor& nonfinite, const at::Tensor& status, double timeout_s) {
+  check_step_dev(step_dev, master);
   TORCH_CHECK(!grad_ptrs.empty() && grad_ptrs.size() <= static_cast<size_t>(kMaxSrc), "1..8 gradient sources");
   const at::cuda::CUDAGuard guard(master.device());
   SrcPtrs src{};
   for (size_t i = 0; i < grad_ptrs.size(); ++i) src.p[i] = reinterpret_cast<const __nv_bfloat16*>(grad_ptrs[i]);
   FlagPtrs f = make_flags(flag_ptrs);
   AdamHyper a;
-  a.lr = static_cast<float>(lr);
+  a.lr = 0.f;  // lr and bias corrections come from step_dev
   a.beta1 = static_cast<float>(beta1);
   a.beta2 = static_cast<float>(beta2);
   a.eps = static_cast<float>(eps);
   a.wd = static_cast<float>(wd);
-  a.bc1 = static_cast<float>(1.0 - std::pow(beta1, static_cast<double>(step)));
-  a.bc2_sqrt = static_cast<float>(std::sqrt(1.0 - std::pow(beta2, static_cast<double>(step))));
+  a.bc1 = 1.f;
+  a.bc2_sqrt = 1.f;
   a.grad_scale = static_cast<float>(grad_scale);
   const long n = master.numel();
   if (n == 0) return;
   const long blocks = std::min<long>((n / 8 + 255) / 256 + 1, static_cast<long>(sm_count()) * 8);
   fused_reduce_adamw_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      src, static_cast<int>(grad_ptrs.size()), f, static_cast<int>(flag_ptrs.size()), static_cast<int>(target),
+      src, static_cast<int>(grad_ptrs.size()), f, static_cast<int>(flag_ptrs.size()), step_dev.data_ptr<int>(),
       master.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), master_out.data_ptr<float>(),
       m_out.data_ptr<float>(), v_out.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(param_out.data_ptr()), n, a,
       nonfinite.data_ptr<int>(), status.data_ptr<int>(), static_cast<uint64_t>(timeout_s * 1e9));
@@ -344,8 +369,8 @@ void fused_reduce_adamw(const std::vector<int64_t>& grad_ptrs, const std::vector
 // Phase A of the two-phase K1 (see reduce_slice_scatter_kernel).  Ranges are
 // element offsets relative to the given base pointers.
 void reduce_slice_scatter(const std::vector<int64_t>& src_ptrs, const std::vector<int64_t>& dst_ptrs, int64_t lo,
-                          int64_t hi, const std::vector<int64_t>& flag_ptrs, int64_t target, double scale,
-                          const at::Tensor& status, double timeout_s) {
+                          int64_t hi, const std::vector<int64_t>& flag_ptrs, const at::Tensor& step_dev,
+                          double scale, const at::Tensor& status, double timeout_s) {
   TORCH_CHECK(!src_ptrs.empty() && src_ptrs.size() <= static_cast<size_t>(kMaxSrc), "1..8 sources");
   TORCH_CHECK(!dst_ptrs.empty() && dst_ptrs.size() <= static_cast<size_t>(kMaxSrc), "1..8 destinations");
   if (hi <= lo) return;
@@ -357,22 +382,25 @@ void reduce_slice_scatter(const std::vector<int64_t>& src_ptrs, const std::vecto
   const long blocks = std::max<long>(1, std::min<long>((n / 8 + 255) / 256 + 1, static_cast<long>(sm_count()) * 4));
   reduce_slice_scatter_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       s, static_cast<int>(src_ptrs.size()), d, static_cast<int>(dst_ptrs.size()), lo, hi, make_flags(flag_ptrs),
-      static_cast<int>(flag_ptrs.size()), static_cast<int>(target), static_cast<float>(scale),
+      static_cast<int>(flag_ptrs.size()), step_dev.data_ptr<int>(), static_cast<float>(scale),
       status.data_ptr<int>(), static_cast<uint64_t>(timeout_s * 1e9));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-void flag_set(int64_t flag_ptr, int64_t value) {
+// flag := step_dev[0] + delta (release, system scope)
+void flag_set(int64_t flag_ptr, const at::Tensor& step_dev, int64_t delta) {
   flag_set_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(reinterpret_cast<int*>(flag_ptr),
-                                                                   static_cast<int>(value));
+                                                                   step_dev.data_ptr<int>(), static_cast<int>(delta));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-void flag_wait(const std::vector<int64_t>& flag_ptrs, int64_t target, const at::Tensor& status, double timeout_s) {
+// bounded wait until every flag >= step_dev[0] + delta
+void flag_wait(const std::vector<int64_t>& flag_ptrs, const at::Tensor& step_dev, int64_t delta,
+               const at::Tensor& status, double timeout_s) {
   if (flag_ptrs.empty()) return;
   flag_wait_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(
-      make_flags(flag_ptrs), static_cast<int>(flag_ptrs.size()), static_cast<int>(target), status.data_ptr<int>(),
-      static_cast<uint64_t>(timeout_s * 1e9));
+      make_flags(flag_ptrs), static_cast<int>(flag_ptrs.size()), step_dev.data_ptr<int>(), static_cast<int>(delta),
+      status.data_ptr<int>(), static_cast<uint64_t>(timeout_s * 1e9));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

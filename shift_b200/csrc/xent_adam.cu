@@ -140,7 +140,12 @@ struct GradSources {
 __global__ void adamw_kernel(const float* __restrict__ master, const float* __restrict__ m_in,
                              const float* __restrict__ v_in, const GradSources grads, int n_grads, float* __restrict__ master_out, float* __restrict__ m_out,
                              float* __restrict__ v_out, __nv_bfloat16* __restrict__ param_out, long n, AdamArgs a,
-                             int* __restrict__ nonfinite) {
+                             int* __restrict__ nonfinite, const int* __restrict__ sdev) {
+  if (sdev != nullptr) {   // per-step scalars from device memory (graph-replayable)
+    a.lr = __int_as_float(sdev[1]);
+    a.bc1 = __int_as_float(sdev[2]);
+    a.bc2_sqrt = __int_as_float(sdev[3]);
+  }
   const long i0 = (static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
   const long stride = static_cast<long>(gridDim.x) * blockDim.x * 4;
   bool bad = false;
@@ -198,8 +203,12 @@ __global__ void adamw_kernel(const float* __restrict__ master, const float* __re
 void adamw_step(const at::Tensor& master, const at::Tensor& m, const at::Tensor& v, const std::vector<at::Tensor>& grads,
                 at::Tensor& master_out, at::Tensor& m_out, at::Tensor& v_out, at::Tensor& param_out, double lr,
                 double beta1, double beta2, double eps, double wd, int64_t step, double grad_scale,
-                const c10::optional<at::Tensor>& nonfinite) {
+                const c10::optional<at::Tensor>& nonfinite, const c10::optional<at::Tensor>& step_dev) {
   TORCH_CHECK(grads.size() >= 1 && grads.size() <= 8, "adamw: 1..8 gradient sources");
+  if (step_dev.has_value())
+    TORCH_CHECK(step_dev->is_cuda() && step_dev->scalar_type() == at::kInt && step_dev->numel() >= 4 &&
+                    step_dev->device() == master.device(),
+                "adamw: step_dev int32[>=4] on the parameter's device");
   const at::cuda::CUDAGuard guard(master.device());
   const long n = master.numel();
   for (auto& g : grads) TORCH_CHECK(g.numel() == n && g.scalar_type() == at::kBFloat16, "adamw: bf16 grads of equal size");
@@ -222,7 +231,8 @@ void adamw_step(const at::Tensor& master, const at::Tensor& m, const at::Tensor&
       src, static_cast<int>(grads.size()),
       master_out.data_ptr<float>(), m_out.data_ptr<float>(), v_out.data_ptr<float>(),
       reinterpret_cast<__nv_bfloat16*>(param_out.data_ptr()), n, a,
-      nonfinite.has_value() ? nonfinite->data_ptr<int>() : nullptr);
+      nonfinite.has_value() ? nonfinite->data_ptr<int>() : nullptr,
+      step_dev.has_value() ? step_dev->data_ptr<int>() : nullptr);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -76,6 +76,42 @@ def synthetic_batch(cfg: MoEConfig, sample: int, B: int, S: int, mode: str = "ra
     return torch.randint(0, cfg.vocab, (B, S + 1), generator=g, dtype=torch.int64).to(torch.int32)
 
 
+class StepBlock:
+    """Per-step scalars the optimizer and flag kernels read from device memory
+    (int32[8]: step tag, then lr, 1 - beta1^t, sqrt(1 - beta2^t) as float
+    bits), so that a captured CUDA graph of a whole step replays correctly.
+    The host writes it once per step with one asynchronous copy from a ring
+    of pinned slots (each slot reused only after its copy has finished)."""
+
+    def __init__(self, device: torch.device, slots: int = 4):
+        self.device = torch.device(device)
+        self.dev = torch.zeros(8, dtype=torch.int32, device=self.device)
+        cuda = self.device.type == "cuda"
+        self.host = torch.zeros(slots, 8, dtype=torch.int32, pin_memory=cuda)
+        self._np = self.host.numpy()
+        self._f32 = self._np.view("float32")
+        self._events: list = [None] * slots
+        self._i = 0
+        self.values = (0, 0.0, 1.0, 1.0)
+
+    def write(self, tag: int, lr: float, beta1: float, beta2: float, step: int):
+        bc1 = 1.0 - beta1 ** step
+        bc2 = math.sqrt(1.0 - beta2 ** step)
+        self.values = (tag, lr, bc1, bc2)
+        k = self._i % len(self._events)
+        self._i += 1
+        ev = self._events[k]
+        if ev is not None:
+            ev.synchronize()
+        self._np[k, 0] = tag
+        self._f32[k, 1:4] = (lr, bc1, bc2)
+        self.dev.copy_(self.host[k], non_blocking=True)
+        if self.device.type == "cuda":
+            ev = torch.cuda.Event()
+            ev.record()
+            self._events[k] = ev
+
+
 class Engine:
     def __init__(self, cfg: MoEConfig, device, part: Partition | None = None, optim: OptimConfig | None = None,
                  seed: int = 2026, bucket_numel: int = 64 * 1024 * 1024, compute_dtype=None,
@@ -92,6 +128,12 @@ class Engine:
         self.model = QwenMoE(cfg, self.store, self.part, tp=tp)
         self.scheduler = StepLR(self.optim.lr, self.optim.step_size, self.optim.gamma)
         self.nonfinite = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.step_block = StepBlock(self.device)
+
+    def prepare_step(self, tag: int = 0):
+        """Write this step's device step block (call before launching the step)."""
+        o = self.optim
+        self.step_block.write(tag, self.scheduler.get_lr(), o.beta1, o.beta2, self.store.step + 1)
 
     # ------------------------------------------------------------------ compute
     def forward_backward(self, batches: list, B: int, S: int):
@@ -115,18 +157,22 @@ class Engine:
         self.model._accumulate = False
         return total / n_tok
 
-    def optimizer_step(self, grad_sources: list | None = None, grad_scale: float = 1.0):
+    def optimizer_step(self, grad_sources: list | None = None, grad_scale: float = 1.0, prepared: bool = False):
         """Fused AdamW over the whole flat buffer: reads generation cur, writes
-        cur^1.  grad_sources defaults to this rank's own gradient."""
+        cur^1.  grad_sources defaults to this rank's own gradient.
+        ``prepared``: the step block was already written for this step (the
+        launch then carries no per-step host scalars, e.g. inside a graph)."""
         st = self.store
         c, n = st.cur, st.nxt
         o = self.optim
         step = st.step + 1
         lr = self.scheduler.get_lr()
+        if not prepared:
+            self.prepare_step(self.step_block.values[0])
         self.nonfinite.zero_()
         Fn.adamw_step(st.master[c], st.exp_avg[c], st.exp_avg_sq[c], grad_sources or [st.grad], st.master[n],
                       st.exp_avg[n], st.exp_avg_sq[n], st.param[n], lr, o.beta1, o.beta2, o.eps, o.weight_decay,
-                      step, grad_scale, self.nonfinite)
+                      step, grad_scale, self.nonfinite, step_dev=self.step_block.dev)
         return self.nonfinite
 
     def commit(self):

@@ -263,10 +263,12 @@ def xent_fwd_bwd(logits, labels, scale, label_lo=0):
 
 # ----------------------------------------------------------------------------- optimizer
 def adamw_step(master, m, v, grads, master_out, m_out, v_out, param_out, lr, beta1, beta2, eps, wd, step,
-               grad_scale, nonfinite=None):
+               grad_scale, nonfinite=None, step_dev=None):
+    """``step_dev`` (CUDA only): int32 device block whose [1..3] hold lr,
+    1 - beta1^t and sqrt(1 - beta2^t) as float bits; it overrides lr/step."""
     if master.is_cuda:
         ext().adamw_step(master, m, v, list(grads), master_out, m_out, v_out, param_out, lr, beta1, beta2, eps, wd,
-                         step, grad_scale, nonfinite)
+                         step, grad_scale, nonfinite, step_dev)
         return
     g = grads[0].float().clone()
     for extra in grads[1:]:

@@ -14,9 +14,10 @@ import torch
 import torch.distributed as dist
 
 from ..engine import Engine, synthetic_batch
+from ..graphs import StepGraphs, graphs_enabled
 from ..models.qwen_moe import MoEConfig
 from ..ops._ext import check_status
-from .symmetric import CrossReplicaFused, SymmetricHeap
+from .symmetric import CrossReplicaFused, SymmetricHeap, _tag
 
 
 def _order(layer: int, layers: int) -> int:
@@ -50,6 +51,8 @@ class ReplicaDPRunner:
         sl = slice(rank * self.B, (rank + 1) * self.B)
         self.dev_batches = [synthetic_batch(cfg, i, batch, seq)[sl].to(self.device) for i in range(4)]
         self.host = synthetic_batch(cfg, 10_000, batch, seq)[sl].contiguous().pin_memory()
+        self.tokens = torch.empty(self.B, seq + 1, dtype=torch.int32, device=self.device)
+        self.graphs = StepGraphs(self.device, graphs_enabled())
         self.manager = None
         self.step_no = 0
         if with_manager:
@@ -68,14 +71,24 @@ class ReplicaDPRunner:
         self.manager = Manager(None, None, None, self.world, f"shift{self.rank}", addr, rank=0, world_size=1,
                                store=store, local_prefix=f"/bench{self.rank}")
 
-    def _train(self, data):
-        tok, lab = data[:, :-1], data[:, 1:]
-        if self.manager is not None:
-            self.manager.start_quorum()
+    def _device_step(self):
+        step = self.step_no
+        tok, lab = self.tokens[:, :-1], self.tokens[:, 1:]
         self.engine.nonfinite.zero_()
-        self.fused.begin_step(self.step_no)
+        self.fused.begin_step(step, prepare=False)
         loss = self.engine.forward_backward([(tok, lab)], self.B, self.S)
         self.fused.finish_step()
+        return loss
+
+    def _train(self):
+        if self.manager is not None:
+            self.manager.start_quorum()
+        step = self.step_no
+        self.engine.prepare_step(_tag(step))
+        if step < 2:      # eager warm-up steps; buffer-reuse waits start at step 2
+            loss = self._device_step()
+        else:
+            loss = self.graphs.run((self.engine.store.cur, step % 2), self._device_step)
         commit = True
         if self.manager is not None:
             commit = self.manager.should_commit()
@@ -85,16 +98,18 @@ class ReplicaDPRunner:
         return loss
 
     def step(self, i: int):
-        return self._train(self.dev_batches[i % len(self.dev_batches)])
+        self.tokens.copy_(self.dev_batches[i % len(self.dev_batches)])
+        return self._train()
 
     def step_e2e(self, i: int):
-        data = self.host.to(self.device, non_blocking=True)
-        loss = self._train(data)
+        self.tokens.copy_(self.host, non_blocking=True)
+        loss = self._train()
         val = loss.item()
         return val, self.host.numel() * self.host.element_size(), 4
 
     def close(self):
         torch.cuda.synchronize()
+        self.graphs.reset()
         check_status(self.device)
         if self.manager is not None:
             self.manager.shutdown()

@@ -147,19 +147,24 @@ class CrossReplicaFused:
         self.segments = list(segments)
 
     # ------------------------------------------------------------------ per step
-    def begin_step(self, step: int, defer: bool = False):
+    def begin_step(self, step: int, defer: bool = False, prepare: bool = True):
         """Select this step's gradient buffer; make sure every peer finished
         reading it two steps ago.  ``defer``: launch no bucket during backward
         (membership may change before the reduction, e.g. a gradient relay);
-        ``finish_step`` then launches every bucket."""
+        ``finish_step`` then launches every bucket.  ``prepare=False``: the
+        caller already wrote the engine's step block (``prepare_step(tag)``),
+        as it must when this step is being captured into a CUDA graph."""
         self.step = step
         par = step % 2
         self.engine.store.select_grad(par)
+        if prepare:
+            self.engine.prepare_step(_tag(step))
+        self.sdev = self.engine.step_block.dev
         if step >= 2:
             since = getattr(self, "member_since", {})
             ptrs = [self.flag_maps[o][self.nb + par].data_ptr() for o in self.peer_owners
                     if o != self.heap.owner and since.get(o, 0) <= step - 2]
-            ext().flag_wait(ptrs, _tag(step - 2), self.status, self.timeout)
+            ext().flag_wait(ptrs, self.sdev, -2, self.status, self.timeout)
         self.launched = set()
         self.active = not defer
         self.progress = -1
@@ -179,7 +184,7 @@ class CrossReplicaFused:
         par = self.step % 2
         tag = _tag(self.step)
         my_flags = self.flags
-        ext().flag_set(my_flags[b].data_ptr(), tag)   # compute stream: grads of bucket b are written
+        ext().flag_set(my_flags[b].data_ptr(), self.sdev, 0)   # compute stream: grads of bucket b are written
         ev = torch.cuda.Event()
         ev.record()
         with torch.cuda.stream(self.side):
@@ -198,11 +203,10 @@ class CrossReplicaFused:
                 sl = slice(s0, s1)
                 grad_ptrs = [self.grad_maps[w][par][sl].data_ptr() for w in srcs]
                 flag_ptrs = [self.flag_maps[w][b].data_ptr() for w in srcs if w != self.heap.owner]
-                ext().fused_reduce_adamw(grad_ptrs, flag_ptrs, tag, st.master[c][sl], st.exp_avg[c][sl],
+                ext().fused_reduce_adamw(grad_ptrs, flag_ptrs, self.sdev, st.master[c][sl], st.exp_avg[c][sl],
                                          st.exp_avg_sq[c][sl], st.master[n][sl], st.exp_avg[n][sl],
-                                         st.exp_avg_sq[n][sl], st.param[n][sl], self.engine.scheduler.get_lr(),
-                                         o.beta1, o.beta2, o.eps, o.weight_decay, st.step + 1, scale,
-                                         self.engine.nonfinite, self.status, self.timeout)
+                                         st.exp_avg_sq[n][sl], st.param[n][sl], o.beta1, o.beta2, o.eps,
+                                         o.weight_decay, scale, self.engine.nonfinite, self.status, self.timeout)
         self.launched.add(b)
 
     def _two_phase(self, b, bk, par, tag, c, n, o):
@@ -228,17 +232,16 @@ class CrossReplicaFused:
             cuts = [s0 + ((s1 - s0) * j // ns) // 8 * 8 for j in range(ns)] + [s1]
             ext().reduce_slice_scatter([self.grad_maps[w][par].data_ptr() for w in srcs],
                                        [self.red_maps[w].data_ptr() for w in members], cuts[k], cuts[k + 1],
-                                       [self.flag_maps[w][b].data_ptr() for w in srcs if w != me], tag, scale,
-                                       self.status, self.timeout)
-        ext().flag_set(self.flags[slice_flag].data_ptr(), tag)
+                                       [self.flag_maps[w][b].data_ptr() for w in srcs if w != me], self.sdev,
+                                       scale, self.status, self.timeout)
+        ext().flag_set(self.flags[slice_flag].data_ptr(), self.sdev, 0)
         for s0, s1, srcs in parts:
             sl = slice(s0, s1)
             ext().fused_reduce_adamw([self.red[sl].data_ptr()],
-                                     [self.flag_maps[w][slice_flag].data_ptr() for w in srcs if w != me], tag,
+                                     [self.flag_maps[w][slice_flag].data_ptr() for w in srcs if w != me], self.sdev,
                                      st.master[c][sl], st.exp_avg[c][sl], st.exp_avg_sq[c][sl], st.master[n][sl],
-                                     st.exp_avg[n][sl], st.exp_avg_sq[n][sl], st.param[n][sl],
-                                     self.engine.scheduler.get_lr(), o.beta1, o.beta2, o.eps, o.weight_decay,
-                                     st.step + 1, 1.0, self.engine.nonfinite, self.status, self.timeout)
+                                     st.exp_avg[n][sl], st.exp_avg_sq[n][sl], st.param[n][sl], o.beta1, o.beta2,
+                                     o.eps, o.weight_decay, 1.0, self.engine.nonfinite, self.status, self.timeout)
 
     def finish_step(self):
         """After backward: launch what is left, publish done, join streams."""
@@ -247,6 +250,6 @@ class CrossReplicaFused:
                 self._launch(b)
         cur = torch.cuda.current_stream()
         cur.wait_stream(self.side)
-        ext().flag_set(self.flags[self.nb + self.step % 2].data_ptr(), _tag(self.step))
+        ext().flag_set(self.flags[self.nb + self.step % 2].data_ptr(), self.sdev, 0)
         self.active = False
         return self.engine.nonfinite

@@ -15,13 +15,15 @@ from __future__ import annotations
 import torch
 
 from .engine import Engine, synthetic_batch
+from .graphs import StepGraphs, graphs_enabled
 from .models.qwen_moe import MoEConfig
 
 
 class SingleRunner:
     layout = "dp1"
 
-    def __init__(self, cfg: MoEConfig, device, batch: int, seq: int, n_prefetch: int = 4):
+    def __init__(self, cfg: MoEConfig, device, batch: int, seq: int, n_prefetch: int = 4,
+                 graphs: bool | None = None):
         self.cfg = cfg
         self.engine = Engine(cfg, device)
         self.B, self.S = batch, seq
@@ -29,25 +31,39 @@ class SingleRunner:
         # device-resident inputs for the kernel-timed loop
         self.dev_batches = [synthetic_batch(cfg, i, batch, seq).to(self.device) for i in range(n_prefetch)]
         self.host = synthetic_batch(cfg, 10_000, batch, seq).pin_memory()
+        # the step reads its tokens from this buffer (static for graph replay)
+        self.tokens = torch.empty(batch, seq + 1, dtype=torch.int32, device=self.device)
+        self.graphs = StepGraphs(self.device, graphs_enabled() if graphs is None else graphs)
+        self.step_no = 0
 
-    def _train(self, data):
-        tok, lab = data[:, :-1], data[:, 1:]
+    def _device_step(self):
+        tok, lab = self.tokens[:, :-1], self.tokens[:, 1:]
         loss = self.engine.forward_backward([(tok, lab)], self.B, self.S)
-        self.engine.optimizer_step()
+        self.engine.optimizer_step(prepared=True)
+        return loss
+
+    def _train(self):
+        self.engine.prepare_step(self.step_no + 1)
+        if self.step_no < 2:      # eager warm-up steps (lazy initialisation)
+            loss = self._device_step()
+        else:
+            loss = self.graphs.run(self.engine.store.cur, self._device_step)
         self.engine.commit()
+        self.step_no += 1
         return loss
 
     def step(self, i: int):
-        return self._train(self.dev_batches[i % len(self.dev_batches)])
+        self.tokens.copy_(self.dev_batches[i % len(self.dev_batches)])
+        return self._train()
 
     def step_e2e(self, i: int):
-        data = self.host.to(self.device, non_blocking=True)
-        loss = self._train(data)
+        self.tokens.copy_(self.host, non_blocking=True)
+        loss = self._train()
         val = loss.item()
         return val, self.host.numel() * self.host.element_size(), 4
 
     def close(self):
-        pass
+        self.graphs.reset()
 
 
 def make_runner(n_gpus: int, rank: int, local_rank: int, batch: int, seq: int, cfg: MoEConfig | None = None):

@@ -13,6 +13,13 @@ from shift_b200.ops._ext import ext, status_word
 pytestmark = pytest.mark.gpu
 
 
+def _step_block(dev, tag, lr, beta1, beta2, step):
+    from shift_b200.engine import StepBlock
+    sb = StepBlock(dev)
+    sb.write(tag, lr, beta1, beta2, step)
+    return sb.dev
+
+
 def test_fused_reduce_adamw_local_sources_matches_reference():
     torch.manual_seed(0)
     n = 100_003
@@ -26,8 +33,9 @@ def test_fused_reduce_adamw_local_sources_matches_reference():
     flag = torch.zeros(1, dtype=torch.int32, device=dev)
     st = status_word(dev)
     st.zero_()
-    ext().fused_reduce_adamw([g.data_ptr() for g in gs], [], 1, master, m, v, *outs, pb, 1e-3, 0.9, 0.999, 1e-8,
-                             0.01, 5, 1 / 3, flag, st, 5.0)
+    sdev = _step_block(dev, 1, 1e-3, 0.9, 0.999, 5)
+    ext().fused_reduce_adamw([g.data_ptr() for g in gs], [], sdev, master, m, v, *outs, pb, 0.9, 0.999, 1e-8,
+                             0.01, 1 / 3, flag, st, 5.0)
     torch.cuda.synchronize()
     g = (gs[0].float() + gs[1].float() + gs[2].float()) / 3
     em, emm, ev = ref.adamw(master, m, v, g, 1e-3, 0.9, 0.999, 1e-8, 0.01, 5)
@@ -44,23 +52,27 @@ def test_flag_wait_times_out_with_status_and_context_survives():
     st = status_word(dev)
     st.zero_()
     # nothing ever sets this flag: the bounded wait must give up and report
-    ext().flag_wait([flags[0].data_ptr()], 1, st, 0.2)
+    s1 = _step_block(dev, 1, 1e-3, 0.9, 0.999, 1)
+    ext().flag_wait([flags[0].data_ptr()], s1, 0, st, 0.2)
     torch.cuda.synchronize()
     assert int(st[0]) == 2
     st.zero_()
-    ext().flag_set(flags[0].data_ptr(), 7)
-    ext().flag_wait([flags[0].data_ptr()], 7, st, 0.2)
+    s7 = _step_block(dev, 7, 1e-3, 0.9, 0.999, 1)
+    ext().flag_set(flags[0].data_ptr(), s7, 0)
+    ext().flag_wait([flags[0].data_ptr()], s7, 0, st, 0.2)
+    ext().flag_wait([flags[0].data_ptr()], s1, 6, st, 0.2)     # tag + delta
     torch.cuda.synchronize()
-    assert int(st[0]) == 0
+    assert int(st[0]) == 0 and int(flags[0]) == 7
     # K1 with an unset peer flag: records the timeout and writes nothing
     n = 4096
     master = torch.randn(n, device=dev)
     out = torch.full_like(master, 123.0)
     g = torch.randn(n, device=dev).to(torch.bfloat16)
     nf = torch.zeros(1, dtype=torch.int32, device=dev)
-    ext().fused_reduce_adamw([g.data_ptr()], [flags[1].data_ptr()], 5, master, master, master, out, out.clone(),
-                             out.clone(), torch.empty(n, device=dev, dtype=torch.bfloat16), 1e-3, 0.9, 0.999, 1e-8,
-                             0.0, 1, 1.0, nf, st, 0.2)
+    s5 = _step_block(dev, 5, 1e-3, 0.9, 0.999, 1)
+    ext().fused_reduce_adamw([g.data_ptr()], [flags[1].data_ptr()], s5, master, master, master, out, out.clone(),
+                             out.clone(), torch.empty(n, device=dev, dtype=torch.bfloat16), 0.9, 0.999, 1e-8,
+                             0.0, 1.0, nf, st, 0.2)
     torch.cuda.synchronize()
     assert int(st[0]) == 2
     assert torch.all(out == 123.0)

@@ -278,3 +278,23 @@ def test_adamw_matches_torch():
     g1[5] = float("inf")
     Fn.adamw_step(master, m, v, [g1], *outs, pb, 1e-3, 0.9, 0.999, 1e-8, 0.01, 7, 1.0, flag)
     assert int(flag) == 1
+
+
+def test_adamw_device_step_block_matches_host_scalars():
+    """The graph-replayable form (lr and bias corrections read from a device
+    block) gives the same bits as the host-scalar form."""
+    from shift_b200.engine import StepBlock
+    torch.manual_seed(13)
+    n = 65_539
+    master = torch.randn(n, device=DEV)
+    m = torch.randn(n, device=DEV).abs() * 0.01
+    v = torch.randn(n, device=DEV).abs() * 0.001
+    g1 = _bf(n)
+    a = [torch.empty_like(master) for _ in range(3)] + [torch.empty(n, device=DEV, dtype=torch.bfloat16)]
+    b = [torch.empty_like(t) for t in a]
+    Fn.adamw_step(master, m, v, [g1], *a, 3e-4, 0.9, 0.999, 1e-8, 0.01, 11, 1.0)
+    blk = StepBlock(torch.device(DEV))
+    blk.write(0, 3e-4, 0.9, 0.999, 11)
+    Fn.adamw_step(master, m, v, [g1], *b, 123.0, 0.9, 0.999, 1e-8, 0.01, 1, 1.0, step_dev=blk.dev)
+    for x, y in zip(a, b):
+        assert torch.equal(x, y)

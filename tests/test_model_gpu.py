@@ -60,3 +60,22 @@ def test_training_reduces_loss_and_is_deterministic():
     # same inputs -> bit-identical trajectory (no atomics decide any reduction order)
     assert runs[0][0] == runs[1][0]
     assert torch.equal(runs[0][1], runs[1][1])
+
+
+def test_cuda_graph_replayed_steps_bit_identical_to_eager():
+    """Steps replayed from captured CUDA graphs (one per state generation)
+    produce exactly the eager trajectory."""
+    from shift_b200.runner import SingleRunner
+    cfg = MoEConfig.tiny()
+    B, S = 2, 128
+    out = []
+    for graphs in (False, True):
+        r = SingleRunner(cfg, torch.device("cuda", 0), B, S, graphs=graphs)
+        losses = [float(r.step(i)) for i in range(7)]
+        torch.cuda.synchronize()
+        check_status()
+        out.append((losses, r.engine.store.state_tensors()["master"].clone(), r.graphs.captures))
+        r.close()
+    assert out[0][2] == 0 and out[1][2] == 2
+    assert out[0][0] == out[1][0]
+    assert torch.equal(out[0][1], out[1][1])

@@ -44,7 +44,7 @@ METRIC = "tokens/s (device-timed, max over ranks)"
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--steps", type=int, default=30)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--seq", type=int, default=SEQ)
@@ -170,7 +170,9 @@ def main():
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record()
     for i in range(args.steps):
+        torch.cuda.nvtx.range_push("step")      # lets a profiler select whole timed steps
         runner.step(args.warmup + 1 + i)
+        torch.cuda.nvtx.range_pop()
     t1.record()
     torch.cuda.synchronize()
     barrier()

@@ -110,14 +110,24 @@ def gemm_cases(T=16384):
     return cases
 
 
+_CASE = None       # substring filter on case names (--case)
+_WARMUP = 3
+
+
+def _want(name: str) -> bool:
+    return _CASE is None or _CASE in name
+
+
 def run_gemm(iters):
     pk = peaks()
     rows = []
     for name, flops, ours, lib in gemm_cases():
-        t = timeit(ours, iters)
+        if not _want(name):
+            continue
+        t = timeit(ours, iters, warmup=_WARMUP)
         row = {"case": name, "ms": round(t, 4), "tflops": round(flops / t / 1e9, 1),
                "frac_of_peak": round(flops / t / 1e9 / pk["bf16_tflops"], 3)}
-        if lib is not None:
+        if lib is not None and _CASE is None:
             tl = timeit(lib, iters)
             row["cublas_ms"] = round(tl, 4)
             row["vs_cublas"] = round(tl / t, 3)
@@ -133,8 +143,8 @@ def run_attn(iters, B=8, S=2048, Hq=16, Hkv=4, D=64):
     o, lse = Fn.attention_fwd(qkv, B, S, Hq, Hkv, D, scale)
     do = bf(T, Hq * D)
     causal_flops = 4.0 * B * Hq * S * S * D / 2
-    tf = timeit(lambda: Fn.attention_fwd(qkv, B, S, Hq, Hkv, D, scale), iters)
-    tb = timeit(lambda: Fn.attention_bwd(qkv, o, lse, do, B, S, Hq, Hkv, D, scale), iters)
+    tf = timeit(lambda: Fn.attention_fwd(qkv, B, S, Hq, Hkv, D, scale), iters, warmup=_WARMUP)
+    tb = timeit(lambda: Fn.attention_bwd(qkv, o, lse, do, B, S, Hq, Hkv, D, scale), iters, warmup=_WARMUP)
     return [{"case": f"attn.fwd B{B} S{S} {Hq}q/{Hkv}kv d{D}", "ms": round(tf, 4),
              "tflops": round(causal_flops / tf / 1e9, 1), "frac_of_peak": round(causal_flops / tf / 1e9 / pk["bf16_tflops"], 3)},
             {"case": "attn.bwd", "ms": round(tb, 4), "tflops": round(2.5 * causal_flops / tb / 1e9, 1),
@@ -180,7 +190,11 @@ def main():
     p = argparse.ArgumentParser()
     p.add_argument("--ops", default="gemm,attn,mem")
     p.add_argument("--iters", type=int, default=20)
+    p.add_argument("--case", default=None, help="only GEMM cases whose name contains this (no cuBLAS comparison)")
+    p.add_argument("--warmup", type=int, default=3)
     args = p.parse_args()
+    global _CASE, _WARMUP
+    _CASE, _WARMUP = args.case, args.warmup
     torch.manual_seed(0)
     out = {"peaks": peaks()}
     ops = args.ops.split(",")

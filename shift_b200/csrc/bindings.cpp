@@ -6,9 +6,13 @@
 namespace sb {
 namespace norm {
 std::vector<at::Tensor> rmsnorm_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& delta, const at::Tensor& w,
-                                    double eps);
+                                    double eps, const c10::optional<at::Tensor>& delta2,
+                                    const c10::optional<at::Tensor>& y_out, const std::vector<int64_t>& xchg,
+                                    const c10::optional<at::Tensor>& status);
 at::Tensor rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& rstd, const at::Tensor& w,
-                       const c10::optional<at::Tensor>& dres, at::Tensor& dw_out, bool accumulate);
+                       const c10::optional<at::Tensor>& dres, at::Tensor& dw_out, bool accumulate,
+                       const c10::optional<at::Tensor>& dy2, const c10::optional<at::Tensor>& dx_out,
+                       const std::vector<int64_t>& xchg, const c10::optional<at::Tensor>& status);
 void column_reduce(const at::Tensor& partial, at::Tensor& out, bool accumulate);
 void rope_(at::Tensor& qkv, const at::Tensor& cos_t, const at::Tensor& sin_t, int64_t S, int64_t n_rot_heads,
            int64_t head_dim, int64_t pos0, bool inverse);
@@ -18,11 +22,14 @@ std::vector<at::Tensor> router_fwd(const at::Tensor& x, const at::Tensor& wr, in
 at::Tensor router_bwd(const at::Tensor& probs, const at::Tensor& topk_idx, const at::Tensor& topk_w,
                       const at::Tensor& d_topk_w, const c10::optional<at::Tensor>& aux_grad, bool normalize);
 at::Tensor router_input_weight_grad(const at::Tensor& x, const at::Tensor& wr, const at::Tensor& dlogits,
-                                    at::Tensor& dx);
+                                    at::Tensor& dx, const std::vector<int64_t>& peer_rows,
+                                    const std::vector<int64_t>& xchg);
 std::vector<at::Tensor> bucket_sort(const at::Tensor& keys, int64_t lo, int64_t hi, int64_t pad, int64_t src_div);
 void gather_rows(const at::Tensor& src, const at::Tensor& row_src, const c10::optional<at::Tensor>& total,
                  at::Tensor& out);
-at::Tensor combine(const at::Tensor& y, const at::Tensor& pos, const at::Tensor& w, int64_t T);
+at::Tensor combine(const at::Tensor& y, const at::Tensor& pos, const at::Tensor& w, int64_t T,
+                   const c10::optional<at::Tensor>& out, const std::vector<int64_t>& split,
+                   const std::vector<int64_t>& xchg);
 std::vector<at::Tensor> combine_bwd(const at::Tensor& dout, const at::Tensor& y, const at::Tensor& pos,
                                     const at::Tensor& w, const at::Tensor& row_src, const at::Tensor& slot_of_row,
                                     const at::Tensor& total);
@@ -65,6 +72,8 @@ void reduce_slice_scatter(const std::vector<int64_t>& src_ptrs, const std::vecto
 void flag_wait(const std::vector<int64_t>& flag_ptrs, const at::Tensor& step_dev, int64_t delta,
                const at::Tensor& status, double timeout_s);
 void peer_copy(int64_t src_ptr, int64_t dst_ptr, int64_t nbytes);
+void xcopy(int64_t src_ptr, int64_t dst_ptr, int64_t nbytes, const std::vector<int64_t>& xchg,
+           const at::Tensor& status);
 std::string fingerprint(const at::Tensor& t);
 void pair_reduce_scatter(int64_t a_ptr, int64_t b_ptr, at::Tensor& out, const std::vector<int64_t>& flag_ptrs,
                          int64_t target, const at::Tensor& status, double timeout_s);
@@ -73,17 +82,29 @@ void pair_reduce_scatter(int64_t a_ptr, int64_t b_ptr, at::Tensor& out, const st
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "shift_b200 sm_100a kernels";
-  m.def("gemm", &sb::gemm::gemm, "tcgen05 GEMM (dense / grouped)");
-  m.def("rmsnorm_fwd", &sb::norm::rmsnorm_fwd);
-  m.def("rmsnorm_bwd", &sb::norm::rmsnorm_bwd);
+  m.def("gemm", &sb::gemm::gemm, "tcgen05 GEMM (dense / grouped, optional tensor-parallel exchange)",
+        py::arg("A"), py::arg("B"), py::arg("D"), py::arg("D2"), py::arg("offs"), py::arg("M"), py::arg("N"),
+        py::arg("K"), py::arg("G"), py::arg("mode"), py::arg("a_mn"), py::arg("b_mn"), py::arg("epi"),
+        py::arg("alpha"), py::arg("bn"), py::arg("status"), py::arg("max_rows_hint"),
+        py::arg("xchg") = std::vector<int64_t>{}, py::arg("tp") = std::vector<int64_t>{});
+  m.def("rmsnorm_fwd", &sb::norm::rmsnorm_fwd, py::arg("x"), py::arg("delta"), py::arg("w"), py::arg("eps"),
+        py::arg("delta2") = py::none(), py::arg("y_out") = py::none(), py::arg("xchg") = std::vector<int64_t>{},
+        py::arg("status") = py::none());
+  m.def("rmsnorm_bwd", &sb::norm::rmsnorm_bwd, py::arg("dy"), py::arg("x"), py::arg("rstd"), py::arg("w"),
+        py::arg("dres"), py::arg("dw_out"), py::arg("accumulate"), py::arg("dy2") = py::none(),
+        py::arg("dx_out") = py::none(), py::arg("xchg") = std::vector<int64_t>{}, py::arg("status") = py::none());
   m.def("column_reduce", &sb::norm::column_reduce);
   m.def("rope_", &sb::norm::rope_);
   m.def("router_fwd", &sb::moe::router_fwd);
   m.def("router_bwd", &sb::moe::router_bwd);
-  m.def("router_input_weight_grad", &sb::moe::router_input_weight_grad);
+  m.def("router_input_weight_grad", &sb::moe::router_input_weight_grad, py::arg("x"), py::arg("wr"),
+        py::arg("dlogits"), py::arg("dx"), py::arg("peer_rows") = std::vector<int64_t>{},
+        py::arg("xchg") = std::vector<int64_t>{});
   m.def("bucket_sort", &sb::moe::bucket_sort);
   m.def("gather_rows", &sb::moe::gather_rows);
-  m.def("combine", &sb::moe::combine);
+  m.def("combine", &sb::moe::combine, py::arg("y"), py::arg("pos"), py::arg("w"), py::arg("T"),
+        py::arg("out") = py::none(), py::arg("split") = std::vector<int64_t>{},
+        py::arg("xchg") = std::vector<int64_t>{});
   m.def("combine_bwd", &sb::moe::combine_bwd);
   m.def("scatter_back", &sb::moe::scatter_back);
   m.def("invert_pos", &sb::moe::invert_pos);
@@ -108,5 +129,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flag_wait", &sb::coll::flag_wait);
   m.def("peer_copy", &sb::coll::peer_copy, "K10: SM-driven peer-memory copy");
   m.def("pair_reduce_scatter", &sb::coll::pair_reduce_scatter);
+  m.def("xcopy", &sb::coll::xcopy, "copy to a local and a peer destination with TP exchange wait/signal");
   m.def("fingerprint", &sb::coll::fingerprint, "deterministic 64-bit fingerprint of a tensor's bytes");
 }

@@ -23,6 +23,7 @@
 #include <c10/cuda/CUDAGuard.h>
 
 #include "common.cuh"
+#include "xchg.h"
 
 namespace sb {
 namespace coll {
@@ -226,6 +227,23 @@ __global__ void peer_copy_kernel(const uint4* __restrict__ src, uint4* __restric
   for (long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n16; i += stride) dst[i] = src[i];
 }
 
+// Copy with tensor-parallel exchange: dst (local, optional) and xc.peer_out
+// (a peer's gather buffer, optional) both receive src; optional wait before
+// and signal after.  Used where the producer of a gathered operand is not a
+// kernel of ours (e.g. a pipeline receive).  Sizes in 16-byte units.
+__global__ void xcopy_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst, long n16, Xchg xc,
+                             int* status) {
+  if (!xchg_wait_cta(xc, status)) return;
+  uint4* peer = reinterpret_cast<uint4*>(xc.peer_out);
+  const long stride = static_cast<long>(gridDim.x) * blockDim.x;
+  for (long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n16; i += stride) {
+    const uint4 v = src[i];
+    if (dst != nullptr) dst[i] = v;
+    if (peer != nullptr) peer[i] = v;
+  }
+  xchg_signal(xc);
+}
+
 // Two-rank reduce-scatter of bf16 rows over peer memory: out = mine[half] + peer[half]
 // (fixed order: rank-0 operand first), optional flag wait on the peer.
 __global__ void pair_reduce_scatter_kernel(const __nv_bfloat16* __restrict__ a, const __nv_bfloat16* __restrict__ b,
@@ -411,6 +429,18 @@ void peer_copy(int64_t src_ptr, int64_t dst_ptr, int64_t nbytes) {
   const long blocks = std::min<long>((n16 + 255) / 256, static_cast<long>(sm_count()) * 4);
   peer_copy_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(reinterpret_cast<const uint4*>(src_ptr),
                                                                           reinterpret_cast<uint4*>(dst_ptr), n16);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// dst_ptr may be 0 (only the peer copy); see xcopy_kernel.
+void xcopy(int64_t src_ptr, int64_t dst_ptr, int64_t nbytes, const std::vector<int64_t>& xchg,
+           const at::Tensor& status) {
+  const Xchg xc = xchg_from(xchg);
+  TORCH_CHECK(nbytes % 16 == 0 && src_ptr % 16 == 0 && dst_ptr % 16 == 0, "xcopy: 16-byte aligned ranges");
+  const long n16 = nbytes / 16;
+  const long blocks = std::max<long>(1, std::min<long>((n16 + 255) / 256, static_cast<long>(sm_count()) * 2));
+  xcopy_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const uint4*>(src_ptr), reinterpret_cast<uint4*>(dst_ptr), n16, xc, status.data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

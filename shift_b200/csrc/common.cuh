@@ -289,4 +289,58 @@ SB_DEVICE bool wait_flag_ge(const volatile int* flag, int target, int* status, u
   }
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-parallel exchange hooks shared by the kernels that produce or consume
+// data another GPU of the TP group reads or writes (norms, GEMM epilogues,
+// MoE combine, push copies).  Every field is optional (null / 0 = unused).
+//   wait_flag : before touching peer-produced data, wait until
+//               *wait_flag >= sdev[0] + wait_delta (a flag the peer
+//               releases at system scope after its kernel finished)
+//   sig_flag  : after the kernel's last store, the last CTA to finish sets
+//               *sig_flag = sdev[0] + sig_delta (sig_counter counts CTAs
+//               and is reset to 0 by that CTA)
+//   peer_out  : a kernel-specific destination in a peer's memory
+// sdev is the device step block (sdev[0] = step tag), so that a replayed
+// CUDA graph signals and waits with the current step's values.
+// ---------------------------------------------------------------------------
+struct Xchg {
+  const int* wait_flag;
+  int wait_delta;
+  int* sig_flag;
+  int* sig_counter;
+  int sig_delta;
+  const int* sdev;
+  void* peer_out;
+};
+
+constexpr uint64_t kPeerWaitNs = 10ull * 1000 * 1000 * 1000;   // 10 s
+
+// Thread 0 of every CTA waits; the CTA barrier then orders every thread's
+// later loads after the acquire.  Returns false (status recorded) on timeout.
+SB_DEVICE bool xchg_wait_cta(const Xchg& x, int* status) {
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) {
+    s_ok = 1;
+    if (x.wait_flag != nullptr && !wait_flag_ge(x.wait_flag, x.sdev[0] + x.wait_delta, status, kPeerWaitNs))
+      s_ok = 0;
+  }
+  __syncthreads();
+  return s_ok != 0;
+}
+
+// Called by EVERY thread of every CTA after its last store of the kernel.
+SB_DEVICE void xchg_signal(const Xchg& x) {
+  if (x.sig_flag == nullptr) return;
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int prev = atomicAdd(x.sig_counter, 1);
+    if (prev == static_cast<int>(gridDim.x * gridDim.y * gridDim.z) - 1) {
+      atomicExch(x.sig_counter, 0);
+      __threadfence_system();
+      st_release_sys(x.sig_flag, x.sdev[0] + x.sig_delta);
+    }
+  }
+}
+
 }  // namespace sb

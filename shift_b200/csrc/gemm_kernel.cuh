@@ -39,6 +39,12 @@ struct Params {
   int ldd, ldd2;
   float alpha;
   int* status;
+  // ---- tensor-parallel exchange (all optional; see Xchg in common.cuh) ----
+  Xchg xc;           // wait before gathered rows / signal after the last store; peer_out = D_peer
+  int wait_lo, wait_hi;   // gathered index range that needs the wait: A rows (row mode) or K rows (k mode)
+  int m_rot;         // row mode, G == 1: row-tile order rotated by m_rot tiles
+  int peer_lo, peer_hi;   // output rows in [peer_lo, peer_hi) go to xc.peer_out at row - peer_lo
+  int d_row_off;     // the other output rows go to D at row - d_row_off
 };
 
 struct TileInfo {
@@ -48,6 +54,7 @@ struct TileInfo {
   int n0;            // first output column
   int m_valid;       // rows of this tile that are real
   int kb;            // number of k-blocks
+  int k0;            // first contraction index (k mode)
 };
 
 template <int BN, bool A_MN, bool B_MN>
@@ -59,13 +66,19 @@ __device__ __forceinline__ bool decode_tile(const Params& p, const int* s_prefix
     int g = 0;
     while (g + 1 < p.G && s_prefix[g + 1] <= tile) ++g;
     const int local = tile - s_prefix[g];
-    const int tm = local / tiles_n, tn = local % tiles_n;
+    int tm = local / tiles_n;
+    const int tn = local % tiles_n;
     const int seg0 = s_offs[g], seg1 = s_offs[g + 1];
+    if (p.m_rot != 0) {
+      const int tiles_m = (seg1 - seg0 + BM - 1) / BM;
+      tm = (tm + p.m_rot) % tiles_m;
+    }
     const int m0 = seg0 + tm * BM;
     t.out_row0 = m0;
     t.m_valid = min(BM, seg1 - m0);
     t.n0 = tn * BN;
     t.kb = (p.K + BK - 1) / BK;
+    t.k0 = 0;
     if (!A_MN) { t.a_x = 0; t.a_y = m0; }
     else       { t.a_x = m0; t.a_y = 0; }
     if (!B_MN) { t.b_x = 0; t.b_y = g * p.N + t.n0; }
@@ -81,6 +94,7 @@ __device__ __forceinline__ bool decode_tile(const Params& p, const int* s_prefix
     t.m_valid = min(BM, p.M - tm * BM);
     t.n0 = tn * BN;
     t.kb = (k1 - k0 + BK - 1) / BK;
+    t.k0 = k0;
     // A: MN-major [K, M] -> x = m, y = k ; K-major [M, K] -> x = k, y = m (not used for k-groups)
     if (A_MN) { t.a_x = tm * BM; t.a_y = k0; }
     else      { t.a_x = k0; t.a_y = g * p.M + tm * BM; }
@@ -166,10 +180,23 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      bool waited = (p.xc.wait_flag == nullptr);
+      // Gathered operand rows written by the TP peer: wait (bounded) for its
+      // flag before the first TMA load that reads them, then order the
+      // async-proxy loads after the acquire.
+      auto peer_wait = [&](int lo, int hi) -> bool {
+        if (waited || hi <= p.wait_lo || lo >= p.wait_hi) return true;
+        if (!wait_flag_ge(p.xc.wait_flag, p.xc.sdev[0] + p.xc.wait_delta, p.status, kPeerWaitNs)) return false;
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        waited = true;
+        return true;
+      };
       for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
         TileInfo t;
         decode_tile<BN, A_MN, B_MN>(p, s_prefix, s_offs, tile, t);
+        if (p.mode == kRowGroups && !peer_wait(t.out_row0, t.out_row0 + BM)) { ok = false; break; }
         for (int kb = 0; kb < t.kb; ++kb) {
+          if (p.mode == kKGroups && !peer_wait(t.k0 + kb * BK, t.k0 + (kb + 1) * BK)) { ok = false; break; }
           if (!mbar_wait(&empty[stage], phase ^ 1, p.status)) { ok = false; break; }
           uint8_t* sA = tiles + stage * C::kStageBytes;
           uint8_t* sB = sA + C::kABytes;
@@ -249,7 +276,11 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       if (!mbar_wait(&tmem_full[acc], acc_phase, p.status)) break;
       tc_fence_after();
       const bool row_ok = r < t.m_valid;
-      const long row = static_cast<long>(t.out_row0) + r;
+      const long grow = static_cast<long>(t.out_row0) + r;
+      // destination: the TP peer's receive buffer for its rows, D otherwise
+      const bool to_peer = p.xc.peer_out != nullptr && grow >= p.peer_lo && grow < p.peer_hi;
+      void* const Dst = to_peer ? p.xc.peer_out : p.D;
+      const long row = to_peer ? grow - p.peer_lo : grow - p.d_row_off;
       const bool empty_k = (t.kb == 0);
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
@@ -264,7 +295,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         const int ncols = min(32, p.N - col);  // N is a multiple of 32 for all callers except tails
         switch (p.epi) {
           case kEpiBF16: {
-            __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.D) + row * p.ldd + col;
+            __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(Dst) + row * p.ldd + col;
             if (ncols == 32) {
 #pragma unroll
               for (int q = 0; q < 4; ++q) reinterpret_cast<bf16x8*>(out)[q] = float_to_bf16x8(f + 8 * q);
@@ -273,7 +304,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             }
           } break;
           case kEpiF32: {
-            float* out = reinterpret_cast<float*>(p.D) + row * p.ldd + col;
+            float* out = reinterpret_cast<float*>(Dst) + row * p.ldd + col;
             if (ncols == 32) {
 #pragma unroll
               for (int q = 0; q < 8; ++q)
@@ -284,7 +315,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
           } break;
           case kEpiAccBF16: {
             if (empty_k) break;
-            __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.D) + row * p.ldd + col;
+            __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(Dst) + row * p.ldd + col;
             if (ncols == 32) {
 #pragma unroll
               for (int q = 0; q < 4; ++q) {
@@ -300,7 +331,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
           } break;
           case kEpiAccF32: {
             if (empty_k) break;
-            float* out = reinterpret_cast<float*>(p.D) + row * p.ldd + col;
+            float* out = reinterpret_cast<float*>(Dst) + row * p.ldd + col;
             if (ncols == 32) {
 #pragma unroll
               for (int q = 0; q < 8; ++q) {
@@ -314,7 +345,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
           } break;
           case kEpiSwiGLU: {
             // columns [col, col+32) hold 16 gate then 16 up values of features col/2 .. col/2+15
-            __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.D) + row * p.ldd + col;
+            __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(Dst) + row * p.ldd + col;
 #pragma unroll
             for (int q = 0; q < 4; ++q) reinterpret_cast<bf16x8*>(out)[q] = float_to_bf16x8(f + 8 * q);
             float a[16];
@@ -326,7 +357,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
               const float u = __bfloat162float(__float2bfloat16(f[16 + i]));
               a[i] = silu_f(g) * u;
             }
-            __nv_bfloat16* out2 = reinterpret_cast<__nv_bfloat16*>(p.D2) + row * p.ldd2 + col / 2;
+            __nv_bfloat16* out2 = reinterpret_cast<__nv_bfloat16*>(p.D2) + grow * p.ldd2 + col / 2;
             reinterpret_cast<bf16x8*>(out2)[0] = float_to_bf16x8(a);
             reinterpret_cast<bf16x8*>(out2)[1] = float_to_bf16x8(a + 8);
           } break;
@@ -344,6 +375,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem_base, C::kTmemCols);
+  xchg_signal(p.xc);
 }
 
 

@@ -39,6 +39,7 @@
 #include <mutex>
 
 #include "gemm_kernel.cuh"
+#include "xchg.h"
 
 namespace sb {
 namespace gemm {
@@ -99,7 +100,7 @@ int num_sms() {
 void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const c10::optional<at::Tensor>& D2,
           const c10::optional<at::Tensor>& offs, int64_t M, int64_t N, int64_t K, int64_t G, int64_t mode,
           bool a_mn, bool b_mn, int64_t epi, double alpha, int64_t bn, const at::Tensor& status,
-          int64_t max_rows_hint) {
+          int64_t max_rows_hint, const std::vector<int64_t>& xchg, const std::vector<int64_t>& tp) {
   TORCH_CHECK(A.is_cuda() && B.is_cuda() && D.is_cuda(), "gemm: CUDA tensors required");
   TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "gemm: bf16 operands");
   TORCH_CHECK(A.stride(-1) == 1 && B.stride(-1) == 1 && D.stride(-1) == 1, "gemm: inner dim must be contiguous");
@@ -134,6 +135,23 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const c10::op
   p.ldd2 = D2.has_value() ? static_cast<int>(D2->dim() >= 2 ? D2->stride(-2) : D2->size(-1)) : 0;
   p.alpha = static_cast<float>(alpha);
   p.status = status.data_ptr<int>();
+  // tensor-parallel exchange: xchg (see xchg.h; peer_out = the peer's
+  // receive buffer) and tp = [wait_lo, wait_hi, m_rot, peer_lo, peer_hi, d_row_off]
+  p.xc = xchg_from(xchg);
+  TORCH_CHECK(tp.empty() || tp.size() == 6, "gemm: tp = [wait_lo, wait_hi, m_rot, peer_lo, peer_hi, d_row_off]");
+  p.wait_lo = tp.empty() ? 0 : static_cast<int>(tp[0]);
+  p.wait_hi = tp.empty() ? 0 : static_cast<int>(tp[1]);
+  p.m_rot = tp.empty() ? 0 : static_cast<int>(tp[2]);
+  p.peer_lo = tp.empty() ? 0 : static_cast<int>(tp[3]);
+  p.peer_hi = tp.empty() ? 0 : static_cast<int>(tp[4]);
+  p.d_row_off = tp.empty() ? 0 : static_cast<int>(tp[5]);
+  if (p.m_rot != 0) TORCH_CHECK(mode == kRowGroups && G == 1 && p.m_rot > 0, "gemm: m_rot needs a dense row-mode GEMM");
+  if (p.xc.peer_out != nullptr) {
+    TORCH_CHECK(mode == kRowGroups && p.peer_lo % BM == 0 && p.peer_hi % BM == 0 && epi != kEpiSwiGLU,
+                "gemm: peer output rows must be whole 128-row tiles of a row-mode GEMM");
+  }
+  if (p.xc.wait_flag != nullptr && mode == kKGroups)
+    TORCH_CHECK(p.wait_lo % BK == 0 && p.wait_hi % BK == 0, "gemm: k-mode wait range must be 64-aligned");
 
   // Upper bound of tiles for the grid size (the kernel computes the exact count).
   const int64_t tn = (N + bn - 1) / bn;

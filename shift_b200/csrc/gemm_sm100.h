@@ -17,7 +17,7 @@ enum Epilogue : int {
 void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const c10::optional<at::Tensor>& D2,
           const c10::optional<at::Tensor>& offs, int64_t M, int64_t N, int64_t K, int64_t G, int64_t mode,
           bool a_mn, bool b_mn, int64_t epi, double alpha, int64_t bn, const at::Tensor& status,
-          int64_t max_rows_hint);
+          int64_t max_rows_hint, const std::vector<int64_t>& xchg, const std::vector<int64_t>& tp);
 
 }  // namespace gemm
 }  // namespace sb

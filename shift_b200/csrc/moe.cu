@@ -17,6 +17,7 @@
 #include <c10/cuda/CUDAGuard.h>
 
 #include "common.cuh"
+#include "xchg.h"
 
 namespace sb {
 namespace moe {
@@ -187,8 +188,13 @@ at::Tensor router_bwd(const at::Tensor& probs, const at::Tensor& topk_idx, const
 template <int NV, int E>
 __global__ void __launch_bounds__(256)
 router_dgrad_kernel(const __nv_bfloat16* __restrict__ wr, const float* __restrict__ dlogits,
-                    __nv_bfloat16* __restrict__ dx, int T) {
+                    __nv_bfloat16* __restrict__ dx, int T, int peer_lo, int peer_hi, Xchg xc) {
+  // Rows in [peer_lo, peer_hi) are finished partial sums that belong to the
+  // tensor-parallel peer: they are stored into its receive buffer
+  // (xc.peer_out, row t - peer_lo) instead of dx -- the reduce-scatter's
+  // transfer fused into the last kernel that writes them.
   constexpr int H = NV * 256;
+  __nv_bfloat16* dpeer = reinterpret_cast<__nv_bfloat16*>(xc.peer_out);
   extern __shared__ uint8_t smem[];
   bf16x8* sw = reinterpret_cast<bf16x8*>(smem);
   for (int i = threadIdx.x; i < E * H / 8; i += blockDim.x) sw[i] = reinterpret_cast<const bf16x8*>(wr)[i];
@@ -213,10 +219,13 @@ router_dgrad_kernel(const __nv_bfloat16* __restrict__ wr, const float* __restric
         for (int j = 0; j < 8; ++j) dxv[i][j] += dl * wv[j];
       }
     }
+    __nv_bfloat16* dst = (dpeer != nullptr && t >= peer_lo && t < peer_hi)
+                             ? dpeer + static_cast<long>(t - peer_lo) * H
+                             : dx + static_cast<long>(t) * H;
 #pragma unroll
-    for (int i = 0; i < NV; ++i)
-      reinterpret_cast<bf16x8*>(dx + static_cast<long>(t) * H)[i * 32 + lane] = float_to_bf16x8(dxv[i]);
+    for (int i = 0; i < NV; ++i) reinterpret_cast<bf16x8*>(dst)[i * 32 + lane] = float_to_bf16x8(dxv[i]);
   }
+  xchg_signal(xc);
 }
 
 // partial[c, e*H + h] = sum_{t in chunk c} dlogits[t, e] * x[t, h]; one block per
@@ -261,7 +270,11 @@ router_wgrad_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict
 
 // In place: dx += dlogits @ Wr ; returns partial [nchunks, E*H] for a column reduction into dWr.
 at::Tensor router_input_weight_grad(const at::Tensor& x, const at::Tensor& wr, const at::Tensor& dlogits,
-                                    at::Tensor& dx) {
+                                    at::Tensor& dx, const std::vector<int64_t>& peer_rows,
+                                    const std::vector<int64_t>& xchg) {
+  const Xchg xc = xchg_from(xchg);
+  const int peer_lo = peer_rows.size() == 2 ? static_cast<int>(peer_rows[0]) : 0;
+  const int peer_hi = peer_rows.size() == 2 ? static_cast<int>(peer_rows[1]) : 0;
   const at::cuda::CUDAGuard guard(x.device());
   const int H = static_cast<int>(x.size(-1));
   const int T = static_cast<int>(x.numel() / H);
@@ -279,7 +292,7 @@ at::Tensor router_input_weight_grad(const at::Tensor& x, const at::Tensor& wr, c
   {                                                                                                  \
     auto kern = router_dgrad_kernel<NV, EV>;                                                         \
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);                  \
-    kern<<<blocks, 256, smem, stream>>>(wp, dlogits.data_ptr<float>(), dxp, T);                      \
+    kern<<<blocks, 256, smem, stream>>>(wp, dlogits.data_ptr<float>(), dxp, T, peer_lo, peer_hi, xc); \
     if (T > 0) router_wgrad_kernel<EV><<<nchunks, 256, 0, stream>>>(xp, dlogits.data_ptr<float>(), T, H, partial.data_ptr<float>()); \
   }
   if (H == 1024 && E == 16) SB_R(4, 16)
@@ -471,8 +484,14 @@ void gather_rows(const at::Tensor& src, const at::Tensor& row_src, const c10::op
 // out[t] = sum_j w[t,j] * y[pos[t,j]]   (pos < 0 skipped);  optional residual add
 template <int NV>
 __global__ void combine_kernel(const __nv_bfloat16* __restrict__ y, const int* __restrict__ pos,
-                               const float* __restrict__ w, int T, int k, __nv_bfloat16* __restrict__ out) {
+                               const float* __restrict__ w, int T, int k, __nv_bfloat16* __restrict__ out,
+                               int peer_lo, int peer_hi, int own_off, Xchg xc) {
+  // Tensor-parallel form: token rows in [peer_lo, peer_hi) go to the peer's
+  // receive buffer (xc.peer_out, row t - peer_lo) over NVLink, the others to
+  // out at row t - own_off; then the kernel signals.  The expert combine's
+  // partial sums thus leave in the same pass that computes them.
   constexpr int H = NV * 256;
+  __nv_bfloat16* opeer = reinterpret_cast<__nv_bfloat16*>(xc.peer_out);
   const int lane = threadIdx.x % 32;
   const int warp = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int nwarps = gridDim.x * (blockDim.x / 32);
@@ -494,10 +513,13 @@ __global__ void combine_kernel(const __nv_bfloat16* __restrict__ y, const int* _
         for (int q = 0; q < 8; ++q) acc[i][q] += wj * v[q];
       }
     }
+    __nv_bfloat16* dst = (opeer != nullptr && t >= peer_lo && t < peer_hi)
+                             ? opeer + static_cast<long>(t - peer_lo) * H
+                             : out + static_cast<long>(t - own_off) * H;
 #pragma unroll
-    for (int i = 0; i < NV; ++i)
-      reinterpret_cast<bf16x8*>(out + static_cast<long>(t) * H)[i * 32 + lane] = float_to_bf16x8(acc[i]);
+    for (int i = 0; i < NV; ++i) reinterpret_cast<bf16x8*>(dst)[i * 32 + lane] = float_to_bf16x8(acc[i]);
   }
+  xchg_signal(xc);
 }
 
 // Backward of combine:
@@ -606,15 +628,27 @@ static int warp_blocks(int rows) { return std::max(1, std::min((rows + 7) / 8, 1
     default: TORCH_CHECK(false, "moe: hidden size must be 256/512/1024"); \
   }
 
-at::Tensor combine(const at::Tensor& y, const at::Tensor& pos, const at::Tensor& w, int64_t T) {
+// split (optional) = [peer_lo, peer_hi, own_off]: rows in [peer_lo, peer_hi)
+// go to xchg's peer_out, the rest to out (allocated [T - (peer_hi - peer_lo), H]
+// when not given) at row t - own_off.
+at::Tensor combine(const at::Tensor& y, const at::Tensor& pos, const at::Tensor& w, int64_t T,
+                   const c10::optional<at::Tensor>& out_opt, const std::vector<int64_t>& split,
+                   const std::vector<int64_t>& xchg) {
   const at::cuda::CUDAGuard guard(y.device());
   const int H = static_cast<int>(y.size(-1));
   const int k = static_cast<int>(pos.size(-1));
-  auto out = at::empty({T, H}, y.options());
+  const Xchg xc = xchg_from(xchg);
+  TORCH_CHECK(split.empty() || (split.size() == 3 && xc.peer_out != nullptr), "combine: split needs a peer buffer");
+  const int peer_lo = split.empty() ? 0 : static_cast<int>(split[0]);
+  const int peer_hi = split.empty() ? 0 : static_cast<int>(split[1]);
+  const int own_off = split.empty() ? 0 : static_cast<int>(split[2]);
+  const int64_t own_rows = T - (peer_hi - peer_lo);
+  at::Tensor out = out_opt.has_value() ? *out_opt : at::empty({own_rows, H}, y.options());
+  TORCH_CHECK(out.is_contiguous() && out.numel() == own_rows * H, "combine: out size");
   auto stream = at::cuda::getCurrentCUDAStream();
   auto yp = reinterpret_cast<const __nv_bfloat16*>(y.data_ptr());
   auto op = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
-#define SB_L(NV) combine_kernel<NV><<<warp_blocks((int)T), 256, 0, stream>>>(yp, pos.data_ptr<int>(), w.data_ptr<float>(), (int)T, k, op)
+#define SB_L(NV) combine_kernel<NV><<<warp_blocks((int)T), 256, 0, stream>>>(yp, pos.data_ptr<int>(), w.data_ptr<float>(), (int)T, k, op, peer_lo, peer_hi, own_off, xc)
   SB_H_DISPATCH(H, SB_L)
 #undef SB_L
   C10_CUDA_KERNEL_LAUNCH_CHECK();

@@ -11,6 +11,7 @@
 #include <c10/cuda/CUDAGuard.h>
 
 #include "common.cuh"
+#include "xchg.h"
 
 namespace sb {
 namespace norm {
@@ -18,12 +19,21 @@ namespace norm {
 constexpr int kWarps = 8;
 
 // NV = H / 256: number of 8-element vectors per lane.
+// Tensor-parallel forms: delta2 (a partial sum another GPU wrote into this
+// GPU's memory; waited for through xc) is added with delta, and y_peer (in
+// xc.peer_out) receives a second copy of y in a peer's gather buffer; the
+// kernel then signals through xc.  This fuses the sequence-parallel
+// all-gather into the norm that produces its input, and the reduce-scatter's
+// reduction into the norm that consumes it.
 template <int NV, bool kAdd>
 __global__ void __launch_bounds__(kWarps * 32)
 rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ delta,
-                   const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ h_out,
-                   __nv_bfloat16* __restrict__ y, float* __restrict__ rstd_out, int rows, float eps) {
+                   const __nv_bfloat16* __restrict__ delta2, const __nv_bfloat16* __restrict__ w,
+                   __nv_bfloat16* __restrict__ h_out, __nv_bfloat16* __restrict__ y, float* __restrict__ rstd_out,
+                   int rows, float eps, Xchg xc, int* status) {
   constexpr int H = NV * 256;
+  if (!xchg_wait_cta(xc, status)) return;
+  __nv_bfloat16* y_peer = reinterpret_cast<__nv_bfloat16*>(xc.peer_out);
   const int lane = threadIdx.x % 32;
   const int warp = blockIdx.x * kWarps + threadIdx.x / 32;
   const int nwarps = gridDim.x * kWarps;
@@ -42,6 +52,11 @@ rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __r
         bf16x8_to_float(reinterpret_cast<const bf16x8*>(delta + static_cast<long>(r) * H)[i * 32 + lane], d);
 #pragma unroll
         for (int j = 0; j < 8; ++j) v[i][j] += d[j];
+        if (delta2 != nullptr) {
+          bf16x8_to_float(reinterpret_cast<const bf16x8*>(delta2 + static_cast<long>(r) * H)[i * 32 + lane], d);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[i][j] += d[j];
+        }
         bf16x8 hv = float_to_bf16x8(v[i]);
         reinterpret_cast<bf16x8*>(h_out + static_cast<long>(r) * H)[i * 32 + lane] = hv;
         bf16x8_to_float(hv, v[i]);  // normalise the rounded residual stream
@@ -57,20 +72,28 @@ rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __r
       float o[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) o[j] = v[i][j] * rs * wv[i][j];
-      reinterpret_cast<bf16x8*>(y + static_cast<long>(r) * H)[i * 32 + lane] = float_to_bf16x8(o);
+      const bf16x8 ov = float_to_bf16x8(o);
+      reinterpret_cast<bf16x8*>(y + static_cast<long>(r) * H)[i * 32 + lane] = ov;
+      if (y_peer != nullptr) reinterpret_cast<bf16x8*>(y_peer + static_cast<long>(r) * H)[i * 32 + lane] = ov;
     }
   }
+  xchg_signal(xc);
 }
 
 // dx = rstd * (dy*w - xhat * mean(dy*w*xhat)) (+ dres);  partial dw per block.
+// Tensor-parallel forms as in the forward: dy2 (a peer-written partial,
+// waited for through xc) is added to dy, and dx is also written to
+// xc.peer_out (a peer's gather buffer), then the kernel signals.
 template <int NV, bool kRes>
 __global__ void __launch_bounds__(kWarps * 32)
-rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
-                   const float* __restrict__ rstd, const __nv_bfloat16* __restrict__ w,
-                   const __nv_bfloat16* __restrict__ dres, __nv_bfloat16* __restrict__ dx,
-                   float* __restrict__ dw_partial, int rows) {
+rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ dy2,
+                   const __nv_bfloat16* __restrict__ x, const float* __restrict__ rstd,
+                   const __nv_bfloat16* __restrict__ w, const __nv_bfloat16* __restrict__ dres,
+                   __nv_bfloat16* __restrict__ dx, float* __restrict__ dw_partial, int rows, Xchg xc, int* status) {
   constexpr int H = NV * 256;
   __shared__ float red[kWarps][H];
+  const bool go = xchg_wait_cta(xc, status);   // uniform per CTA
+  __nv_bfloat16* dx_peer = reinterpret_cast<__nv_bfloat16*>(xc.peer_out);
   const int lane = threadIdx.x % 32;
   const int wib = threadIdx.x / 32;
   const int warp = blockIdx.x * kWarps + wib;
@@ -82,7 +105,7 @@ rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __
 #pragma unroll
     for (int j = 0; j < 8; ++j) dwacc[i][j] = 0.f;
   }
-  for (int r = warp; r < rows; r += nwarps) {
+  for (int r = go ? warp : rows; r < rows; r += nwarps) {
     const float rs = rstd[r];
     float xh[NV][8], g[NV][8];
     float dot = 0.f;
@@ -91,6 +114,12 @@ rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __
       float dv[8];
       bf16x8_to_float(reinterpret_cast<const bf16x8*>(x + static_cast<long>(r) * H)[i * 32 + lane], xh[i]);
       bf16x8_to_float(reinterpret_cast<const bf16x8*>(dy + static_cast<long>(r) * H)[i * 32 + lane], dv);
+      if (dy2 != nullptr) {
+        float d2[8];
+        bf16x8_to_float(reinterpret_cast<const bf16x8*>(dy2 + static_cast<long>(r) * H)[i * 32 + lane], d2);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) dv[j] += d2[j];
+      }
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         xh[i][j] *= rs;
@@ -107,9 +136,12 @@ rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __
       if (kRes) bf16x8_to_float(reinterpret_cast<const bf16x8*>(dres + static_cast<long>(r) * H)[i * 32 + lane], rr);
 #pragma unroll
       for (int j = 0; j < 8; ++j) o[j] = rs * (g[i][j] - xh[i][j] * dot) + (kRes ? rr[j] : 0.f);
-      reinterpret_cast<bf16x8*>(dx + static_cast<long>(r) * H)[i * 32 + lane] = float_to_bf16x8(o);
+      const bf16x8 ov = float_to_bf16x8(o);
+      reinterpret_cast<bf16x8*>(dx + static_cast<long>(r) * H)[i * 32 + lane] = ov;
+      if (dx_peer != nullptr) reinterpret_cast<bf16x8*>(dx_peer + static_cast<long>(r) * H)[i * 32 + lane] = ov;
     }
   }
+  xchg_signal(xc);
 #pragma unroll
   for (int i = 0; i < NV; ++i)
 #pragma unroll
@@ -152,14 +184,32 @@ static int blocks_for(int rows) {
   }
 
 // Returns (y, rstd) ; if delta is given also h = x + delta (written to h_out).
+// Tensor-parallel options: delta2 (second partial added with delta), y_out
+// (write y there instead of a new tensor), xchg (see xchg.h; peer_out gets a
+// copy of y), status (the launch's status word).
 std::vector<at::Tensor> rmsnorm_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& delta,
-                                    const at::Tensor& w, double eps) {
+                                    const at::Tensor& w, double eps, const c10::optional<at::Tensor>& delta2,
+                                    const c10::optional<at::Tensor>& y_out, const std::vector<int64_t>& xchg,
+                                    const c10::optional<at::Tensor>& status) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous(), "rmsnorm: bf16 contiguous x");
   TORCH_CHECK(w.scalar_type() == at::kBFloat16, "rmsnorm: bf16 weight");
   const at::cuda::CUDAGuard guard(x.device());
   const int H = static_cast<int>(x.size(-1));
   const int rows = static_cast<int>(x.numel() / H);
-  auto y = at::empty_like(x);
+  at::Tensor y;
+  if (y_out.has_value()) {
+    TORCH_CHECK(y_out->is_contiguous() && y_out->numel() == x.numel() && y_out->scalar_type() == at::kBFloat16,
+                "rmsnorm: y_out must be a contiguous bf16 tensor of x's size");
+    y = *y_out;
+  } else {
+    y = at::empty_like(x);
+  }
+  const Xchg xc = xchg_from(xchg);
+  TORCH_CHECK(!delta2.has_value() || (delta.has_value() && delta2->is_contiguous() && delta2->numel() == x.numel()),
+              "rmsnorm: delta2 needs delta and x's size");
+  TORCH_CHECK(xc.wait_flag == nullptr || status.has_value(), "rmsnorm: a wait needs a status word");
+  int* st = status.has_value() ? status->data_ptr<int>() : nullptr;
+  auto d2p = delta2.has_value() ? reinterpret_cast<const __nv_bfloat16*>(delta2->data_ptr()) : nullptr;
   auto rstd = at::empty({rows}, x.options().dtype(at::kFloat));
   at::Tensor h;
   const bool add = delta.has_value();
@@ -175,8 +225,8 @@ std::vector<at::Tensor> rmsnorm_fwd(const at::Tensor& x, const c10::optional<at:
   auto hp = add ? reinterpret_cast<__nv_bfloat16*>(h.data_ptr()) : nullptr;
   auto yp = reinterpret_cast<__nv_bfloat16*>(y.data_ptr());
 #define SB_LAUNCH(NV)                                                                                       \
-  if (add) rmsnorm_fwd_kernel<NV, true><<<blocks, kWarps * 32, 0, stream>>>(xp, dp, wp, hp, yp, rstd.data_ptr<float>(), rows, (float)eps); \
-  else rmsnorm_fwd_kernel<NV, false><<<blocks, kWarps * 32, 0, stream>>>(xp, dp, wp, hp, yp, rstd.data_ptr<float>(), rows, (float)eps);
+  if (add) rmsnorm_fwd_kernel<NV, true><<<blocks, kWarps * 32, 0, stream>>>(xp, dp, d2p, wp, hp, yp, rstd.data_ptr<float>(), rows, (float)eps, xc, st); \
+  else rmsnorm_fwd_kernel<NV, false><<<blocks, kWarps * 32, 0, stream>>>(xp, dp, d2p, wp, hp, yp, rstd.data_ptr<float>(), rows, (float)eps, xc, st);
   SB_NORM_DISPATCH(H, SB_LAUNCH)
 #undef SB_LAUNCH
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -185,13 +235,29 @@ std::vector<at::Tensor> rmsnorm_fwd(const at::Tensor& x, const c10::optional<at:
 }
 
 // Returns dx; accumulates dw into dw_out (fp32 or bf16 tensor of shape [H]).
+// Tensor-parallel options as in rmsnorm_fwd: dy2 (second partial of dy),
+// dx_out, xchg (peer_out gets a copy of dx), status.
 at::Tensor rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& rstd, const at::Tensor& w,
-                       const c10::optional<at::Tensor>& dres, at::Tensor& dw_out, bool accumulate) {
+                       const c10::optional<at::Tensor>& dres, at::Tensor& dw_out, bool accumulate,
+                       const c10::optional<at::Tensor>& dy2, const c10::optional<at::Tensor>& dx_out,
+                       const std::vector<int64_t>& xchg, const c10::optional<at::Tensor>& status) {
   TORCH_CHECK(dy.is_contiguous() && x.is_contiguous(), "rmsnorm_bwd: contiguous inputs");
   const at::cuda::CUDAGuard guard(x.device());
   const int H = static_cast<int>(x.size(-1));
   const int rows = static_cast<int>(x.numel() / H);
-  auto dx = at::empty_like(x);
+  at::Tensor dx;
+  if (dx_out.has_value()) {
+    TORCH_CHECK(dx_out->is_contiguous() && dx_out->numel() == x.numel() && dx_out->scalar_type() == at::kBFloat16,
+                "rmsnorm_bwd: dx_out must be a contiguous bf16 tensor of x's size");
+    dx = *dx_out;
+  } else {
+    dx = at::empty_like(x);
+  }
+  const Xchg xc = xchg_from(xchg);
+  TORCH_CHECK(!dy2.has_value() || (dy2->is_contiguous() && dy2->numel() == x.numel()), "rmsnorm_bwd: dy2 size");
+  TORCH_CHECK(xc.wait_flag == nullptr || status.has_value(), "rmsnorm_bwd: a wait needs a status word");
+  int* st = status.has_value() ? status->data_ptr<int>() : nullptr;
+  auto dy2p = dy2.has_value() ? reinterpret_cast<const __nv_bfloat16*>(dy2->data_ptr()) : nullptr;
   const int blocks = blocks_for(rows);
   auto partial = at::empty({blocks, H}, x.options().dtype(at::kFloat));
   auto stream = at::cuda::getCurrentCUDAStream();
@@ -202,8 +268,8 @@ at::Tensor rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tens
   auto rp = res ? reinterpret_cast<const __nv_bfloat16*>(dres->data_ptr()) : nullptr;
   auto dxp = reinterpret_cast<__nv_bfloat16*>(dx.data_ptr());
 #define SB_LAUNCH(NV)                                                                                       \
-  if (res) rmsnorm_bwd_kernel<NV, true><<<blocks, kWarps * 32, 0, stream>>>(dyp, xp, rstd.data_ptr<float>(), wp, rp, dxp, partial.data_ptr<float>(), rows); \
-  else rmsnorm_bwd_kernel<NV, false><<<blocks, kWarps * 32, 0, stream>>>(dyp, xp, rstd.data_ptr<float>(), wp, rp, dxp, partial.data_ptr<float>(), rows);
+  if (res) rmsnorm_bwd_kernel<NV, true><<<blocks, kWarps * 32, 0, stream>>>(dyp, dy2p, xp, rstd.data_ptr<float>(), wp, rp, dxp, partial.data_ptr<float>(), rows, xc, st); \
+  else rmsnorm_bwd_kernel<NV, false><<<blocks, kWarps * 32, 0, stream>>>(dyp, dy2p, xp, rstd.data_ptr<float>(), wp, rp, dxp, partial.data_ptr<float>(), rows, xc, st);
   SB_NORM_DISPATCH(H, SB_LAUNCH)
 #undef SB_LAUNCH
   C10_CUDA_KERNEL_LAUNCH_CHECK();

@@ -162,12 +162,25 @@ class QwenMoE:
             delta = None
         else:
             resid, delta = hidden[0], hidden[1]
+        fused = self._fused_tp()
+        pend = None      # (peer-written partial of delta, the layer whose flag covers it)
         for i in self.layers:
-            resid, delta, ctx = self._layer_fwd(i, resid, delta, B, S)
+            if fused:
+                resid, delta, pend, ctx = self._layer_fwd_peer(i, resid, delta, pend, B, S)
+            else:
+                resid, delta, ctx = self._layer_fwd(i, resid, delta, B, S)
             saved["layers"].append(ctx)
+        if pend is not None and not self.part.has_head:
+            self.tp.wait("rMoe", pend[1])          # the next stage needs delta in one tensor
+            delta = delta + pend[0]
+            pend = None
         loss_sum = None
         if self.part.has_head:
-            y, rstd, h = Fn.rmsnorm_fwd(resid, st.w("norm.weight"), cfg.eps, delta)
+            if pend is not None:
+                y, rstd, h = Fn.rmsnorm_fwd(resid, st.w("norm.weight"), cfg.eps, delta, delta2=pend[0],
+                                            xchg=self.tp.xchg(wait=("rMoe", pend[1])))
+            else:
+                y, rstd, h = Fn.rmsnorm_fwd(resid, st.w("norm.weight"), cfg.eps, delta)
             logits = G.linear_fwd(y, st.w("lm_head.weight"))
             lab = labels.reshape(-1).to(torch.int32)
             if self.tp is not None:
@@ -206,7 +219,89 @@ class QwenMoE:
         ctx = dict(h=h, rstd1=rstd1, a_in=a_in, qkv=qkv, o=o, lse=lse, h2=h2, rstd2=rstd2, m_in=m_in, **mctx)
         return h2, moe_out, ctx
 
-    def _moe_fwd(self, p, x, T):
+    # ------------------------------------------------------------------ fused tensor parallel
+    def _fused_tp(self) -> bool:
+        return self.tp is not None and getattr(self.tp, "fused", False)
+
+    def _layer_fwd_peer(self, i, resid, delta, pend, B, S):
+        """One layer with the TP exchanges inside our kernels (see
+        parallel.tp.TPPeer).  resid/delta/outputs are this rank's token rows;
+        ``pend`` is (peer partial of delta, layer of its flag) or None."""
+        cfg, st, tp = self.cfg, self.store, self.tp
+        p = f"layers.{i}."
+        Hq, Hkv, D = self.hq, self.hkv, cfg.head_dim
+        T = B * S
+        own = tp.own()
+        plo, phi = tp.peer_range()
+        gA, gM = tp.buf("gA", i), tp.buf("gM", i)
+        # ln1 (+ the previous layer's reduce-scatter) -> both gather buffers
+        _, rstd1, h = Fn.rmsnorm_fwd(resid, st.w(p + "ln1.weight"), cfg.eps, delta,
+                                     delta2=None if pend is None else pend[0], y_out=gA[own],
+                                     xchg=tp.xchg(wait=None if pend is None else ("rMoe", pend[1]), sig=("gA", i),
+                                                  peer_out=tp.pbuf("gA", i)[own]))
+        # column-parallel QKV: own rows first, the peer's after its flag
+        qkv = G.linear_fwd(gA, st.w(p + "attn.qkv"), xchg=tp.xchg(wait=("gA", i)),
+                           tp=(plo, phi, tp.rot_own_first(), 0, 0, 0))
+        Fn.rope_(qkv, self.cos, self.sin, S, Hq + Hkv, D)
+        o, lse = Fn.attention_fwd(qkv, B, S, Hq, Hkv, D, self.scale)
+        # row-parallel output projection: the peer's rows go straight to it
+        attn_own = torch.empty(T // 2, cfg.hidden, dtype=o.dtype, device=o.device)
+        G.linear_fwd(o, st.w(p + "attn.o"), out=attn_own,
+                     xchg=tp.xchg(sig=("rAttn", i), peer_out=tp.pbuf("rAttn", i)),
+                     tp=(0, 0, tp.rot_peer_first(), plo, phi, own.start))
+        _, rstd2, h2 = Fn.rmsnorm_fwd(h, st.w(p + "ln2.weight"), cfg.eps, attn_own, delta2=tp.buf("rAttn", i),
+                                      y_out=gM[own], xchg=tp.xchg(wait=("rAttn", i), sig=("gM", i),
+                                                                  peer_out=tp.pbuf("gM", i)[own]))
+        tp.wait("gM", i)
+        moe_own = torch.empty(T // 2, cfg.hidden, dtype=o.dtype, device=o.device)
+        _, mctx = self._moe_fwd(p, gM, T, combine_out=moe_own, split=(plo, phi, own.start),
+                                xchg=tp.xchg(sig=("rMoe", i), peer_out=tp.pbuf("rMoe", i)))
+        ctx = dict(h=h, rstd1=rstd1, a_in=gA, qkv=qkv, o=o, lse=lse, h2=h2, rstd2=rstd2, m_in=gM, **mctx)
+        return h2, moe_own, (tp.buf("rMoe", i), i), ctx
+
+    def _layer_bwd_peer(self, i, c, B, S, accumulate):
+        """Backward of _layer_fwd_peer.  The gradient w.r.t. the layer output
+        is already in gather buffer gD of layer i (own rows written by our
+        producer, the peer's by the peer).  Returns dh (own rows), written
+        into gD of layer i-1 (both ranks) when that layer is in this stage."""
+        cfg, st, tp = self.cfg, self.store, self.tp
+        p = f"layers.{i}."
+        Hq, Hkv, D = self.hq, self.hkv, cfg.head_dim
+        T = B * S
+        own = tp.own()
+        plo, phi = tp.peer_range()
+        gD, gH = tp.buf("gD", i), tp.buf("gH", i)
+        dout_own = gD[own]
+        # ---- MoE: every token's gradient, then the partial dx of the peer's rows goes to it
+        tp.wait("gD", i)
+        dx = self._moe_bwd(p, c, gD, T, accumulate, peer_rows=(plo, phi),
+                           xchg=tp.xchg(sig=("rDm", i), peer_out=tp.pbuf("rDm", i)))
+        dh2 = Fn.rmsnorm_bwd(dx[own], c["h2"], c["rstd2"], st.w(p + "ln2.weight"), cfg.eps, st.g(p + "ln2.weight"),
+                             dout_own, accumulate, dy2=tp.buf("rDm", i), dx_out=gH[own],
+                             xchg=tp.xchg(wait=("rDm", i), sig=("gH", i), peer_out=tp.pbuf("gH", i)[own]))
+        # ---- attention: the gathered dh2 feeds both GEMMs (each waits in-kernel)
+        G.linear_wgrad(gH, c["o"], st.g(p + "attn.o"), accumulate, xchg=tp.xchg(wait=("gH", i)),
+                       tp=(plo, phi, 0, 0, 0, 0))
+        d_o = G.linear_dgrad(gH, st.w(p + "attn.o"), xchg=tp.xchg(wait=("gH", i)),
+                             tp=(plo, phi, tp.rot_own_first(), 0, 0, 0))
+        dqkv = Fn.attention_bwd(c["qkv"], c["o"], c["lse"], d_o, B, S, Hq, Hkv, D, self.scale)
+        Fn.rope_(dqkv, self.cos, self.sin, S, Hq + Hkv, D, inverse=True)
+        G.linear_wgrad(dqkv, c["a_in"], st.g(p + "attn.qkv"), accumulate)
+        da_own = torch.empty(T // 2, cfg.hidden, dtype=dqkv.dtype, device=dqkv.device)
+        G.linear_dgrad(dqkv, st.w(p + "attn.qkv"), out=da_own,
+                       xchg=tp.xchg(sig=("rDa", i), peer_out=tp.pbuf("rDa", i)),
+                       tp=(0, 0, tp.rot_peer_first(), plo, phi, own.start))
+        if i - 1 >= self.part.layer_lo:
+            dnext = tp.buf("gD", i - 1)[own]
+            xc = tp.xchg(wait=("rDa", i), sig=("gD", i - 1), peer_out=tp.pbuf("gD", i - 1)[own])
+        else:
+            dnext = None
+            xc = tp.xchg(wait=("rDa", i))
+        dh = Fn.rmsnorm_bwd(da_own, c["h"], c["rstd1"], st.w(p + "ln1.weight"), cfg.eps, st.g(p + "ln1.weight"),
+                            dh2, accumulate, dy2=tp.buf("rDa", i), dx_out=dnext, xchg=xc)
+        return dh
+
+    def _moe_fwd(self, p, x, T, combine_out=None, split=(), xchg=()):
         cfg, st = self.cfg, self.store
         probs, idx, w = Fn.router_fwd(x, st.w(p + "mlp.router"), cfg.top_k, cfg.norm_topk)
         e_n = self.e_hi - self.e_lo
@@ -217,7 +312,7 @@ class QwenMoE:
         hgu, act = G.grouped_fwd(xp, st.w(p + "mlp.w1"), offs, swiglu=True)
         y = G.grouped_fwd(act, st.w(p + "mlp.w2"), offs)
         pos2 = pos.view(T, cfg.top_k)
-        out = Fn.combine(y, pos2, w, T)
+        out = Fn.combine(y, pos2, w, T, combine_out, split, xchg)
         ctx = dict(probs=probs, idx=idx, w=w, pos=pos2, offs=offs, counts=counts, row_src=row_src, total=total,
                    xp=xp, hgu=hgu, act=act, y=y)
         return out, ctx
@@ -236,14 +331,30 @@ class QwenMoE:
             y = saved["final_y"]
             G.linear_wgrad(dlogits, y, st.g("lm_head.weight"), accumulate)
             dy = G.linear_dgrad(dlogits, st.w("lm_head.weight"))
-            dres = Fn.rmsnorm_bwd(dy, saved["final_h"], saved["final_rstd"], st.w("norm.weight"), cfg.eps,
-                                  st.g("norm.weight"), None, accumulate)
+            fused = self._fused_tp() and len(saved["layers"]) > 0
+            if fused:
+                # the layer below needs this gradient for every token: write it
+                # into both gather buffers of its exchange
+                top = self.layer_hi - 1
+                own = self.tp.own()
+                dres = Fn.rmsnorm_bwd(dy, saved["final_h"], saved["final_rstd"], st.w("norm.weight"), cfg.eps,
+                                      st.g("norm.weight"), None, accumulate,
+                                      dx_out=self.tp.buf("gD", top)[own],
+                                      xchg=self.tp.xchg(sig=("gD", top), peer_out=self.tp.pbuf("gD", top)[own]))
+            else:
+                dres = Fn.rmsnorm_bwd(dy, saved["final_h"], saved["final_rstd"], st.w("norm.weight"), cfg.eps,
+                                      st.g("norm.weight"), None, accumulate)
             self._hook(-1)
         else:
             dres = d_hidden
+            if self._fused_tp() and len(saved["layers"]) > 0:
+                self.tp.push(dres, "gD", self.layer_hi - 1)
         for idx_l in reversed(range(len(saved["layers"]))):
             i = self.part.layer_lo + idx_l
-            dres = self._layer_bwd(i, saved["layers"][idx_l], dres, B, S, accumulate)
+            if self._fused_tp():
+                dres = self._layer_bwd_peer(i, saved["layers"][idx_l], B, S, accumulate)
+            else:
+                dres = self._layer_bwd(i, saved["layers"][idx_l], dres, B, S, accumulate)
             self._hook(i)
         if self.part.has_embed:
             tok = saved["tokens"]
@@ -288,7 +399,7 @@ class QwenMoE:
                             accumulate)
         return dh
 
-    def _moe_bwd(self, p, c, dout, T, accumulate):
+    def _moe_bwd(self, p, c, dout, T, accumulate, peer_rows=(), xchg=()):
         cfg, st = self.cfg, self.store
         cap = c["row_src"].shape[0]
         slot_of_row = Fn.invert_pos(c["pos"], cap)
@@ -308,11 +419,13 @@ class QwenMoE:
             if self.e_hi - self.e_lo == cfg.experts:
                 counts = c["counts"].float()
             else:
-                counts = torch.bincount(c["idx"].reshape(-1).long(), minlength=cfg.experts).float()
+                ids = c["idx"].reshape(-1).long()
+                counts = torch.zeros(cfg.experts, dtype=torch.float32, device=ids.device)
+                counts.scatter_add_(0, ids, torch.ones_like(ids, dtype=torch.float32))   # exact (integers)
             f = counts / float(T * cfg.top_k)
             aux_grad = (f * (cfg.aux_coef * cfg.experts / float(T))).contiguous()
         Fn.router_bwd(c["m_in"], st.w(p + "mlp.router"), c["probs"], c["idx"], c["w"], dw_topk.contiguous(),
-                      aux_grad, cfg.norm_topk, dx, st.g(p + "mlp.router"), accumulate)
+                      aux_grad, cfg.norm_topk, dx, st.g(p + "mlp.router"), accumulate, peer_rows, xchg)
         return dx
 
     def clear(self):

@@ -13,23 +13,51 @@ from ._ext import ext, status_word
 
 
 # ----------------------------------------------------------------------------- RMSNorm
-def rmsnorm_fwd(x, w, eps, delta=None):
-    """Returns (y, rstd, h) where h = x + delta (or x when delta is None)."""
+def rmsnorm_fwd(x, w, eps, delta=None, delta2=None, y_out=None, xchg=()):
+    """Returns (y, rstd, h) where h = x + delta (+ delta2) (or x when delta
+    is None).  ``delta2``/``y_out``/``xchg``: tensor-parallel forms (CUDA)."""
     if x.is_cuda:
-        r = ext().rmsnorm_fwd(x, delta, w, eps)
+        r = ext().rmsnorm_fwd(x, delta, w, eps, delta2, y_out, list(xchg),
+                              status_word(x.device) if xchg else None)
         if delta is None:
             return r[0], r[1], x
         return r[0], r[1], r[2]
+    _before(xchg)
     h = x if delta is None else (x.float() + delta.float()).to(x.dtype)
+    if delta2 is not None:
+        h = (x.float() + delta.float() + delta2.float()).to(x.dtype)
     hf = h.float()
     rstd = torch.rsqrt(hf.pow(2).mean(-1) + eps)
-    return ref.rmsnorm(h, w, eps), rstd, h
+    y = ref.rmsnorm(h, w, eps)
+    if y_out is not None:
+        y = y_out.copy_(y)
+    _after(xchg, y)
+    return y, rstd, h
 
 
-def rmsnorm_bwd(dy, h, rstd, w, eps, dw_out, dres=None, accumulate=False):
-    """dx = d(norm)/dh + dres;  dw_out (+)= dw."""
+def _before(xchg):
+    """CPU stand-ins of the kernels' tensor-parallel exchange hooks."""
+    if xchg and hasattr(xchg, "before"):
+        xchg.before()
+
+
+def _after(xchg, peer_rows=None):
+    if xchg and hasattr(xchg, "after"):
+        if peer_rows is not None and xchg.peer_out is not None:
+            xchg.peer_out.copy_(peer_rows)
+        xchg.after()
+
+
+def rmsnorm_bwd(dy, h, rstd, w, eps, dw_out, dres=None, accumulate=False, dy2=None, dx_out=None, xchg=()):
+    """dx = d(norm)/dh + dres;  dw_out (+)= dw.  ``dy2``: a second partial of
+    dy (tensor-parallel reduce-scatter fused in); ``dx_out``/``xchg``: write
+    dx there and copy it into a peer's gather buffer, then signal."""
     if dy.is_cuda:
-        return ext().rmsnorm_bwd(dy, h, rstd, w, dres, dw_out, accumulate)
+        return ext().rmsnorm_bwd(dy, h, rstd, w, dres, dw_out, accumulate, dy2, dx_out, list(xchg),
+                                 status_word(h.device) if xchg else None)
+    _before(xchg)
+    if dy2 is not None:
+        dy = (dy.float() + dy2.float()).to(dy.dtype)
     dh, dw = ref.grad_of(lambda a, b: ref.rmsnorm(a, b, eps), [h, w], dy)
     if dres is not None:
         dh = dh + dres
@@ -37,7 +65,11 @@ def rmsnorm_bwd(dy, h, rstd, w, eps, dw_out, dres=None, accumulate=False):
         dw_out.add_(dw.to(dw_out.dtype))
     else:
         dw_out.copy_(dw)
-    return dh.to(dy.dtype)
+    dh = dh.to(dy.dtype)
+    if dx_out is not None:
+        dh = dx_out.copy_(dh)
+    _after(xchg, dh)
+    return dh
 
 
 # ----------------------------------------------------------------------------- RoPE
@@ -89,13 +121,24 @@ def router_fwd(x, wr, k, normalize):
     return ref.router(x, wr, k, normalize)
 
 
-def router_bwd(x, wr, probs, idx, w, dw_topk, aux_grad, normalize, dx, dwr_out, accumulate=False):
-    """dx += d(router)/dx (in place); dwr_out (+)= dWr."""
+def router_bwd(x, wr, probs, idx, w, dw_topk, aux_grad, normalize, dx, dwr_out, accumulate=False,
+               peer_rows=(), xchg=()):
+    """dx += d(router)/dx (in place); dwr_out (+)= dWr.  ``peer_rows`` /
+    ``xchg`` (CUDA): rows [lo, hi) of the finished dx are stored into the
+    tensor-parallel peer's receive buffer instead, then the kernel signals."""
     if x.is_cuda:
         dl = ext().router_bwd(probs, idx, w, dw_topk, aux_grad, normalize)
-        partial = ext().router_input_weight_grad(x, wr, dl, dx)
+        partial = ext().router_input_weight_grad(x, wr, dl, dx, list(peer_rows), list(xchg))
         ext().column_reduce(partial, dwr_out.view(-1), accumulate)
         return dx
+    _router_bwd_cpu(x, wr, idx, dw_topk, aux_grad, normalize, dx, dwr_out, accumulate)
+    if xchg:
+        lo, hi = peer_rows
+        _after(xchg, dx[lo:hi])
+    return dx
+
+
+def _router_bwd_cpu(x, wr, idx, dw_topk, aux_grad, normalize, dx, dwr_out, accumulate):
     E = wr.shape[0]
 
     def f(xx, ww):
@@ -156,16 +199,27 @@ def gather_rows(src, row_src, total, cap):
     return out
 
 
-def combine(y, pos, w, T):
+def combine(y, pos, w, T, out=None, split=(), xchg=()):
+    """Weighted sum of each token's expert rows.  ``split`` = (peer_lo,
+    peer_hi, own_off) with ``xchg`` (CUDA): token rows [peer_lo, peer_hi) go
+    to the tensor-parallel peer's receive buffer, the rest to ``out``."""
     if y.is_cuda:
-        return ext().combine(y, pos, w, T)
-    out = torch.zeros(T, y.shape[1], dtype=torch.float32)
+        return ext().combine(y, pos, w, T, out, list(split), list(xchg))
+    full = torch.zeros(T, y.shape[1], dtype=torch.float32)
     k = pos.shape[1]
     for j in range(k):
         p = pos[:, j].long()
         ok = p >= 0
-        out[ok] += w[ok, j:j + 1].float() * y[p[ok]].float()
-    return out.to(y.dtype)
+        full[ok] += w[ok, j:j + 1].float() * y[p[ok]].float()
+    full = full.to(y.dtype)
+    if not split:
+        return full
+    lo, hi, own_off = split
+    keep = torch.ones(T, dtype=torch.bool)
+    keep[lo:hi] = False
+    out.copy_(full[keep])
+    _after(xchg, full[lo:hi])
+    return out
 
 
 def combine_bwd(dout, y, pos, w, row_src, slot_of_row, total):

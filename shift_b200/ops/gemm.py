@@ -35,40 +35,71 @@ def pick_bn(n: int) -> int:
     return best
 
 
-def _run(A, B, D, D2, offs, M, N, K, G, mode, a_mn, b_mn, epi, alpha, max_rows):
+def _run(A, B, D, D2, offs, M, N, K, G, mode, a_mn, b_mn, epi, alpha, max_rows, xchg=(), tp=()):
     ext().gemm(A, B, D, D2, offs, M, N, K, G, mode, a_mn, b_mn, epi, float(alpha), pick_bn(N),
-               status_word(A.device), max_rows)
+               status_word(A.device), max_rows, list(xchg), list(tp))
 
 
-def linear_fwd(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+def _cpu_split(y_full, out, xchg, tp, dtype):
+    """CPU stand-in of the kernel's tensor-parallel forms: wait, peer-owned
+    output rows to the peer, own rows to ``out``, signal."""
+    if xchg and hasattr(xchg, "before"):
+        xchg.before()
+    if tp and tp[4] > tp[3] and xchg and xchg.peer_out is not None:
+        plo, phi, off = tp[3], tp[4], tp[5]
+        xchg.peer_out.copy_(y_full[plo:phi])
+        keep = torch.ones(y_full.shape[0], dtype=torch.bool)
+        keep[plo:phi] = False
+        own = y_full[keep]
+        del off
+    else:
+        own = y_full
+    res = own.to(dtype) if out is None else out.copy_(own)
+    if xchg and hasattr(xchg, "after"):
+        xchg.after()
+    return res
+
+
+def linear_fwd(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, xchg=(), tp=()) -> torch.Tensor:
+    """``xchg`` / ``tp``: tensor-parallel exchange of the kernel (see
+    ``parallel.tp.TPPeer``): a wait on the peer's flag before gathered rows,
+    a rotated row-tile order, peer-owned output rows stored into the peer's
+    receive buffer (``out`` then holds only this rank's rows) and a signal."""
     M, K = x.shape
     N = w.shape[0]
     if not x.is_cuda:
-        y = x.float() @ w.float().t()
-        return y.to(x.dtype) if out is None else out.copy_(y)
+        if xchg and hasattr(xchg, "before"):
+            xchg.before()           # gathered rows must be complete before reading x
+            xchg = type(xchg)(None, xchg.sig_ev, xchg.peer_out)
+        return _cpu_split(x.float() @ w.float().t(), out, xchg, tp, x.dtype)
     if out is None:
         out = torch.empty(M, N, dtype=x.dtype, device=x.device)
-    _run(x, w, out, None, None, M, N, K, 1, ROW_GROUPS, False, False, EPI_BF16, 1.0, M)
+    _run(x, w, out, None, None, M, N, K, 1, ROW_GROUPS, False, False, EPI_BF16, 1.0, M, xchg, tp)
     return out
 
 
-def linear_dgrad(dy: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+def linear_dgrad(dy: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, xchg=(), tp=()) -> torch.Tensor:
     M, N = dy.shape
     K = w.shape[1]
     if not dy.is_cuda:
-        d = dy.float() @ w.float()
-        return d.to(dy.dtype) if out is None else out.copy_(d)
+        if xchg and hasattr(xchg, "before"):
+            xchg.before()
+            xchg = type(xchg)(None, xchg.sig_ev, xchg.peer_out)
+        return _cpu_split(dy.float() @ w.float(), out, xchg, tp, dy.dtype)
     if out is None:
         out = torch.empty(M, K, dtype=dy.dtype, device=dy.device)
-    _run(dy, w, out, None, None, M, K, N, 1, ROW_GROUPS, False, True, EPI_BF16, 1.0, M)
+    _run(dy, w, out, None, None, M, K, N, 1, ROW_GROUPS, False, True, EPI_BF16, 1.0, M, xchg, tp)
     return out
 
 
-def linear_wgrad(dy: torch.Tensor, x: torch.Tensor, dw: torch.Tensor, accumulate: bool = False) -> torch.Tensor:
+def linear_wgrad(dy: torch.Tensor, x: torch.Tensor, dw: torch.Tensor, accumulate: bool = False, xchg=(),
+                 tp=()) -> torch.Tensor:
     """dw[N,K] = dy^T x (or +=).  dw may be bf16 or fp32."""
     M, N = dy.shape
     K = x.shape[1]
     if not dy.is_cuda:
+        if xchg and hasattr(xchg, "before"):
+            xchg.before()
         g = dy.float().t() @ x.float()
         if accumulate:
             dw.add_(g.to(dw.dtype))
@@ -79,7 +110,7 @@ def linear_wgrad(dy: torch.Tensor, x: torch.Tensor, dw: torch.Tensor, accumulate
         epi = EPI_ACC_F32 if accumulate else EPI_F32
     else:
         epi = EPI_ACC_BF16 if accumulate else EPI_BF16
-    _run(dy, x, dw, None, None, N, K, M, 1, K_GROUPS, True, True, epi, 1.0, N)
+    _run(dy, x, dw, None, None, N, K, M, 1, K_GROUPS, True, True, epi, 1.0, N, xchg, tp)
     return dw
 
 

@@ -112,7 +112,10 @@ def adamw(master, m, v, grad, lr, beta1, beta2, eps, wd, step):
 
 def grad_of(fn, inputs, grad_out):
     """Gradients of fn(*inputs) w.r.t. the floating inputs, via autograd."""
-    leaves = [t.detach().requires_grad_(t.is_floating_point()) if isinstance(t, torch.Tensor) else t for t in inputs]
+    # cloned: an input may be a view of a buffer another rank's thread writes
+    # into meanwhile (tensor-parallel emulation), which autograd would reject
+    leaves = [t.detach().clone().requires_grad_(t.is_floating_point()) if isinstance(t, torch.Tensor) else t
+              for t in inputs]
     with torch.enable_grad():
         out = fn(*leaves)
     diff = [t for t in leaves if isinstance(t, torch.Tensor) and t.requires_grad]

@@ -12,6 +12,7 @@ over replicas inside the same kernel.
 """
 from __future__ import annotations
 
+import os
 import zlib
 
 import torch
@@ -22,7 +23,7 @@ from ..models.qwen_moe import TP_SHARDED, MoEConfig, Partition, param_specs
 from ..ops._ext import check_status
 from .replicas import _order
 from .symmetric import CrossReplicaFused, SymmetricHeap
-from .tp import TPComm
+from .tp import TPComm, TPPeer
 
 
 def _is_sharded(name: str) -> bool:
@@ -31,7 +32,10 @@ def _is_sharded(name: str) -> bool:
 
 class ModelParallelRunner:
     def __init__(self, cfg: MoEConfig, n_gpus: int, rank: int, local_rank: int, batch: int, seq: int,
-                 replicas: int, tp: int, pp: int, microbatch: int = 1):
+                 replicas: int, tp: int, pp: int, microbatch: int | None = None, tp_backend: str | None = None):
+        if microbatch is None:
+            # one microbatch per replica without pipelining; 1F1B over single sequences with it
+            microbatch = batch // replicas if pp == 1 else 1
         if replicas * tp * pp != n_gpus:
             raise ValueError(f"{replicas} x tp{tp} x pp{pp} != {n_gpus} GPUs")
         if batch % (replicas * microbatch):
@@ -77,15 +81,26 @@ class ModelParallelRunner:
             salt = f"/tp{t_rank}" if _is_sharded(spec.name) else ""
             return 2026 + zlib.crc32((spec.name + salt).encode())
 
-        self.comm = TPComm(self.tp_group, self.t, tp, self.device)
+        store = dist.distributed_c10d._get_default_store()
+        self.heap = SymmetricHeap(store, f"r{self.r}s{self.s}t{self.t}", self.device)
+        self.tp_backend = tp_backend or os.environ.get("SHIFT_TP_BACKEND", "peer")
+        if self.tp_backend == "peer" and tp == 2:
+            # activations cross the TP pair inside our kernels (symmetric memory)
+            self.comm = TPPeer(self.tp_group, self.t, tp, self.device, self.heap, f"r{self.r}s{self.s}t{1 - self.t}",
+                               tokens=microbatch * seq, hidden=cfg.hidden, layers=range(part.layer_lo, part.layer_hi),
+                               microbatches=self.M)
+        else:
+            self.tp_backend = "nccl"
+            self.comm = TPComm(self.tp_group, self.t, tp, self.device)
+        self.layout += f", TP over {'peer memory (fused kernels)' if self.tp_backend == 'peer' else 'NCCL'}"
         self.engine = Engine(cfg, self.device, part=part, specs=rep + shard, seed_of=seed_of, tp=self.comm)
         st = self.engine.store
         self.rep_end = st.offsets[shard[0].name][0] if shard else st.numel
         # ---- fused cross-replica (and cross-TP for replicated params) reduction ----
-        store = dist.distributed_c10d._get_default_store()
-        self.heap = SymmetricHeap(store, f"r{self.r}s{self.s}t{self.t}", self.device)
         self.fused = CrossReplicaFused(self.engine, self.heap)
         dist.barrier()
+        if isinstance(self.comm, TPPeer):
+            self.comm.connect(self.engine.step_block.dev)
         rep_src = [f"r{r}s{self.s}t{t}" for r in range(replicas) for t in range(tp)]
         shard_src = [f"r{r}s{self.s}t{self.t}" for r in range(replicas)]
         owners = sorted(set(rep_src) | set(shard_src))
@@ -119,7 +134,12 @@ class ModelParallelRunner:
         return (2, self.tok_loc, self.cfg.hidden)
 
     # ------------------------------------------------------------------ one step (1F1B)
+    def _slot(self, i):
+        if isinstance(self.comm, TPPeer):
+            self.comm.set_slot(i, self.step_no % 2)
+
     def _fwd(self, i, data, hidden):
+        self._slot(i)
         model = self.engine.model
         tok = data[i * self.mb:(i + 1) * self.mb]
         out, loss = model.forward(tok[:, :-1] if self.s == 0 else None,
@@ -131,6 +151,7 @@ class ModelParallelRunner:
         return None if out is None else torch.stack([out[0], out[1]])
 
     def _bwd(self, i, dout):
+        self._slot(i)
         model = self.engine.model
         model._accumulate = i > 0
         model.layer_done_hook = self._hook if i == self.M - 1 else None

@@ -142,3 +142,85 @@ def test_sharded_names_and_seeded_init_are_rank_consistent():
     for name in e0.store.offsets:
         same = torch.equal(e0.store.w(name), e1.store.w(name))
         assert same == (not _sharded(name)) or "ln" in name, name
+
+
+def test_tp2_peer_exchange_protocol_matches_single_rank():
+    """The symmetric-memory TP path (TPPeer: gather buffers written by the
+    producer on both ranks, partial sums stored into the peer's receive
+    buffer, flags as events) on CPU threads gives the single-rank result."""
+    from shift_b200.parallel.tp import TPPeer
+
+    class Heap:
+        def __init__(self, owner):
+            self.owner = owner
+
+    torch.manual_seed(0)
+    cfg = _cfg()
+    B, S, tp = 1, 256, 2
+    data = synthetic_batch(cfg, 12, B, S)
+    tok, lab = data[:, :-1].contiguous(), data[:, 1:].contiguous()
+    full = Engine(cfg, "cpu", bucket_numel=1 << 20)
+    loss_full = float(full.forward_backward([(tok, lab)], B, S))
+    W = full.store.model_state_dict()
+    D = cfg.head_dim
+    hq, hkv = cfg.heads // tp, cfg.kv_heads // tp
+    e_per = cfg.experts // tp
+    bar = threading.Barrier(tp)
+    engines, losses, errors = [None] * tp, [None] * tp, []
+
+    def shard_of(name, t):
+        w = W[name]
+        if name.endswith("attn.qkv"):
+            q = w[: cfg.heads * D].view(cfg.heads, D, -1)[t * hq:(t + 1) * hq].reshape(-1, w.shape[1])
+            k = w[cfg.heads * D:(cfg.heads + cfg.kv_heads) * D].view(cfg.kv_heads, D, -1)[t * hkv:(t + 1) * hkv]
+            v = w[(cfg.heads + cfg.kv_heads) * D:].view(cfg.kv_heads, D, -1)[t * hkv:(t + 1) * hkv]
+            return torch.cat([q, k.reshape(-1, w.shape[1]), v.reshape(-1, w.shape[1])], 0)
+        if name.endswith("attn.o"):
+            return w.view(w.shape[0], cfg.heads, D)[:, t * hq:(t + 1) * hq].reshape(w.shape[0], -1)
+        if name.endswith("mlp.w1") or name.endswith("mlp.w2"):
+            return w[t * e_per:(t + 1) * e_per]
+        return w
+
+    def run(t):
+        try:
+            peer = TPPeer(None, t, tp, "cpu", Heap(f"cpu_t{t}"), f"cpu_t{1 - t}", tokens=B * S, hidden=cfg.hidden,
+                          layers=range(cfg.layers), microbatches=1, timeout_s=60)
+            part = Partition(expert_lo=t * e_per, expert_hi=(t + 1) * e_per, tp_size=tp)
+            eng = Engine(cfg, "cpu", part=part, bucket_numel=1 << 20, tp=peer)
+            for name in eng.store.offsets:
+                eng.store.w(name).copy_(shard_of(name, t))
+            bar.wait()
+            peer.connect(eng.step_block.dev)
+            peer.set_slot(0, 0)
+            eng.prepare_step(1)
+            losses[t] = float(eng.forward_backward([(tok, lab)], B, S))
+            engines[t] = eng
+        except BaseException as e:  # pragma: no cover - surfaced below
+            errors.append(e)
+            bar.abort()
+
+    ths = [threading.Thread(target=run, args=(t,)) for t in range(tp)]
+    for th in ths:
+        th.start()
+    for th in ths:
+        th.join(300)
+    assert not errors, errors
+    assert abs(sum(losses) - loss_full) < 1e-4
+    for name in W:
+        g_full = full.store.g(name)
+        if _sharded(name):
+            if "mlp" in name:
+                got = torch.cat([engines[t].store.g(name) for t in range(tp)], 0)
+            elif name.endswith("attn.o"):
+                got = torch.cat([engines[t].store.g(name).view(g_full.shape[0], hq, D) for t in range(tp)], 1)
+                got = got.reshape(g_full.shape)
+            else:
+                gq = torch.cat([engines[t].store.g(name)[: hq * D] for t in range(tp)], 0)
+                gk = torch.cat([engines[t].store.g(name)[hq * D:(hq + hkv) * D] for t in range(tp)], 0)
+                gv = torch.cat([engines[t].store.g(name)[(hq + hkv) * D:] for t in range(tp)], 0)
+                got = torch.cat([gq, gk, gv], 0)
+        else:
+            got = engines[0].store.g(name) + engines[1].store.g(name)
+        err = (got - g_full).abs().max().item()
+        scale = g_full.abs().max().item() + 1e-8
+        assert err <= 2e-4 * max(1.0, scale) + 1e-7, (name, err, scale)

@@ -21,8 +21,9 @@ import torch.distributed as dist
 from ..engine import Engine, synthetic_batch
 from ..models.qwen_moe import TP_SHARDED, MoEConfig, Partition, param_specs
 from ..ops._ext import check_status
+from ..graphs import StepGraphs, graphs_enabled
 from .replicas import _order
-from .symmetric import CrossReplicaFused, SymmetricHeap
+from .symmetric import CrossReplicaFused, SymmetricHeap, _tag
 from .tp import TPComm, TPPeer
 
 
@@ -113,6 +114,11 @@ class ModelParallelRunner:
         sl = slice(self.r * b_per, (self.r + 1) * b_per)
         self.dev_batches = [synthetic_batch(cfg, i, batch, seq)[sl].to(self.device) for i in range(2)]
         self.host = synthetic_batch(cfg, 10_000, batch, seq)[sl].contiguous().pin_memory()
+        self.tokens = torch.empty_like(self.dev_batches[0])      # static step input (graph replay)
+        use_graphs = graphs_enabled() and (pp == 1 or os.environ.get("SHIFT_PP_GRAPHS") == "1")
+        if self.tp_backend == "nccl" and tp > 1:
+            use_graphs = use_graphs and os.environ.get("SHIFT_PP_GRAPHS") == "1"
+        self.graphs = StepGraphs(self.device, use_graphs)
         self.step_no = 0
         self.tok_loc = self.mb * seq // tp
         dist.barrier()
@@ -160,9 +166,27 @@ class ModelParallelRunner:
         return None if d is None else torch.stack([d, d])
 
     def _train(self, data):
+        """One step.  Without pipelining (no NCCL on the step's path when the
+        TP pair runs over peer memory) the step is captured as a CUDA graph per
+        (state generation, step parity) after two eager steps; with pipelining
+        it runs eagerly unless SHIFT_PP_GRAPHS=1 (NCCL p2p inside the graph)."""
+        step = self.step_no
+        self.engine.prepare_step(_tag(step))
+        if data is not self.tokens:
+            self.tokens.copy_(data, non_blocking=True)
+        if step < 2 or not self.graphs.enabled:
+            loss = self._device_step()
+        else:
+            loss = self.graphs.run((self.engine.store.cur, step % 2), self._device_step)
+        self.engine.commit()
+        self.step_no += 1
+        return loss
+
+    def _device_step(self):
+        data = self.tokens
         eng = self.engine
         eng.nonfinite.zero_()
-        self.fused.begin_step(self.step_no)
+        self.fused.begin_step(self.step_no, prepare=False)
         eng.store.zero_grad()
         self._loss = None
         M, s, pp = self.M, self.s, self.PP
@@ -191,21 +215,19 @@ class ModelParallelRunner:
                 self._p2p(send=dx, send_to=s - 1)
         eng.model._accumulate = False
         self.fused.finish_step()
-        eng.commit()
-        self.step_no += 1
         return self._loss if self._loss is not None else torch.zeros((), device=self.device)
 
     def step(self, i: int):
         return self._train(self.dev_batches[i % len(self.dev_batches)])
 
     def step_e2e(self, i: int):
-        data = self.host.to(self.device, non_blocking=True)
-        loss = self._train(data)
+        loss = self._train(self.host)
         val = loss.item()
         return val, self.host.numel() * self.host.element_size(), 4
 
     def close(self):
         torch.cuda.synchronize()
+        self.graphs.reset()
         check_status(self.device)
         dist.barrier()
         self.heap.close_peers()

@@ -85,10 +85,13 @@ def verify(session_dir, replicas: int = 2, ranks: int = 1) -> dict:
     seq = defaultdict(list)
     for c in commits:
         seq[(c["rid"], c["rank"], c.get("generation"))].append(c["step"])
+    breaks = []
     for k, s in seq.items():
-        if any(b != a + 1 for a, b in zip(s, s[1:])):
+        bad = [(a, b) for a, b in zip(s, s[1:]) if b != a + 1]
+        if bad:
             mono = False
-    add("monotonic_steps", mono)
+            breaks.append({"rid": k[0], "rank": k[1], "generation": k[2], "pairs": bad[:5]})
+    add("monotonic_steps", mono, breaks=breaks)
     pids = defaultdict(set)
     for x in rows:
         if x["kind"] in ("commit", "ready") and "pid" in x:

@@ -5,8 +5,11 @@
 //   as at least min_replicas replicas are waiting AND every replica that is
 //   still heartbeating is among them (event driven: no tick is waited for in
 //   the common case), or when join_timeout_ms has passed since the first
-//   request of the round.  Replicas whose heartbeat is older than
-//   heartbeat_timeout_ms do not hold a quorum back.  The quorum id increases
+//   request of the round -- unless a live replica outside the waiting set is
+//   ahead of every waiting one (then the round waits for it, up to a bounded
+//   cap), so that a relaunched replica heals instead of training alone.
+//   Replicas whose heartbeat is older than heartbeat_timeout_ms do not hold a
+//   quorum back.  The quorum id increases
 //   whenever membership changes.  Members are ordered by replica id.
 //   Behaviour mirrors the torchft lighthouse that the reference launches with
 //   --min_replicas / --join_timeout_ms / --heartbeat_timeout_ms /
@@ -85,6 +88,7 @@ class Lighthouse {
       m.maddr = r[5];
       m.saddr = r[6];
       last_hb_[m.rid] = t;
+      last_step_[m.rid] = m.step;
       if (waiting_.empty()) first_wait_ms_ = t;
       // a replica re-requesting replaces its previous pending request
       for (auto it = waiting_.begin(); it != waiting_.end();) {
@@ -133,6 +137,23 @@ class Lighthouse {
       }
     }
     if (!all_alive_waiting && t - first_wait_ms_ < join_timeout_ms_) return;
+    if (!all_alive_waiting) {
+      // Joining on the timeout must not leave behind a live replica that is
+      // AHEAD of every waiting one: a relaunched replica (step 0) would
+      // otherwise form a quorum of its own and train from scratch instead of
+      // healing from the live state.  Bounded: after stale_cap the live
+      // replica is presumed stuck and the quorum forms without it.
+      int64_t max_waiting = 0;
+      for (auto& w : waiting_) max_waiting = std::max(max_waiting, w.second.step);
+      bool ahead_alive = false;
+      for (auto& kv : last_hb_) {
+        if (t - kv.second > hb_timeout_ms_ || waiting_ids.count(kv.first)) continue;
+        auto st = last_step_.find(kv.first);
+        if (st != last_step_.end() && st->second > max_waiting) ahead_alive = true;
+      }
+      const int64_t stale_cap = std::max<int64_t>(5LL * hb_timeout_ms_, 20LL * join_timeout_ms_);
+      if (ahead_alive && t - first_wait_ms_ < stale_cap) return;
+    }
     // form
     std::vector<Member> members;
     for (auto& w : waiting_) members.push_back(w.second);
@@ -155,6 +176,7 @@ class Lighthouse {
   int min_replicas_, join_timeout_ms_, hb_timeout_ms_, tick_ms_;
   LineServer srv_;
   std::map<std::string, int64_t> last_hb_;
+  std::map<std::string, int64_t> last_step_;   // step of each replica's latest quorum request
   std::vector<std::pair<int, Member>> waiting_;
   int64_t first_wait_ms_ = 0;
   int64_t quorum_id_ = 0;

@@ -4,11 +4,11 @@
 namespace sb {
 namespace gemm {
 
-void dispatch_bn128(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int hint,
-                    cudaStream_t stream) {
-  if (!a_mn && !b_mn) launch<128, false, false>(ta, tb, p, hint, stream);
-  else if (!a_mn && b_mn) launch<128, false, true>(ta, tb, p, hint, stream);
-  else if (a_mn && b_mn) launch<128, true, true>(ta, tb, p, hint, stream);
+void dispatch_bn128(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td,
+                    const CUtensorMap& td2, const Params& p, int hint, cudaStream_t stream) {
+  if (!a_mn && !b_mn) launch<128, false, false>(ta, tb, td, td2, p, hint, stream);
+  else if (!a_mn && b_mn) launch<128, false, true>(ta, tb, td, td2, p, hint, stream);
+  else if (a_mn && b_mn) launch<128, true, true>(ta, tb, td, td2, p, hint, stream);
   else TORCH_CHECK(false, "gemm: unsupported major combination (A MN-major, B K-major)");
 }
 

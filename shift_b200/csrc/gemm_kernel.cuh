@@ -22,10 +22,19 @@ struct Cfg {
   static constexpr int kABytes = BM * BK * 2;   // 16 KB
   static constexpr int kBBytes = BN * BK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = (BN == 256) ? 4 : (BN == 192 ? 5 : 6);
+  static constexpr int kStages = (BN == 256) ? 4 : (BN == 192 ? 4 : 5);
   static constexpr int kTmemCols = 512;          // two accumulators of <= 256 columns
-  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/ +
+  // Epilogue staging for TMA stores: per epilogue warp two buffers of 32 rows
+  // x 64 bf16 (128 B rows, 128-byte swizzle) and, below BN 256, two SwiGLU
+  // activation buffers of 32 rows x 32 bf16 (64 B rows, 64-byte swizzle).
+  static constexpr bool kD2Staged = BN != 256;
+  static constexpr int kEpiD = 32 * 128;
+  static constexpr int kEpiD2 = kD2Staged ? 32 * 64 : 0;
+  static constexpr int kEpiWarpBytes = 2 * (kEpiD + kEpiD2);
+  static constexpr int kEpiBytes = 4 * kEpiWarpBytes;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kEpiBytes + 1024 /*align*/ + 256 /*barriers*/ +
                                     2 * (kMaxGroups + 1) * 4;
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
 struct Params {
@@ -45,6 +54,8 @@ struct Params {
   int m_rot;         // row mode, G == 1: row-tile order rotated by m_rot tiles
   int peer_lo, peer_hi;   // output rows in [peer_lo, peer_hi) go to xc.peer_out at row - peer_lo
   int d_row_off;     // the other output rows go to D at row - d_row_off
+  int use_tma_store; // tmD (and tmD2 for SwiGLU) describe D / D2: bf16 tiles leave through TMA
+  int d_rows;        // rows of the tensor tmD describes
 };
 
 struct TileInfo {
@@ -108,13 +119,15 @@ __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)
 
 template <int BN, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
-gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
+gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+            const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmD2, Params p) {
   using C = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023) & ~1023u) - raw_addr);
   uint8_t* tiles = smem;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
+  uint8_t* epi_stage = smem + C::kStages * C::kStageBytes;   // 1024-aligned (stage sizes are)
+  uint64_t* full = reinterpret_cast<uint64_t*>(epi_stage + C::kEpiBytes);
   uint64_t* empty = full + C::kStages;
   uint64_t* tmem_full = empty + C::kStages;
   uint64_t* tmem_empty = tmem_full + 2;
@@ -270,11 +283,73 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     const int r = quarter * 32 + lane;         // row within tile
     int acc = 0;
     uint32_t acc_phase = 0;
+    uint32_t epi_slab = 0;                     // staging double-buffer counter (TMA-store path)
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
       TileInfo t;
       decode_tile<BN, A_MN, B_MN>(p, s_prefix, s_offs, tile, t);
       if (!mbar_wait(&tmem_full[acc], acc_phase, p.status)) break;
       tc_fence_after();
+      // ---- TMA-store path: bf16 / SwiGLU outputs of local destinations.  The
+      // tile's accumulator slab (32 rows x 64 columns per warp) is converted
+      // and written to swizzled shared memory, then one lane stores it with
+      // TMA: whole 128-byte row segments instead of one row per thread.
+      const bool tile_to_peer = p.xc.peer_out != nullptr && t.out_row0 >= p.peer_lo && t.out_row0 < p.peer_hi;
+      const bool tma_ok = p.use_tma_store && !tile_to_peer && t.kb > 0 &&
+                          (t.m_valid == BM || t.out_row0 - p.d_row_off + t.m_valid >= p.d_rows) &&
+                          (p.epi == kEpiBF16 || (p.epi == kEpiSwiGLU && C::kD2Staged));
+      if (tma_ok) {
+        const int drow0 = t.out_row0 - p.d_row_off + quarter * 32;
+        uint8_t* wbuf = epi_stage + (warp - 2) * C::kEpiWarpBytes;
+        const int nslabs = min(BN, p.N - t.n0 + 63) / 64;
+#pragma unroll 1
+        for (int sb = 0; sb < nslabs; ++sb) {
+          const int c = sb * 64;
+          uint32_t v[64];
+          tmem_ld_32x32b_x32(tmem_base + acc * BN + c + ((quarter * 32) << 16), v);
+          tmem_ld_32x32b_x32(tmem_base + acc * BN + c + 32 + ((quarter * 32) << 16), v + 32);
+          tmem_wait_ld();
+          if (sb == nslabs - 1) {        // accumulator fully read: hand it back to the MMA warp
+            tc_fence_before();
+            mbar_arrive(&tmem_empty[acc]);
+          }
+          uint8_t* bd = wbuf + (epi_slab & 1) * (C::kEpiD + C::kEpiD2);
+          uint8_t* bd2 = bd + C::kEpiD;
+          ++epi_slab;
+          if (lane == 0) bulk_wait_group_read<1>();   // this buffer's previous store has read it
+          __syncwarp();
+          float f[64];
+#pragma unroll
+          for (int i = 0; i < 64; ++i) f[i] = __uint_as_float(v[i]) * p.alpha;
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<bf16x8*>(bd + lane * 128 + ((j ^ (lane & 7)) * 16)) = float_to_bf16x8(f + 8 * j);
+          if (C::kD2Staged && p.epi == kEpiSwiGLU) {
+            // columns [c, c+64) = (16 gate, 16 up) x 2 -> 32 activations
+            float a[32];
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                const float g = __bfloat162float(__float2bfloat16(f[32 * h + i]));
+                const float u = __bfloat162float(__float2bfloat16(f[32 * h + 16 + i]));
+                a[16 * h + i] = silu_f(g) * u;
+              }
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              *reinterpret_cast<bf16x8*>(bd2 + lane * 64 + ((j ^ ((lane >> 1) & 3)) * 16)) = float_to_bf16x8(a + 8 * j);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmD, bd, t.n0 + c, drow0);
+            if (C::kD2Staged && p.epi == kEpiSwiGLU) tma_store_2d(&tmD2, bd2, (t.n0 + c) / 2, drow0);
+            bulk_commit_group();
+          }
+        }
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+        continue;
+      }
       const bool row_ok = r < t.m_valid;
       const long grow = static_cast<long>(t.out_row0) + r;
       // destination: the TP peer's receive buffer for its rows, D otherwise
@@ -369,6 +444,13 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
+    // every TMA store of this warp has written global memory before the CTA
+    // finishes (and before a tensor-parallel signal)
+    if (lane == 0) {
+      bulk_wait_group<0>();
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+    }
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -382,8 +464,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
 int num_sms();
 
 template <int BN, bool A_MN, bool B_MN>
-inline void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int total_tiles_hint,
-                   cudaStream_t stream) {
+inline void launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td, const CUtensorMap& td2,
+                   const Params& p, int total_tiles_hint, cudaStream_t stream) {
   using C = Cfg<BN>;
   auto kern = gemm_kernel<BN, A_MN, B_MN>;
   static bool configured = false;
@@ -392,7 +474,7 @@ inline void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p
     configured = true;
   }
   int grid = std::min(num_sms(), std::max(1, total_tiles_hint));
-  kern<<<grid, kThreads, C::kSmemBytes, stream>>>(ta, tb, p);
+  kern<<<grid, kThreads, C::kSmemBytes, stream>>>(ta, tb, td, td2, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -36,6 +36,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <cstring>
 #include <mutex>
 
 #include "gemm_kernel.cuh"
@@ -44,9 +45,12 @@
 namespace sb {
 namespace gemm {
 
-void dispatch_bn128(bool, bool, const CUtensorMap&, const CUtensorMap&, const Params&, int, cudaStream_t);
-void dispatch_bn192(bool, bool, const CUtensorMap&, const CUtensorMap&, const Params&, int, cudaStream_t);
-void dispatch_bn256(bool, bool, const CUtensorMap&, const CUtensorMap&, const Params&, int, cudaStream_t);
+void dispatch_bn128(bool, bool, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&,
+                    const Params&, int, cudaStream_t);
+void dispatch_bn192(bool, bool, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&,
+                    const Params&, int, cudaStream_t);
+void dispatch_bn256(bool, bool, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&,
+                    const Params&, int, cudaStream_t);
 
 // ---------------------------------------------------------------------------
 // Host side
@@ -70,17 +74,21 @@ static EncodeFn get_encode() {
 }
 
 // 2D bf16 tensor map over a row-major matrix [rows, cols] with row stride ld
-// (elements), box {64, box_rows}, 128-byte swizzle.
-static CUtensorMap make_map(const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+// (elements), box {box_cols, box_rows}; 128-byte swizzle for 64-column
+// boxes, 64-byte swizzle for 32-column boxes.
+static CUtensorMap make_map(const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows,
+                            int box_cols = 64) {
   TORCH_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base must be 16-byte aligned");
   TORCH_CHECK((ld * 2) % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
+  TORCH_CHECK(box_cols == 64 || box_cols == 32, "TMA box width");
   CUtensorMap m;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
-  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = get_encode()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
-                            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            box_cols == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed with code ", static_cast<int>(r));
   return m;
@@ -153,6 +161,30 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const c10::op
   if (p.xc.wait_flag != nullptr && mode == kKGroups)
     TORCH_CHECK(p.wait_lo % BK == 0 && p.wait_hi % BK == 0, "gemm: k-mode wait range must be 64-aligned");
 
+  // Output through TMA stores (bf16 / SwiGLU epilogues into local memory):
+  // D viewed as [d_rows, N] with row stride ldd, D2 as [d_rows, N/2].
+  CUtensorMap td, td2;
+  std::memset(&td, 0, sizeof(td));
+  std::memset(&td2, 0, sizeof(td2));
+  p.use_tma_store = 0;
+  p.d_rows = 0;
+  const int64_t d_rows = D.dim() >= 2 ? D.numel() / D.size(-1) : 1;
+  const bool d_dense = D.dim() < 3 || D.is_contiguous();
+  if ((epi == kEpiBF16 || epi == kEpiSwiGLU) && d_dense && reinterpret_cast<uintptr_t>(D.data_ptr()) % 16 == 0 &&
+      (static_cast<int64_t>(p.ldd) * 2) % 16 == 0 && N % 8 == 0 && d_rows > 0) {
+    bool ok = true;
+    if (epi == kEpiSwiGLU) {
+      ok = reinterpret_cast<uintptr_t>(D2->data_ptr()) % 16 == 0 && (static_cast<int64_t>(p.ldd2) * 2) % 16 == 0 &&
+           (N / 2) % 8 == 0;
+      if (ok) td2 = make_map(D2->data_ptr(), d_rows, N / 2, p.ldd2, 32, 32);
+    }
+    if (ok) {
+      td = make_map(D.data_ptr(), d_rows, N, p.ldd, 32, 64);
+      p.use_tma_store = 1;
+      p.d_rows = static_cast<int>(d_rows);
+    }
+  }
+
   // Upper bound of tiles for the grid size (the kernel computes the exact count).
   const int64_t tn = (N + bn - 1) / bn;
   int64_t tiles;
@@ -161,9 +193,9 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const c10::op
   const int hint = static_cast<int>(std::min<int64_t>(tiles, 1 << 30));
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
 
-  if (bn == 256) dispatch_bn256(a_mn, b_mn, ta, tb, p, hint, stream);
-  else if (bn == 192) dispatch_bn192(a_mn, b_mn, ta, tb, p, hint, stream);
-  else dispatch_bn128(a_mn, b_mn, ta, tb, p, hint, stream);
+  if (bn == 256) dispatch_bn256(a_mn, b_mn, ta, tb, td, td2, p, hint, stream);
+  else if (bn == 192) dispatch_bn192(a_mn, b_mn, ta, tb, td, td2, p, hint, stream);
+  else dispatch_bn128(a_mn, b_mn, ta, tb, td, td2, p, hint, stream);
 }
 
 }  // namespace gemm

@@ -298,3 +298,77 @@ def test_adamw_device_step_block_matches_host_scalars():
     Fn.adamw_step(master, m, v, [g1], *b, 123.0, 0.9, 0.999, 1e-8, 0.01, 1, 1.0, step_dev=blk.dev)
     for x, y in zip(a, b):
         assert torch.equal(x, y)
+
+
+def test_gemm_tensor_parallel_forms_single_gpu():
+    """The exchange forms of the GEMM on one GPU (the 'peer' buffers are
+    local tensors): rows of the peer half go to the peer buffer, the rest to
+    out; the rotated tile order changes nothing; the in-kernel wait passes on
+    a set flag; the last CTA signals with the step tag."""
+    from shift_b200.engine import StepBlock
+    torch.manual_seed(21)
+    T, N, K = 1024, 768, 512
+    half = T // 2
+    x, w = _bf(T, K), _bf(N, K)
+    ref_y = x.float() @ w.float().t()
+    blk = StepBlock(torch.device(DEV))
+    blk.write(5, 1e-4, 0.9, 0.999, 1)
+    flags = torch.zeros(8, dtype=torch.int32, device=DEV)
+    flags[0] = 5                                    # the "peer" has published its rows
+    for rank in (0, 1):
+        own = slice(rank * half, (rank + 1) * half)
+        plo, phi = (1 - rank) * half, (2 - rank) * half
+        out = torch.zeros(half, N, dtype=torch.bfloat16, device=DEV)
+        peer = torch.zeros(half, N, dtype=torch.bfloat16, device=DEV)
+        xc = [flags[0].data_ptr(), 0, flags[1 + rank].data_ptr(), flags[4 + rank].data_ptr(), 0,
+              blk.dev.data_ptr(), peer.data_ptr()]
+        G.linear_fwd(x, w, out=out, xchg=xc, tp=(plo, phi, (plo // 128), plo, phi, own.start))
+        torch.cuda.synchronize()
+        check_status()
+        _close(out, ref_y[own])
+        _close(peer, ref_y[plo:phi])
+        assert int(flags[1 + rank]) == 5 and int(flags[4 + rank]) == 0   # signalled, counter reset
+    # k-mode (weight gradient) with a wait over the peer's token rows
+    dy = _bf(T, N)
+    dw = torch.empty(N, K, dtype=torch.bfloat16, device=DEV)
+    G.linear_wgrad(dy, x, dw, xchg=[flags[0].data_ptr(), 0, 0, 0, 0, blk.dev.data_ptr(), 0], tp=(half, T, 0, 0, 0, 0))
+    torch.cuda.synchronize()
+    check_status()
+    _close(dw, dy.float().t() @ x.float())
+
+
+def test_norm_exchange_forms_single_gpu():
+    """RMSNorm fwd/bwd with a second partial (delta2 / dy2), an explicit
+    output buffer and a copy into a 'peer' buffer, signalled with the tag."""
+    from shift_b200.engine import StepBlock
+    torch.manual_seed(22)
+    T, H = 512, 1024
+    x, d1, d2 = _bf(T, H), _bf(T, H), _bf(T, H)
+    w = _bf(H, std=0.1) + 1
+    blk = StepBlock(torch.device(DEV))
+    blk.write(9, 1e-4, 0.9, 0.999, 1)
+    flags = torch.zeros(8, dtype=torch.int32, device=DEV)
+    flags[0] = 9
+    y_out = torch.empty(T, H, dtype=torch.bfloat16, device=DEV)
+    y_peer = torch.empty_like(y_out)
+    xc = [flags[0].data_ptr(), 0, flags[1].data_ptr(), flags[2].data_ptr(), 0, blk.dev.data_ptr(), y_peer.data_ptr()]
+    y, rstd, h = Fn.rmsnorm_fwd(x, w, 1e-6, d1, delta2=d2, y_out=y_out, xchg=xc)
+    torch.cuda.synchronize()
+    check_status()
+    hr = (x.float() + d1.float() + d2.float()).to(torch.bfloat16)
+    assert torch.equal(h, hr)
+    _close(y_out, ref.rmsnorm(hr.float(), w.float(), 1e-6))
+    assert torch.equal(y_out, y_peer) and int(flags[1]) == 9
+    dy, dy2, dres = _bf(T, H), _bf(T, H), _bf(T, H)
+    dw = torch.zeros(H, device=DEV)
+    dx_out = torch.empty_like(y_out)
+    dx_peer = torch.empty_like(y_out)
+    xc = [flags[0].data_ptr(), 0, flags[3].data_ptr(), flags[4].data_ptr(), 0, blk.dev.data_ptr(), dx_peer.data_ptr()]
+    Fn.rmsnorm_bwd(dy, h, rstd, w, 1e-6, dw, dres=dres, dy2=dy2, dx_out=dx_out, xchg=xc)
+    torch.cuda.synchronize()
+    check_status()
+    dsum = dy.float() + dy2.float()
+    (gx, gw) = ref.grad_of(lambda a, b: ref.rmsnorm(a, b, 1e-6), [h.float(), w.float()], dsum)
+    _close(dx_out, gx + dres.float())
+    _close(dw, gw)
+    assert torch.equal(dx_out, dx_peer) and int(flags[3]) == 9

@@ -132,3 +132,32 @@ def test_standalone_daemon():
     finally:
         p.terminate()
         p.wait(5)
+
+
+def test_timeout_quorum_waits_for_a_live_replica_that_is_ahead():
+    """A relaunched replica (step 0) must not form a quorum of its own on the
+    join timeout while a live replica ahead of it is between requests: it
+    waits and heals from that replica (bounded)."""
+    lh = LighthouseServer(min_replicas=1, join_timeout_ms=100, heartbeat_timeout_ms=2000, quorum_tick_ms=10)
+    try:
+        a, b = LighthouseClient(lh.address), LighthouseClient(lh.address)
+        _, ma = a.quorum("A", 20)              # A trains alone at step 20
+        assert [m["replica_id"] for m in ma] == ["A"]
+        a.heartbeat("A")
+        res = {}
+        th = threading.Thread(target=lambda: res.setdefault("b", b.quorum("B", 0)))
+        t0 = time.monotonic()
+        th.start()
+        time.sleep(0.6)                        # far past the join timeout
+        assert "b" not in res, "B formed a quorum without the live replica ahead of it"
+        a.heartbeat("A")
+        _, ma2 = a.quorum("A", 21)
+        th.join(10)
+        waited = time.monotonic() - t0
+        assert waited >= 0.6
+        ids = sorted(m["replica_id"] for m in res["b"][1])
+        assert ids == ["A", "B"] and sorted(m["replica_id"] for m in ma2) == ["A", "B"]
+        a.close()
+        b.close()
+    finally:
+        lh.stop()

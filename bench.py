@@ -51,6 +51,8 @@ def parse():
     p.add_argument("--batch", type=int, default=GLOBAL_BATCH)
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-launch-count", action="store_true")
+    p.add_argument("--trace", default=None,
+                   help="write a kernel timeline (chrome trace) of one untimed step per rank into this folder")
     return p.parse_args()
 
 
@@ -160,6 +162,16 @@ def main():
             else:
                 lib += 1
         per_step_launches, library_launches = ours, lib
+
+    if args.trace:
+        from torch.profiler import ProfilerActivity, profile
+        os.makedirs(args.trace, exist_ok=True)
+        barrier()
+        with profile(activities=[ProfilerActivity.CUDA, ProfilerActivity.CPU]) as prof:
+            runner.step(args.warmup)
+            torch.cuda.synchronize()
+        prof.export_chrome_trace(os.path.join(args.trace, f"trace_n{world}_r{rank}.json"))
+        barrier()
 
     # ---------------- device-timed loop ----------------
     clocks = ClockSampler(local)

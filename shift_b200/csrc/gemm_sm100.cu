@@ -37,7 +37,9 @@
 #include <c10/cuda/CUDAGuard.h>
 
 #include <cstring>
+#include <map>
 #include <mutex>
+#include <tuple>
 
 #include "gemm_kernel.cuh"
 #include "xchg.h"
@@ -104,6 +106,58 @@ int num_sms() {
   return n;
 }
 
+// ---------------------------------------------------------------------------
+// Split-K for dense weight gradients with few output tiles (e.g. a 1024 x 1024
+// weight over 16k tokens is 32 tiles on 148 SMs): the contraction is cut into
+// S 64-aligned ranges run as the kernel's k-groups into an fp32 workspace
+// [S*M, N], then summed over S in a fixed order (deterministic) into D with
+// the requested epilogue.
+// ---------------------------------------------------------------------------
+__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int S, long MN, int epi, void* D) {
+  const long i = (static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
+  if (i >= MN) return;
+  float4 acc = *reinterpret_cast<const float4*>(ws + i);
+  for (int s = 1; s < S; ++s) {
+    const float4 v = *reinterpret_cast<const float4*>(ws + static_cast<long>(s) * MN + i);
+    acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+  }
+  if (epi == kEpiF32 || epi == kEpiAccF32) {
+    float4* o = reinterpret_cast<float4*>(static_cast<float*>(D) + i);
+    if (epi == kEpiAccF32) {
+      const float4 b = *o;
+      acc.x += b.x; acc.y += b.y; acc.z += b.z; acc.w += b.w;
+    }
+    *o = acc;
+  } else {
+    __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(static_cast<__nv_bfloat16*>(D) + i);
+    if (epi == kEpiAccBF16) {
+      const float2 b0 = __bfloat1622float2(o[0]), b1 = __bfloat1622float2(o[1]);
+      acc.x += b0.x; acc.y += b0.y; acc.z += b1.x; acc.w += b1.y;
+    }
+    o[0] = __floats2bfloat162_rn(acc.x, acc.y);
+    o[1] = __floats2bfloat162_rn(acc.z, acc.w);
+  }
+}
+
+// device table of split boundaries, created once per (K, S, device) outside
+// graph capture and reused (a capture may not upload host data)
+static const at::Tensor* split_offsets(int64_t K, int S, const at::Device& dev) {
+  static std::map<std::tuple<int64_t, int, int>, at::Tensor> cache;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  const auto key = std::make_tuple(K, S, static_cast<int>(dev.index()));
+  auto it = cache.find(key);
+  if (it != cache.end()) return &it->second;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  cudaStreamIsCapturing(at::cuda::getCurrentCUDAStream(), &cs);
+  if (cs != cudaStreamCaptureStatusNone) return nullptr;
+  std::vector<int> o(S + 1);
+  for (int s = 0; s <= S; ++s) o[s] = static_cast<int>((K * s / S) / 64 * 64);
+  o[S] = static_cast<int>(K);
+  auto t = at::tensor(o, at::TensorOptions().dtype(at::kInt)).to(dev);
+  return &(cache[key] = t);
+}
+
 // Generic entry.  See gemm_sm100.h for argument meaning.
 void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const c10::optional<at::Tensor>& D2,
           const c10::optional<at::Tensor>& offs, int64_t M, int64_t N, int64_t K, int64_t G, int64_t mode,
@@ -111,6 +165,26 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const c10::op
           int64_t max_rows_hint, const std::vector<int64_t>& xchg, const std::vector<int64_t>& tp) {
   TORCH_CHECK(A.is_cuda() && B.is_cuda() && D.is_cuda(), "gemm: CUDA tensors required");
   TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "gemm: bf16 operands");
+  // split-K for a dense k-mode GEMM (weight gradient) that fills few SMs
+  if (mode == kKGroups && G == 1 && !offs.has_value() && epi != kEpiSwiGLU && D.is_contiguous() &&
+      (xchg.empty() || xchg[2] == 0) && (M * N) % 4 == 0) {
+    const int64_t tiles = ((M + BM - 1) / BM) * ((N + bn - 1) / bn);
+    const int S = static_cast<int>(std::min<int64_t>(num_sms() / std::max<int64_t>(tiles, 1), K / 1024));
+    if (S >= 2) {
+      const at::Tensor* so = split_offsets(K, S, A.device());
+      if (so != nullptr) {
+        const at::cuda::CUDAGuard guard(A.device());
+        auto ws = at::empty({S * M, N}, A.options().dtype(at::kFloat));
+        gemm(A, B, ws, c10::nullopt, *so, M, N, K, S, kKGroups, a_mn, b_mn, kEpiF32, alpha, bn, status,
+             max_rows_hint, xchg, tp);
+        const long MN = M * N;
+        splitk_reduce_kernel<<<static_cast<unsigned>((MN / 4 + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+            ws.data_ptr<float>(), S, MN, static_cast<int>(epi), D.data_ptr());
+        C10_CUDA_KERNEL_LAUNCH_CHECK();
+        return;
+      }
+    }
+  }
   TORCH_CHECK(A.stride(-1) == 1 && B.stride(-1) == 1 && D.stride(-1) == 1, "gemm: inner dim must be contiguous");
   TORCH_CHECK(G >= 1 && G <= kMaxGroups, "gemm: group count out of range");
   TORCH_CHECK(N % 16 == 0, "gemm: N must be a multiple of 16");

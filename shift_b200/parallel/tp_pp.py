@@ -240,4 +240,6 @@ def make_model_parallel_runner(layout: str, cfg, n_gpus, rank, local_rank, batch
     tp = 2
     pp = 2 if layout == "tppp" else 1
     replicas = n_gpus // (tp * pp)
-    return ModelParallelRunner(cfg, n_gpus, rank, local_rank, batch, seq, replicas, tp, pp)
+    mb = os.environ.get("SHIFT_MICROBATCH")      # sequences per pipeline microbatch
+    return ModelParallelRunner(cfg, n_gpus, rank, local_rank, batch, seq, replicas, tp, pp,
+                               microbatch=int(mb) if mb else None)

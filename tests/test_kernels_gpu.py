@@ -45,11 +45,12 @@ def test_linear_dgrad(M, N, K):
     _close(dx, dy.float() @ w.float())
 
 
+@pytest.mark.parametrize("M", [640, 8192])          # 8192 tokens: split-K path (few output tiles)
 @pytest.mark.parametrize("dtype,acc", [(torch.float32, False), (torch.float32, True), (torch.bfloat16, False),
                                        (torch.bfloat16, True)])
-def test_linear_wgrad(dtype, acc):
+def test_linear_wgrad(dtype, acc, M):
     torch.manual_seed(2)
-    M, N, K = 640, 384, 256
+    N, K = 384, 256
     dy, x = _bf(M, N), _bf(M, K)
     base = torch.randn(N, K, device=DEV).to(dtype)
     dw = base.clone()

@@ -58,6 +58,8 @@ struct Params {
   int dqkv_stride;
   int o_stride;
   int* status;
+  int hsplit;        // dK/dV: CTAs per (key block, kv head), each over group/hsplit query heads
+  float* ws;         // hsplit > 1: fp32 partials [B, Hkv, hsplit, S, 2*D] (dK scaled | dV)
 };
 
 SB_DEVICE float ex2(float x) {
@@ -307,8 +309,13 @@ dkdv_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUte
   uint64_t* drain = acc_done + 1;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(drain + 1);
 
-  const int kb = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
-  const int group = p.Hq / p.Hkv;
+  // At small batch a causal key block near the start of the sequence is the
+  // critical path (it meets every later query block of every head of its
+  // group); with hsplit > 1 the group's query heads are spread over hsplit
+  // CTAs whose fp32 partials are summed in a fixed order afterwards.
+  const int kb = blockIdx.x, kvh = blockIdx.y / p.hsplit, part = blockIdx.y % p.hsplit, b = blockIdx.z;
+  const int group = p.Hq / p.Hkv / p.hsplit;     // query heads handled by this CTA
+  const int h_first = kvh * (p.Hq / p.Hkv) + part * group;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int k0 = kb * BN;
   const int tok0 = b * p.S;
@@ -347,7 +354,7 @@ dkdv_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUte
       tma_load_2d(sK, &tm, kv_full, (p.Hq + kvh) * D, tok0 + k0);
       tma_load_2d(sV, &tm, kv_full, (p.Hq + p.Hkv + kvh) * D, tok0 + k0);
       for (int it = 0; it < n_it; ++it) {
-        const int h = kvh * group + it / per_head;
+        const int h = h_first + it / per_head;
         const int qb = kb + it % per_head;
         const int st = it % kBwdStages;
         if (!mbar_wait(&qo_empty[st], ((it / kBwdStages) & 1) ^ 1, p.status)) break;
@@ -397,7 +404,7 @@ dkdv_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUte
     const int sm_tid = threadIdx.x - 64;     // 0..127
     bool ok = true;
     for (int it = 0; it < n_it; ++it) {
-      const int h = kvh * group + it / per_head;
+      const int h = h_first + it / per_head;
       const int qb = kb + it % per_head;
       const int q0 = qb * BM;
       // stage this block's lse / delta (one value per thread), then wait for S^T / dP^T
@@ -443,7 +450,27 @@ dkdv_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUte
       tc_fence_before();
       mbar_arrive(ds_full);
     }
-    if (ok && mbar_wait(acc_done, 0, p.status)) {
+    if (ok && p.hsplit > 1 && mbar_wait(acc_done, 0, p.status)) {
+      tc_fence_after();
+      uint32_t v[32];
+      float* wrow = p.ws + ((((static_cast<long>(b) * p.Hkv + kvh) * p.hsplit + part) * p.S) + key) * (2 * D);
+#pragma unroll
+      for (int c = 0; c < D; c += 32) {
+        tmem_ld_32x32b_x32(tdK + c + lane_off, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int t = 0; t < 32; t += 4)
+          *reinterpret_cast<float4*>(wrow + c + t) =
+              make_float4(__uint_as_float(v[t]) * p.scale, __uint_as_float(v[t + 1]) * p.scale,
+                          __uint_as_float(v[t + 2]) * p.scale, __uint_as_float(v[t + 3]) * p.scale);
+        tmem_ld_32x32b_x32(tdV + c + lane_off, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int t = 0; t < 32; t += 4)
+          *reinterpret_cast<float4*>(wrow + D + c + t) = make_float4(
+              __uint_as_float(v[t]), __uint_as_float(v[t + 1]), __uint_as_float(v[t + 2]), __uint_as_float(v[t + 3]));
+      }
+    } else if (ok && mbar_wait(acc_done, 0, p.status)) {
       tc_fence_after();
       uint32_t v[32];
       __nv_bfloat16* krow = p.dqkv + static_cast<long>(tok0 + key) * p.dqkv_stride + (p.Hq + kvh) * D;
@@ -697,6 +724,32 @@ static CUtensorMap tile_map(const void* base, int64_t rows, int64_t cols, int64_
   return m;
 }
 
+// dK/dV of a head split: sum the hsplit partials in order, write bf16.
+// One thread per (b, key, kv head, 8 values of the 2*D row).
+__global__ void dkdv_reduce_kernel(const float* __restrict__ ws, int B, int S, int Hq, int Hkv, int hsplit,
+                                   __nv_bfloat16* __restrict__ dqkv, int stride) {
+  const long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long per_row = 2 * D / 8;
+  const long total = static_cast<long>(B) * Hkv * S * per_row;
+  if (i >= total) return;
+  const int c8 = static_cast<int>(i % per_row);
+  const long r = i / per_row;                 // (b, kvh, key)
+  const int key = static_cast<int>(r % S);
+  const int kvh = static_cast<int>((r / S) % Hkv);
+  const int b = static_cast<int>(r / (static_cast<long>(S) * Hkv));
+  float acc[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+  for (int pt = 0; pt < hsplit; ++pt) {
+    const float* src = ws + ((((static_cast<long>(b) * Hkv + kvh) * hsplit + pt) * S) + key) * (2 * D) + c8 * 8;
+    const float4 a = reinterpret_cast<const float4*>(src)[0], c = reinterpret_cast<const float4*>(src)[1];
+    acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
+    acc[4] += c.x; acc[5] += c.y; acc[6] += c.z; acc[7] += c.w;
+  }
+  const int col = (c8 * 8 < D) ? (Hq + kvh) * D + c8 * 8 : (Hq + Hkv + kvh) * D + (c8 * 8 - D);
+  *reinterpret_cast<bf16x8*>(dqkv + (static_cast<long>(b) * S + key) * stride + col) = float_to_bf16x8(acc);
+}
+
 static Params base_params(const at::Tensor& qkv, int64_t B, int64_t S, int64_t Hq, int64_t Hkv, double scale,
                           const at::Tensor& status) {
   TORCH_CHECK(qkv.scalar_type() == at::kBFloat16 && qkv.stride(-1) == 1, "attention: bf16 qkv");
@@ -712,6 +765,8 @@ static Params base_params(const at::Tensor& qkv, int64_t B, int64_t S, int64_t H
   p.scale = static_cast<float>(scale);
   p.scale_log2 = static_cast<float>(scale) * kLog2e;
   p.status = status.data_ptr<int>();
+  p.hsplit = 1;
+  p.ws = nullptr;
   return p;
 }
 
@@ -760,8 +815,27 @@ at::Tensor bwd(const at::Tensor& qkv, const at::Tensor& o, const at::Tensor& lse
     cudaFuncSetAttribute(dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDqSmem);
     cfg = true;
   }
-  dim3 g1(static_cast<unsigned>(S / BN), static_cast<unsigned>(Hkv), static_cast<unsigned>(B));
+  // head split when the dK/dV grid would leave most SMs idle (small batch)
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int group = static_cast<int>(Hq / Hkv);
+  const long ctas = (S / BN) * Hkv * B;
+  int hs = 1;
+  while (hs < group && group % (hs * 2) == 0 && ctas * hs * 2 <= 2L * sms) hs *= 2;
+  at::Tensor ws;
+  if (hs > 1) {
+    ws = at::empty({B * Hkv * hs * S * 2 * D}, qkv.options().dtype(at::kFloat));
+    p.hsplit = hs;
+    p.ws = ws.data_ptr<float>();
+  }
+  dim3 g1(static_cast<unsigned>(S / BN), static_cast<unsigned>(Hkv * hs), static_cast<unsigned>(B));
   dkdv_kernel<<<g1, kThreads, kDkdvSmem, stream>>>(tm, tmo, p);
+  if (hs > 1) {
+    const long total = B * Hkv * S * (2 * D / 8);
+    dkdv_reduce_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(
+        p.ws, (int)B, (int)S, (int)Hq, (int)Hkv, hs, p.dqkv, p.dqkv_stride);
+  }
   dim3 g2(static_cast<unsigned>(S / BM), static_cast<unsigned>(Hq), static_cast<unsigned>(B));
   dq_kernel<<<g2, kThreads, kDqSmem, stream>>>(tm, tmo, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();

@@ -234,11 +234,11 @@ constexpr int kWgChunk = 128;
 template <int E>
 __global__ void __launch_bounds__(256)
 router_wgrad_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ dlogits, int T, int H,
-                    float* __restrict__ partial) {
+                    float* __restrict__ partial, int chunk) {
   __shared__ float sdl[kWgChunk][E];
-  const int t0 = blockIdx.x * kWgChunk;
-  const int nt = min(kWgChunk, T - t0);
-  for (int i = threadIdx.x; i < kWgChunk * E; i += blockDim.x) {
+  const int t0 = blockIdx.x * chunk;
+  const int nt = min(chunk, T - t0);
+  for (int i = threadIdx.x; i < chunk * E; i += blockDim.x) {
     const int tt = i / E, e = i % E;
     sdl[tt][e] = tt < nt ? dlogits[static_cast<long>(t0 + tt) * E + e] : 0.f;
   }
@@ -280,7 +280,10 @@ at::Tensor router_input_weight_grad(const at::Tensor& x, const at::Tensor& wr, c
   const int T = static_cast<int>(x.numel() / H);
   const int E = static_cast<int>(wr.size(0));
   TORCH_CHECK(H % 1024 == 0 || H == 256 || H == 512, "router grad: H");
-  const int nchunks = std::max(1, (T + kWgChunk - 1) / kWgChunk);
+  // token chunk per block: enough blocks to fill the GPU at small T, few
+  // enough partial rows for the column reduction at large T
+  const int chunk = std::max(16, std::min(kWgChunk, T / 256));
+  const int nchunks = std::max(1, (T + chunk - 1) / chunk);
   auto partial = at::empty({nchunks, E * H}, x.options().dtype(at::kFloat));
   auto stream = at::cuda::getCurrentCUDAStream();
   auto xp = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
@@ -293,7 +296,7 @@ at::Tensor router_input_weight_grad(const at::Tensor& x, const at::Tensor& wr, c
     auto kern = router_dgrad_kernel<NV, EV>;                                                         \
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);                  \
     kern<<<blocks, 256, smem, stream>>>(wp, dlogits.data_ptr<float>(), dxp, T, peer_lo, peer_hi, xc); \
-    if (T > 0) router_wgrad_kernel<EV><<<nchunks, 256, 0, stream>>>(xp, dlogits.data_ptr<float>(), T, H, partial.data_ptr<float>()); \
+    if (T > 0) router_wgrad_kernel<EV><<<nchunks, 256, 0, stream>>>(xp, dlogits.data_ptr<float>(), T, H, partial.data_ptr<float>(), chunk); \
   }
   if (H == 1024 && E == 16) SB_R(4, 16)
   else if (H == 1024 && E == 8) SB_R(4, 8)

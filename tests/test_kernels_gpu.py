@@ -156,7 +156,8 @@ def test_rope_roundtrip_and_reference():
 
 
 # ----------------------------------------------------------------------------- attention
-@pytest.mark.parametrize("B,S,Hq,Hkv", [(2, 128, 4, 2), (1, 256, 16, 4)])
+# small grids take the head-split dK/dV path, (8, 1024, 16, 4) the direct one
+@pytest.mark.parametrize("B,S,Hq,Hkv", [(2, 128, 4, 2), (1, 256, 16, 4), (8, 1024, 16, 4)])
 def test_attention_fwd_bwd(B, S, Hq, Hkv):
     torch.manual_seed(7)
     D = 64

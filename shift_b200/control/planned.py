@@ -124,23 +124,28 @@ class PlannedSession:
         self.lighthouses.append(p)
         self.log("lighthouse_started", port=port)
 
-    def launch(self, role: str):
+    def launch(self, role: str, name: str | None = None, generation: int | None = None, round_: int = 0,
+               extra=()):
+        """Launch one replica process tree.  ``name`` is the physical process
+        (A, B or C; in a rotation the spare alternates between C and B);
+        ``role`` its protocol role at launch."""
+        name = name or role
         rid = 0 if role == "A" else 1
-        gen = 1 if role == "C" else 0
+        gen = (1 if role == "C" else 0) if generation is None else generation
         env = dict(os.environ)
         env["PYTHONPATH"] = str(Path(__file__).resolve().parents[2]) + os.pathsep + env.get("PYTHONPATH", "")
         env["SHIFT_RESULT_DIR"] = str(self.dir)
-        env["SHIFT_STORE_PORT"] = str(self.store_base + 20 * {"A": 0, "B": 1, "C": 2}[role])
+        env["SHIFT_STORE_PORT"] = str(self.store_base + 20 * {"A": 0, "B": 1, "C": 2}[name])
         env.setdefault("NCCL_NVLS_ENABLE", "0")
         cmd = [sys.executable, "-m", "shift_b200.control.launch", "--nproc", str(self.nproc), "--master-port",
-               str(self.master_base + 10 * {"A": 0, "B": 1, "C": 2}[role]), "--module", "shift_b200.ft.planned_train"]
-        if role in self.devices:
-            cmd += ["--devices", ",".join(str(d) for d in self.devices[role])]
+               str(self.master_base + 10 * {"A": 0, "B": 1, "C": 2}[name]), "--module", "shift_b200.ft.planned_train"]
+        if name in self.devices:
+            cmd += ["--devices", ",".join(str(d) for d in self.devices[name])]
         cmd += ["--", "--session", self.name, "--replica", str(rid), "--generation", str(gen), "--root",
-                str(self.root), "--planned-role", role, *self.train_args]
-        log = (self.dir / f"role_{role}.log").open("w")
-        self.procs[role] = sp.Popen(cmd, env=env, stdout=log, stderr=sp.STDOUT)
-        self.log("launched", role=role, pid=self.procs[role].pid)
+                str(self.root), "--planned-role", role, "--planned-round", str(round_), *self.train_args, *extra]
+        log = (self.dir / f"role_{name}_g{gen}.log").open("w")
+        self.procs[name] = sp.Popen(cmd, env=env, stdout=log, stderr=sp.STDOUT)
+        self.log("launched", role=role, name=name, generation=gen, round=round_, pid=self.procs[name].pid)
 
     def commits(self, rid, gen, rank=0):
         return self.reader.rows("commit", rid=rid, generation=gen, rank=rank)
@@ -186,6 +191,44 @@ class PlannedSession:
             self.wait("ac_target", lambda: any(c["step"] >= target for c in self.commits(1, 1)), 600)
         return self.finish({"cut": cut, "t_request": t_request, "post_steps": post_steps})
 
+    def run_cycles(self, cycles=3, post_steps=6):
+        """Continuous B/C rotation: ``cycles`` consecutive planned handoffs.
+        Round r hands replica 1 from the process that won round r-1 (or B) to
+        a freshly launched spare (physical C in even rounds, a relaunched B in
+        odd ones), epoch r -> r+1; ``post_steps`` committed steps follow each
+        cut before the next request."""
+        n = self.nproc
+        extra = ["--planned-cycles", str(cycles)]
+        self.start_lighthouse(self.lh_port)
+        self.launch("A", extra=extra)
+        self.launch("B", extra=extra)
+        self.wait("ab_ready", lambda: len(self.rows("ready", generation=0)) == 2 * n, 300)
+        atomic_write(self.dir / "START", "")
+        self.wait("ab_two_steps", lambda: all(any(c["step"] >= 2 for c in self.commits(r, 0)) for r in (0, 1)))
+        cuts, t_requests = [], []
+        for r in range(cycles):
+            spare = "C" if r % 2 == 0 else "B"
+            if spare in self.procs:                         # the previous owner of that name has retired
+                self.wait(f"retired_{spare}_{r}", lambda: self.procs[spare].poll() is not None, 300)
+            pre = f"round/{r}/" if r else ""
+            t_requests.append(time.time())
+            self.log("REQUEST", variant=self.variant, round=r)
+            self.launch("C", name=spare, generation=r + 1, round_=r, extra=extra)
+            self.key(pre + "request")
+            self.start_lighthouse(self.lh_port + 10 * (r + 1))
+            if self.variant == "p2":
+                self.start_lighthouse(self.lh_port + 10 * (r + 1) + 1)
+            self.wait(f"c_local_ready_{r}", lambda: len(self.rows("planned_local_ready", generation=r + 1)) == n)
+            self.key(pre + "arm")
+            cut = self.wait(f"cut_selected_{r}", lambda: [x for x in self.rows("planned_cut_selected", rid=0)
+                                                         if x.get("round", 0) == r])[-1]["step"]
+            cuts.append(cut)
+            target = cut + post_steps
+            if r == cycles - 1:
+                atomic_write(self.dir / "TRAIN_UNTIL", str(target))
+            self.wait(f"post_steps_{r}", lambda: any(c["step"] >= target for c in self.commits(0, 0)), 600)
+        return self.finish({"cuts": cuts, "t_requests": t_requests, "post_steps": post_steps, "cycles": cycles})
+
     def finish(self, info):
         atomic_write(self.dir / "STOP", "")
         for role, p in self.procs.items():
@@ -204,8 +247,52 @@ class PlannedSession:
         return summary
 
 
+def summarize_cycles(reader, variant, info, nproc=1) -> dict:
+    """Per-round handoff interval, exposed transfer time and audits of a rotation."""
+    rows = reader.all_rows
+    a0 = sorted((r for r in rows if r["kind"] == "commit" and r["rid"] == 0 and r["rank"] == 0),
+                key=lambda r: r["step"])
+    by_step = {r["step"]: r for r in a0}
+    cuts = info["cuts"]
+    normal = [b["time"] - a["time"] for a, b in zip(a0, a0[1:])
+              if b["step"] == a["step"] + 1 and all(not (c <= a["step"] <= c + 1) for c in cuts)]
+    med = sorted(normal)[len(normal) // 2] if normal else 0.0
+    out = {"variant": variant, **info, "normal_step_s": med, "rounds": []}
+    checks = {}
+    for r, cut in enumerate(cuts):
+        gen = r + 1
+        rd = {"round": r, "cut": cut}
+        if cut in by_step and cut + 1 in by_step:
+            rd["handoff_interval_s"] = by_step[cut + 1]["time"] - by_step[cut]["time"]
+            rd["exposed_transfer_s"] = rd["handoff_interval_s"] - med
+        recv = [x for x in rows if x["kind"] == "commit" and x["rid"] == 1 and x["generation"] == gen]
+        exact, compared = True, 0
+        for c in recv:
+            a = next((x for x in a0 if x["step"] == c["step"] and x["rank"] == c["rank"]), None)
+            if a and a.get("hashes") and c.get("hashes"):
+                compared += 1
+                for k in ("model", "optimizer", "scheduler"):
+                    exact &= a["hashes"].get(k) == c["hashes"].get(k)
+        restored = [x for x in rows if x["kind"] == "restored" and x["generation"] == gen]
+        rd["compared_commits"] = compared
+        checks[f"round{r}_state_exact"] = {"pass": exact and compared > 0, "compared": compared}
+        checks[f"round{r}_restore_hashes_match"] = {"pass": bool(restored) and all(x["hashes_match"]
+                                                                                  for x in restored)}
+        if variant == "p2":
+            rel = [x for x in rows if x["kind"] == "planned_gradient_received" and x["generation"] == gen]
+            checks[f"round{r}_gradient_relay"] = {"pass": len(rel) >= nproc and all(
+                x.get("forward_calls") == 0 for x in rel)}
+        out["rounds"].append(rd)
+    checks["monotonic_a"] = {"pass": all(b["step"] == a["step"] + 1 for a, b in zip(a0, a0[1:]))}
+    out["checks"] = checks
+    out["pass"] = all(c["pass"] for c in checks.values())
+    return out
+
+
 def summarize(reader, variant, info, nproc=1) -> dict:
     """Handoff interval and audit checks from a session's events."""
+    if "cuts" in info:
+        return summarize_cycles(reader, variant, info, nproc)
     rows = reader.all_rows
     a0 = [r for r in rows if r["kind"] == "commit" and r["rid"] == 0 and r["rank"] == 0 and r["generation"] == 0]
     checks = {}
@@ -267,6 +354,7 @@ def main(argv=None):
                     choices=["healthy", "prepare-fail", "ready-timeout", "stale-state", "relay-reject", "slow-compute"])
     ap.add_argument("--post-steps", type=int, default=3)
     ap.add_argument("--cancel", action="store_true")
+    ap.add_argument("--cycles", type=int, default=1, help="consecutive B/C rotation rounds (1 = one handoff)")
     ap.add_argument("--model", default="tiny")
     ap.add_argument("--device", default="cpu")
     ap.add_argument("--nproc", type=int, default=1)
@@ -280,7 +368,7 @@ def main(argv=None):
     import shlex
     s = PlannedSession(a.root, a.name, a.variant, a.scenario, a.model, a.device, a.nproc, devices=devices,
                        train_args=shlex.split(a.train_args))
-    res = s.run(a.post_steps, a.cancel)
+    res = s.run_cycles(a.cycles, a.post_steps) if a.cycles > 1 else s.run(a.post_steps, a.cancel)
     print(json.dumps({k: v for k, v in res.items() if k != "checks"}, indent=1, default=str))
     print(json.dumps({k: v["pass"] for k, v in res.get("checks", {}).items()}, indent=1))
     return 0 if res.get("pass") else 1

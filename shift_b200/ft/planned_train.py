@@ -38,6 +38,8 @@ def parse_args(argv=None):
                                 "slow-compute"])
     extra.add_argument("--planned-slow-ms", type=float, default=250)
     extra.add_argument("--planned-round", type=int, default=0)
+    extra.add_argument("--planned-cycles", type=int, default=1,
+                       help="rotation: rounds of the experiment; a process serves rounds [planned-round, cycles)")
     extra.add_argument("--coord", required=True)
     extra.add_argument("--lighthouse-host", default="127.0.0.1")
     extra.add_argument("--lighthouse-port", type=int, required=True)
@@ -54,6 +56,7 @@ class PlannedWorker(Worker):
         super().__init__(args)
         self.role = args.planned_role
         self.logical_rid = 0 if self.role == "A" else 1
+        self.round = args.planned_round
         self.forward_calls = 0
 
     def manifest(self):
@@ -133,7 +136,7 @@ class PlannedWorker(Worker):
 
     def make_manager(self, epoch: int, members: str = "AB", activate: bool = True):
         a = self.args
-        port = a.lighthouse_port + 10 * epoch + (1 if members == "AB" and epoch > a.planned_round else 0)
+        port = a.lighthouse_port + 10 * epoch + (1 if members == "AB" and epoch > self.round else 0)
         if self.device.type == "cuda":
             # fused peer-memory reduction + IPC healing: a new epoch only re-maps handles
             from .fused import PeerStateTransport
@@ -207,16 +210,7 @@ class PlannedWorker(Worker):
         self.engine.scheduler._last_lr = [a.lr]
         if cuda:
             self.ensure_reducer()
-        prefix = f"round/{a.planned_round}" if a.planned_round else ""
-        self.coord = Coordinator(a.coord, prefix)
-        mover = a.mover if a.mover != "auto" else ("ipc" if cuda else "packed")
-        cls = OverlapHandoff if a.planned_variant == "p2" else PlannedHandoff
-        hooks = [self.premap_k1, self.warmup_spare, self.precreate_manager] if cuda else [self.precreate_manager]
-        self.handoff = cls(self.role, a.planned_variant, self.rank, self.local_world, self.coord, self.event,
-                           self.export_state, self.load_state, self.progress, self.manifest, self.device, mover,
-                           round_=a.planned_round, source=a.planned_source, inject=a.planned_inject,
-                           engine=self.engine, prepare_hooks=hooks)
-        self.handoff.rng_tail = self.rng_tail
+        self.handoff = self.new_handoff(self.round)
         self.transport_on_cpu = False
         base_epoch = a.planned_round
         if self.role == "C":
@@ -229,6 +223,7 @@ class PlannedWorker(Worker):
             self.manager = self.take_manager(base_epoch + 1, "AC")
             self.manager.load_state_dict({"step": self.progress["updates"]})
             self.event("planned_epoch_activated", step=self.progress["updates"], epoch=base_epoch + 1)
+            self._advance_pending = True
         else:
             self.manager = self.make_manager(base_epoch, "AB")
             self.event("ready", role=self.role, planned_variant=a.planned_variant,
@@ -239,6 +234,39 @@ class PlannedWorker(Worker):
                     raise RuntimeError("Stopped or timed out before START")
                 time.sleep(0.02)
         self.loop_planned(time.monotonic() + a.max_seconds)
+
+    def new_handoff(self, round_: int):
+        """The handoff protocol object of one rotation round (keys under
+        ``round/<r>/`` of the coordination store, epochs r -> r+1)."""
+        a = self.args
+        cuda = self.device.type == "cuda"
+        self.coord = Coordinator(a.coord, f"round/{round_}" if round_ else "")
+        mover = a.mover if a.mover != "auto" else ("ipc" if cuda else "packed")
+        cls = OverlapHandoff if a.planned_variant == "p2" else PlannedHandoff
+        hooks = [self.premap_k1, self.warmup_spare, self.precreate_manager] if cuda else [self.precreate_manager]
+        emit = lambda kind, **kw: self.event(kind, round=round_, **kw)   # noqa: E731
+        h = cls(self.role, a.planned_variant, self.rank, self.local_world, self.coord, emit,
+                self.export_state, self.load_state, self.progress, self.manifest, self.device, mover,
+                round_=round_, source=a.planned_source, inject=a.planned_inject if round_ == a.planned_round else
+                "healthy", engine=self.engine, prepare_hooks=hooks)
+        h.rng_tail = self.rng_tail
+        return h
+
+    def advance_round(self):
+        """Continuous rotation (the reference's ``advance_round``): once epoch
+        r+1 is active, the next round starts -- A stays A, the replica-1
+        process that just took over becomes the donor B of round r+1, and a
+        freshly launched spare will be its C."""
+        if self.round + 1 >= self.args.planned_cycles:
+            return
+        self.round += 1
+        if self.role == "C":
+            self.role = "B"
+        # the finished round still tracks its post-cut commits (the retired
+        # donor of that round waits for them before it exits)
+        self.prev_handoff = self.handoff
+        self.handoff = self.new_handoff(self.round)
+        self.event("planned_round_advanced", round=self.round, role=self.role, step=self.progress["updates"])
 
     def requested_stop(self):
         if super().requested_stop():
@@ -263,6 +291,8 @@ class PlannedWorker(Worker):
                     mgr.load_state_dict({"step": self.progress["updates"]})
                     self.event("planned_epoch_activated", step=self.progress["updates"],
                                epoch=self.handoff.gate.epoch)
+                    self.manager = mgr
+                    self._advance_pending = True
                 self.manager = mgr
             mgr = self.manager
             mgr.start_quorum()
@@ -284,12 +314,16 @@ class PlannedWorker(Worker):
                 if a.planned_inject == "slow-compute":
                     time.sleep(a.planned_slow_ms / 1000.0)
             if relay:
+                old_mgr = mgr
                 mgr, retired = self.handoff.at_gradient(mgr, eng.store.grad, self.take_manager, sample_ids,
                                                         self.apply_tail)
                 if retired:
                     self.event("stopped", step=self.progress["updates"], role=self.role, retired=True)
                     self.event.close()
                     return
+                if mgr is not old_mgr and self.handoff.gate.epoch > self.handoff.base_epoch and \
+                        not getattr(self.handoff, "fallback", False):
+                    self._advance_pending = True       # A activated the new epoch inside the relay step
                 self.manager = mgr
                 self.event("planned_ac_outer_begin", step=step)
             if fused:
@@ -312,6 +346,12 @@ class PlannedWorker(Worker):
                            global_batch=a.batch * a.microbatches * mgr.num_participants(),
                            **self.handoff.commit_fields(mgr))
                 self.handoff.committed()
+                if getattr(self, "prev_handoff", None) is not None:
+                    self.prev_handoff.committed()
+                if getattr(self, "_advance_pending", False):
+                    # the next rotation round starts after the first commit of the new epoch
+                    self._advance_pending = False
+                    self.advance_round()
             else:
                 self.event("skipped", step=step, error=str(mgr.errored()))
         self.event("stopped", step=self.progress["updates"], attempts=attempts, role=self.role)

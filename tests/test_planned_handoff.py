@@ -48,3 +48,16 @@ def test_prepare_failure_cancels_and_old_epoch_continues(tmp_path):
     s = PlannedSession(tmp_path, "pf", variant="p1f", scenario="prepare-fail")
     res = s.run(post_steps=3)
     assert res["cancelled"] and res["pass"]
+
+
+@pytest.mark.parametrize("variant", ["p1f", "p2"])
+def test_three_rotation_cycles_with_audits(tmp_path, variant):
+    """Continuous B/C rotation: three consecutive planned handoffs (B -> C,
+    C -> relaunched B, B -> relaunched C), six post-steps each; every round's
+    receiver is bit-exact with A and restored the donor's hashes."""
+    s = PlannedSession(tmp_path, f"rot_{variant}", variant=variant)
+    res = s.run_cycles(cycles=3, post_steps=6)
+    failed = {k: v for k, v in res["checks"].items() if not v["pass"]}
+    assert res["pass"], failed
+    assert len(res["rounds"]) == 3 and all(r.get("handoff_interval_s", 0) > 0 for r in res["rounds"])
+    assert all(rc == 0 for rc in res["returncodes"].values()), res["returncodes"]

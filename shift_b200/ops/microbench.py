@@ -1,6 +1,6 @@
 """Kernel micro-benchmarks at the shapes of the 0.494B MoE training step.
 
-    python -m shift_b200.ops.microbench [--ops gemm,attn,norm,moe,adam] [--iters N]
+    python -m shift_b200.ops.microbench [--ops gemm,attn,mem,fused] [--iters N]
 
 Each case is timed with CUDA events on the launching stream after warm-up,
 with a synchronize on both sides; inputs of the timed cases are larger than
@@ -186,6 +186,87 @@ def run_mem(iters, T=16384, H=1024):
     return rows
 
 
+def run_fused(iters):
+    """The fused compute+collective kernels on ONE GPU: every 'peer' buffer is
+    a second local tensor (the kernels only see addresses), so the numbers
+    are the kernels' own DRAM/tensor work; the NVLink share is measured in the
+    multi-GPU step timelines."""
+    from ..engine import StepBlock
+    from ._ext import ext, status_word
+    pk = peaks()
+    rows = []
+    dev = torch.device("cuda")
+    st = status_word(dev)
+    blk = StepBlock(dev)
+    blk.write(1, 1e-4, 0.9, 0.999, 1)
+    flags = torch.zeros(64, dtype=torch.int32, device=dev)
+    flags[0] = 1 << 30                                   # a peer flag that is always set
+    # ---- K1 two-phase: reduce-scatter a slice of two replicas' bf16 grads, then AdamW
+    n = 62_000_000                                       # one replica-rank's flat state at 2 x TP2 x PP2
+    g0, g1 = bf(n), bf(n)
+    red0, red1 = torch.empty_like(g0), torch.empty_like(g0)
+    master = torch.randn(n, device=dev)
+    m, v = torch.zeros(n, device=dev), torch.zeros(n, device=dev)
+    outs = [torch.empty_like(master) for _ in range(3)]
+    pb = torch.empty(n, device=dev, dtype=torch.bfloat16)
+    nf = torch.zeros(1, dtype=torch.int32, device=dev)
+    t = timeit(lambda: ext().reduce_slice_scatter([g0.data_ptr(), g1.data_ptr()], [red0.data_ptr(), red1.data_ptr()],
+                                                  0, n // 2, [], blk.dev, 0.5, st, 5.0), iters, warmup=_WARMUP)
+    nbytes = (n // 2) * 2 * (2 + 2)                     # read 2 sources, write 2 destinations (bf16)
+    rows.append({"case": f"K1.reduce_slice_scatter half of {n}", "ms": round(t, 4), "gbs": round(nbytes / t / 1e6, 1),
+                 "frac_of_peak": round(nbytes / t / 1e6 / pk["hbm_gbs"], 3)})
+    t = timeit(lambda: ext().fused_reduce_adamw([red0.data_ptr()], [], blk.dev, master, m, v, *outs, pb, 0.9, 0.999,
+                                                1e-8, 0.01, 1.0, nf, st, 5.0), iters, warmup=_WARMUP)
+    nbytes = n * (2 + 12 + 12 + 2)
+    rows.append({"case": f"K1.fused_reduce_adamw {n}", "ms": round(t, 4), "gbs": round(nbytes / t / 1e6, 1),
+                 "frac_of_peak": round(nbytes / t / 1e6 / pk["hbm_gbs"], 3)})
+    # ---- TP exchange forms at the 2 x TP2 shapes (8192 tokens per replica, hidden 1024)
+    T, H = 8192, 1024
+    half = T // 2
+    x, d1, d2 = bf(half, H), bf(half, H), bf(half, H)
+    w = bf(H, std=0.1) + 1
+    gA, gA_peer = bf(T, H), bf(T, H)
+    xc = [flags[0].data_ptr(), 0, flags[1].data_ptr(), flags[2].data_ptr(), 0, blk.dev.data_ptr(),
+          gA_peer[:half].data_ptr()]
+    t = timeit(lambda: Fn.rmsnorm_fwd(x, w, 1e-6, d1, delta2=d2, y_out=gA[:half], xchg=xc), iters, warmup=_WARMUP)
+    nbytes = half * H * 2 * (3 + 1 + 2)                   # x, d1, d2 in; h, y (local), y (peer) out
+    rows.append({"case": f"K2.rmsnorm_fwd+delta2+push {half}x{H}", "ms": round(t, 4),
+                 "gbs": round(nbytes / t / 1e6, 1), "frac_of_peak": round(nbytes / t / 1e6 / pk["hbm_gbs"], 3)})
+    wq = bf(768, H)
+    from . import gemm as Gm
+    xq = [flags[0].data_ptr(), 0, 0, 0, 0, blk.dev.data_ptr(), 0]
+    t = timeit(lambda: Gm.linear_fwd(gA, wq, xchg=xq, tp=(half, T, 0, 0, 0, 0)), iters, warmup=_WARMUP)
+    flops = 2.0 * T * 768 * H
+    rows.append({"case": f"K2.qkv GEMM (gathered A, peer wait) {T}x768x{H}", "ms": round(t, 4),
+                 "tflops": round(flops / t / 1e9, 1), "frac_of_peak": round(flops / t / 1e9 / pk["bf16_tflops"], 3)})
+    o, wo = bf(T, 512), bf(H, 512)
+    own, peer = torch.empty(half, H, dtype=torch.bfloat16, device=dev), torch.empty(half, H, dtype=torch.bfloat16,
+                                                                                     device=dev)
+    xo = [0, 0, flags[3].data_ptr(), flags[4].data_ptr(), 0, blk.dev.data_ptr(), peer.data_ptr()]
+    t = timeit(lambda: Gm.linear_fwd(o, wo, out=own, xchg=xo, tp=(0, 0, half // 128, half, T, 0)), iters,
+               warmup=_WARMUP)
+    flops = 2.0 * T * H * 512
+    rows.append({"case": f"K3.o-proj GEMM -> peer rows {T}x{H}x512", "ms": round(t, 4),
+                 "tflops": round(flops / t / 1e9, 1), "frac_of_peak": round(flops / t / 1e9 / pk["bf16_tflops"], 3)})
+    # ---- K4 combine with peer-row stores (8 local experts of 16, top-4)
+    k = 4
+    R = T * k // 2
+    y = bf(R, H)
+    pos = torch.randint(0, R, (T, k), device=dev, dtype=torch.int32)
+    pos[torch.rand(T, k, device=dev) < 0.5] = -1
+    wts = torch.rand(T, k, device=dev)
+    cown = torch.empty(half, H, dtype=torch.bfloat16, device=dev)
+    cpeer = torch.empty(half, H, dtype=torch.bfloat16, device=dev)
+    xcmb = [0, 0, flags[5].data_ptr(), flags[6].data_ptr(), 0, blk.dev.data_ptr(), cpeer.data_ptr()]
+    t = timeit(lambda: Fn.combine(y, pos, wts, T, cown, (half, T, 0), xcmb), iters, warmup=_WARMUP)
+    nbytes = R * H * 2 + T * H * 2
+    rows.append({"case": f"K4.combine -> peer rows T{T} k{k}", "ms": round(t, 4), "gbs": round(nbytes / t / 1e6, 1),
+                 "frac_of_peak": round(nbytes / t / 1e6 / pk["hbm_gbs"], 3)})
+    torch.cuda.synchronize()
+    assert int(st[0]) == 0, f"status word {int(st[0])}"
+    return rows
+
+
 def main():
     p = argparse.ArgumentParser()
     p.add_argument("--ops", default="gemm,attn,mem")
@@ -204,6 +285,8 @@ def main():
         out["attn"] = run_attn(args.iters)
     if "mem" in ops:
         out["mem"] = run_mem(args.iters)
+    if "fused" in ops:
+        out["fused"] = run_fused(args.iters)
     for k, v in out.items():
         if isinstance(v, list):
             for r in v:

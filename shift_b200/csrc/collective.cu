@@ -68,7 +68,12 @@ SB_DEVICE void load_step(const int* sdev, int& tag, AdamHyper& a) {
   a.bc2_sqrt = __int_as_float(sdev[3]);
 }
 
-__global__ void __launch_bounds__(256)
+// NS: compile-time bound on the number of sources (registers scale with it).
+// With one source (the two-phase form's local reduced buffer, or a replica
+// alone) loads go through L2 only; with several, the sources are peers'
+// memory and are read as volatile (never from a stale cache line).
+template <int NS>
+__global__ void __launch_bounds__(256, NS <= 2 ? 3 : 2)
 fused_reduce_adamw_kernel(SrcPtrs src, int n_src, FlagPtrs flags, int n_flags, const int* __restrict__ sdev,
                           const float* __restrict__ master, const float* __restrict__ m_in,
                           const float* __restrict__ v_in, float* __restrict__ master_out, float* __restrict__ m_out,
@@ -83,15 +88,16 @@ fused_reduce_adamw_kernel(SrcPtrs src, int n_src, FlagPtrs flags, int n_flags, c
     if (i + 8 <= n) {
       float g[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       // issue all peer loads first (they travel over NVLink), then reduce in order
-      bf16x8 raw[kMaxSrc];
+      bf16x8 raw[NS];
 #pragma unroll
-      for (int s = 0; s < kMaxSrc; ++s)
+      for (int s = 0; s < NS; ++s)
         if (s < n_src) {
-          const uint4 u = __ldcv(reinterpret_cast<const uint4*>(src.p[s] + i));
+          const uint4 u = NS == 1 ? __ldcg(reinterpret_cast<const uint4*>(src.p[s] + i))
+                                  : __ldcv(reinterpret_cast<const uint4*>(src.p[s] + i));
           raw[s].w[0] = u.x; raw[s].w[1] = u.y; raw[s].w[2] = u.z; raw[s].w[3] = u.w;
         }
 #pragma unroll
-      for (int s = 0; s < kMaxSrc; ++s) {
+      for (int s = 0; s < NS; ++s) {
         if (s < n_src) {
           float f[8];
           bf16x8_to_float(raw[s], f);
@@ -157,6 +163,7 @@ struct DstPtrs {
   __nv_bfloat16* p[kMaxSrc];
 };
 
+template <int NS>
 __global__ void __launch_bounds__(256)
 reduce_slice_scatter_kernel(SrcPtrs src, int n_src, DstPtrs dst, int n_dst, long lo, long hi, FlagPtrs flags,
                             int n_flags, const int* __restrict__ sdev, float scale, int* __restrict__ status,
@@ -166,16 +173,16 @@ reduce_slice_scatter_kernel(SrcPtrs src, int n_src, DstPtrs dst, int n_dst, long
   const long stride = static_cast<long>(gridDim.x) * blockDim.x * 8;
   for (long i = lo + (static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x) * 8; i < hi; i += stride) {
     if (i + 8 <= hi) {
-      bf16x8 raw[kMaxSrc];
+      bf16x8 raw[NS];
 #pragma unroll
-      for (int s = 0; s < kMaxSrc; ++s)
+      for (int s = 0; s < NS; ++s)
         if (s < n_src) {
           const uint4 u = __ldcv(reinterpret_cast<const uint4*>(src.p[s] + i));
           raw[s].w[0] = u.x; raw[s].w[1] = u.y; raw[s].w[2] = u.z; raw[s].w[3] = u.w;
         }
       float g[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int s = 0; s < kMaxSrc; ++s)
+      for (int s = 0; s < NS; ++s)
         if (s < n_src) {
           float f[8];
           bf16x8_to_float(raw[s], f);
@@ -197,7 +204,9 @@ reduce_slice_scatter_kernel(SrcPtrs src, int n_src, DstPtrs dst, int n_dst, long
       }
     }
   }
-  __threadfence_system();
+  // publish the remote stores (one cumulative system fence per CTA)
+  __syncthreads();
+  if (threadIdx.x == 0) __threadfence_system();
 }
 
 // ---------------------------------------------------------------------------
@@ -376,11 +385,18 @@ void fused_reduce_adamw(const std::vector<int64_t>& grad_ptrs, const std::vector
   const long n = master.numel();
   if (n == 0) return;
   const long blocks = std::min<long>((n / 8 + 255) / 256 + 1, static_cast<long>(sm_count()) * 8);
-  fused_reduce_adamw_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      src, static_cast<int>(grad_ptrs.size()), f, static_cast<int>(flag_ptrs.size()), step_dev.data_ptr<int>(),
-      master.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), master_out.data_ptr<float>(),
-      m_out.data_ptr<float>(), v_out.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(param_out.data_ptr()), n, a,
-      nonfinite.data_ptr<int>(), status.data_ptr<int>(), static_cast<uint64_t>(timeout_s * 1e9));
+  const int ns = static_cast<int>(grad_ptrs.size());
+#define SB_K1(NS)                                                                                              \
+  fused_reduce_adamw_kernel<NS><<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(                          \
+      src, ns, f, static_cast<int>(flag_ptrs.size()), step_dev.data_ptr<int>(), master.data_ptr<float>(),       \
+      m.data_ptr<float>(), v.data_ptr<float>(), master_out.data_ptr<float>(), m_out.data_ptr<float>(),          \
+      v_out.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(param_out.data_ptr()), n, a,                     \
+      nonfinite.data_ptr<int>(), status.data_ptr<int>(), static_cast<uint64_t>(timeout_s * 1e9))
+  if (ns == 1) SB_K1(1);
+  else if (ns == 2) SB_K1(2);
+  else if (ns <= 4) SB_K1(4);
+  else SB_K1(8);
+#undef SB_K1
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -398,10 +414,16 @@ void reduce_slice_scatter(const std::vector<int64_t>& src_ptrs, const std::vecto
   for (size_t i = 0; i < dst_ptrs.size(); ++i) d.p[i] = reinterpret_cast<__nv_bfloat16*>(dst_ptrs[i]);
   const long n = hi - lo;
   const long blocks = std::max<long>(1, std::min<long>((n / 8 + 255) / 256 + 1, static_cast<long>(sm_count()) * 4));
-  reduce_slice_scatter_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      s, static_cast<int>(src_ptrs.size()), d, static_cast<int>(dst_ptrs.size()), lo, hi, make_flags(flag_ptrs),
-      static_cast<int>(flag_ptrs.size()), step_dev.data_ptr<int>(), static_cast<float>(scale),
-      status.data_ptr<int>(), static_cast<uint64_t>(timeout_s * 1e9));
+  const int ns = static_cast<int>(src_ptrs.size());
+#define SB_RS(NS)                                                                                           \
+  reduce_slice_scatter_kernel<NS><<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(                     \
+      s, ns, d, static_cast<int>(dst_ptrs.size()), lo, hi, make_flags(flag_ptrs),                           \
+      static_cast<int>(flag_ptrs.size()), step_dev.data_ptr<int>(), static_cast<float>(scale),              \
+      status.data_ptr<int>(), static_cast<uint64_t>(timeout_s * 1e9))
+  if (ns <= 2) SB_RS(2);
+  else if (ns <= 4) SB_RS(4);
+  else SB_RS(8);
+#undef SB_RS
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -348,11 +348,13 @@ SB_DEVICE bool xchg_wait_cta(const Xchg& x, int* status) {
 }
 
 // Called by EVERY thread of every CTA after its last store of the kernel.
+// The CTA barrier orders every thread's stores before thread 0's system-scope
+// fence (fences are cumulative), so one fence per CTA publishes them all.
 SB_DEVICE void xchg_signal(const Xchg& x) {
   if (x.sig_flag == nullptr) return;
-  __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) {
+    __threadfence_system();
     const int prev = atomicAdd(x.sig_counter, 1);
     if (prev == static_cast<int>(gridDim.x * gridDim.y * gridDim.z) - 1) {
       atomicExch(x.sig_counter, 0);

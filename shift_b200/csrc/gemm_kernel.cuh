@@ -293,12 +293,19 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       // tile's accumulator slab (32 rows x 64 columns per warp) is converted
       // and written to swizzled shared memory, then one lane stores it with
       // TMA: whole 128-byte row segments instead of one row per thread.
+      // Tiles owned by the tensor-parallel peer take the same staging but
+      // leave through coalesced SM stores into the peer's receive buffer
+      // (whole 512-byte row runs per warp instruction, over NVLink).
       const bool tile_to_peer = p.xc.peer_out != nullptr && t.out_row0 >= p.peer_lo && t.out_row0 < p.peer_hi;
-      const bool tma_ok = p.use_tma_store && !tile_to_peer && t.kb > 0 &&
-                          (t.m_valid == BM || t.out_row0 - p.d_row_off + t.m_valid >= p.d_rows) &&
-                          (p.epi == kEpiBF16 || (p.epi == kEpiSwiGLU && C::kD2Staged));
+      const bool tma_ok = t.kb > 0 &&
+                          ((p.use_tma_store && !tile_to_peer &&
+                            (t.m_valid == BM || t.out_row0 - p.d_row_off + t.m_valid >= p.d_rows) &&
+                            (p.epi == kEpiBF16 || (p.epi == kEpiSwiGLU && C::kD2Staged))) ||
+                           (tile_to_peer && p.epi == kEpiBF16 && (p.ldd % 8) == 0));
       if (tma_ok) {
-        const int drow0 = t.out_row0 - p.d_row_off + quarter * 32;
+        const int drow0 = tile_to_peer ? t.out_row0 - p.peer_lo + quarter * 32
+                                       : t.out_row0 - p.d_row_off + quarter * 32;
+        const int rows_here = min(32, t.m_valid - quarter * 32);
         uint8_t* wbuf = epi_stage + (warp - 2) * C::kEpiWarpBytes;
         const int nslabs = min(BN, p.N - t.n0 + 63) / 64;
 #pragma unroll 1
@@ -337,6 +344,21 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
 #pragma unroll
             for (int j = 0; j < 4; ++j)
               *reinterpret_cast<bf16x8*>(bd2 + lane * 64 + ((j ^ ((lane >> 1) & 3)) * 16)) = float_to_bf16x8(a + 8 * j);
+          }
+          if (tile_to_peer) {
+            __syncwarp();
+            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.xc.peer_out);
+            const int col_lim = p.N - (t.n0 + c);
+#pragma unroll
+            for (int it = 0; it < 8; ++it) {
+              const int ch = it * 32 + lane;        // 16-byte chunk of the warp's 32 x 128 B slab
+              const int rr = ch >> 3, j = ch & 7;
+              if (rr < rows_here && j * 8 < col_lim)
+                *reinterpret_cast<uint4*>(dst + static_cast<long>(drow0 + rr) * p.ldd + t.n0 + c + j * 8) =
+                    *reinterpret_cast<const uint4*>(bd + rr * 128 + ((j ^ (rr & 7)) * 16));
+            }
+            __syncwarp();
+            continue;
           }
           fence_proxy_async_smem();
           __syncwarp();

@@ -44,7 +44,12 @@ namespace fa {
 constexpr int D = 64;
 constexpr int BM = 128;
 constexpr int BN = 128;
-constexpr int kThreads = 192;
+// warp 0: TMA producer, warp 1: TMEM owner + MMA issuer, warps 2..9: softmax /
+// epilogue.  Two softmax warps share each TMEM lane quarter (warp % 4) and
+// split the 128 columns of a tile (half = (warp - 2) / 4), which halves the
+// per-thread exponent/convert/store stream that bounds these kernels.
+constexpr int kThreads = 320;
+constexpr int kSoftThreads = 256;
 constexpr int kTile = 128 * 128;   // bytes of one 128 x 64 bf16 tile
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -81,7 +86,8 @@ SB_DEVICE void named_bar(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(
 
 // ============================ forward ============================
 constexpr int kFwdStages = 2;
-constexpr int kFwdSmem = 1024 + kTile /*Q*/ + 2 * kFwdStages * kTile /*K,V*/ + 2 * 2 * kTile /*P x2*/ + 256;
+constexpr int kFwdSmem = 1024 + kTile /*Q*/ + 2 * kFwdStages * kTile /*K,V*/ + 2 * 2 * kTile /*P x2*/ + 256 +
+                         (2 * 2 * 128 + 2 * 128) * 4 /*row max / sum exchange*/;
 
 __global__ void __launch_bounds__(kThreads, 1)
 fwd_kernel(const __grid_constant__ CUtensorMap tm, Params p) {
@@ -101,6 +107,10 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm, Params p) {
   uint64_t* o_full = p_full + 2;
   uint64_t* drain = o_full + 2;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(drain + 1);
+  // row-max exchange between the two softmax warps of a lane quarter,
+  // double-buffered by block parity: [parity][half][row]; then the row sums
+  float* s_max = reinterpret_cast<float*>(tslot + 4);
+  float* s_sum = s_max + 2 * 2 * BM;
 
   const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int kvh = h / (p.Hq / p.Hkv);
@@ -117,7 +127,7 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm, Params p) {
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 128);
+      mbar_init(&p_full[i], kSoftThreads);
       mbar_init(&o_full[i], 1);
     }
     mbar_init(drain, 1);
@@ -183,42 +193,41 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm, Params p) {
   } else {
     // ----------------------------- softmax -----------------------------
     const int quarter = warp % 4;
+    const int half = (warp - 2) / 4;          // columns [64*half, 64*half+64) of S, [32*half, +32) of O
     const int row = quarter * 32 + lane;
     const int q = q0 + row;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const int pair_bar = 1 + quarter;         // named barrier of the two warps of this quarter
     float m_run = -INFINITY, l_run = 0.f, m_fold = -INFINITY;
-    float o_acc[D];
+    float o_acc[D / 2];
 #pragma unroll
-    for (int i = 0; i < D; ++i) o_acc[i] = 0.f;
+    for (int i = 0; i < D / 2; ++i) o_acc[i] = 0.f;
     bool ok = true;
     auto fold = [&](int i, float m_i) -> bool {
       if (!mbar_wait(&o_full[i & 1], (i >> 1) & 1, p.status)) return false;
       tc_fence_after();
       const float a = (m_fold == -INFINITY) ? 0.f : ex2(m_fold - m_i);
       uint32_t v[32];
+      tmem_ld_32x32b_x32(tbase + 256 + (i & 1) * D + half * 32 + lane_off, v);
+      tmem_wait_ld();
 #pragma unroll
-      for (int c = 0; c < D; c += 32) {
-        tmem_ld_32x32b_x32(tbase + 256 + (i & 1) * D + c + lane_off, v);
-        tmem_wait_ld();
-#pragma unroll
-        for (int t = 0; t < 32; ++t) o_acc[c + t] = o_acc[c + t] * a + __uint_as_float(v[t]);
-      }
+      for (int t = 0; t < 32; ++t) o_acc[t] = o_acc[t] * a + __uint_as_float(v[t]);
       m_fold = m_i;
       return true;
     };
-    for (int j = 0; j < n_kv && ok; ++j) {
-      if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1, p.status)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
+    // Both warps of a pair run every iteration's named barrier even after a
+    // bounded wait failed (they then skip the work), so a failure in one warp
+    // can never leave its partner blocked on the barrier.
+    for (int j = 0; j < n_kv; ++j) {
+      if (ok && !mbar_wait(&s_full[j & 1], (j >> 1) & 1, p.status)) ok = false;
+      if (ok) tc_fence_after();
       const uint32_t ts = tbase + (j & 1) * BN + lane_off;
       const bool diag = (j == qb);
-      // pass 1: row max
+      // pass 1: row max over this warp's 64 columns, combined with the partner's
       float mx = m_run;
       uint32_t v[32];
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
+      for (int c = half * 64; ok && c < half * 64 + 64; c += 32) {
         tmem_ld_32x32b_x32(ts + c, v);
         tmem_wait_ld();
 #pragma unroll
@@ -228,13 +237,17 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm, Params p) {
           mx = fmaxf(mx, s);
         }
       }
+      s_max[((j & 1) * 2 + half) * BM + row] = mx;
+      named_bar(pair_bar, 64);
+      if (!ok) continue;
+      mx = fmaxf(mx, s_max[((j & 1) * 2 + (half ^ 1)) * BM + row]);
       const float m_prev = m_run;
       l_run = (m_prev == -INFINITY) ? 0.f : l_run * ex2(m_prev - mx);
       m_run = mx;
       // pass 2: probabilities -> shared memory (bf16, swizzled)
       uint8_t* pbuf = sP + (j & 1) * 2 * kTile;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
+      for (int c = half * 64; c < half * 64 + 64; c += 32) {
         tmem_ld_32x32b_x32(ts + c, v);
         tmem_wait_ld();
         float pr[32];
@@ -255,23 +268,24 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm, Params p) {
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&p_full[j & 1]);
-      if (j >= 1 && !fold(j - 1, m_prev)) {
-        ok = false;
-        break;
-      }
+      if (j >= 1 && !fold(j - 1, m_prev)) ok = false;
     }
     if (ok) ok = fold(n_kv - 1, m_run);
+    // row sum = both halves' partial sums (same running max)
+    s_sum[half * BM + row] = l_run;
+    named_bar(pair_bar, 64);
+    l_run += s_sum[(half ^ 1) * BM + row];
     if (ok) {
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-      __nv_bfloat16* orow = p.o + static_cast<long>(tok0 + q) * p.o_stride + h * D;
+      __nv_bfloat16* orow = p.o + static_cast<long>(tok0 + q) * p.o_stride + h * D + half * 32;
 #pragma unroll
-      for (int c = 0; c < D; c += 8) {
+      for (int c = 0; c < D / 2; c += 8) {
         float t8[8];
 #pragma unroll
         for (int t = 0; t < 8; ++t) t8[t] = o_acc[c + t] * inv;
         *reinterpret_cast<bf16x8*>(orow + c) = float_to_bf16x8(t8);
       }
-      p.lse[(static_cast<long>(b) * p.Hq + h) * p.S + q] = m_run + log2f(l_run);
+      if (half == 0) p.lse[(static_cast<long>(b) * p.Hq + h) * p.S + q] = m_run + log2f(l_run);
     }
   }
   tc_fence_before();
@@ -330,7 +344,7 @@ dkdv_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUte
       mbar_init(&qo_empty[s], 1);
     }
     mbar_init(sdp_full, 1);
-    mbar_init(ds_full, 128);
+    mbar_init(ds_full, kSoftThreads);
     mbar_init(pds_empty, 1);
     mbar_init(acc_done, 1);
     mbar_init(drain, 1);
@@ -398,34 +412,35 @@ dkdv_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUte
     }
   } else {
     const int quarter = warp % 4;
+    const int half = (warp - 2) / 4;         // query columns [64*half, +64); dK/dV columns [32*half, +32)
     const int row = quarter * 32 + lane;     // key row within the block
     const int key = k0 + row;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    const int sm_tid = threadIdx.x - 64;     // 0..127
+    const int sm_tid = threadIdx.x - 64;     // 0..255
     bool ok = true;
+    // every softmax warp runs both named barriers of every iteration, also
+    // after a bounded wait failed (it then skips the work): no warp can be
+    // left blocked on a barrier its peers never reach
     for (int it = 0; it < n_it; ++it) {
       const int h = h_first + it / per_head;
       const int qb = kb + it % per_head;
       const int q0 = qb * BM;
       // stage this block's lse / delta (one value per thread), then wait for S^T / dP^T
-      named_bar(1, 128);  // previous iteration finished reading s_lse / s_del
-      const long li = (static_cast<long>(b) * p.Hq + h) * p.S + q0 + sm_tid;
-      s_lse[sm_tid] = p.lse[li];
-      s_del[sm_tid] = p.delta[li];
-      named_bar(1, 128);
-      if (!mbar_wait(sdp_full, it & 1, p.status)) {
-        ok = false;
-        break;
+      named_bar(1, kSoftThreads);  // previous iteration finished reading s_lse / s_del
+      if (sm_tid < BM) {
+        const long li = (static_cast<long>(b) * p.Hq + h) * p.S + q0 + sm_tid;
+        s_lse[sm_tid] = p.lse[li];
+        s_del[sm_tid] = p.delta[li];
       }
-      tc_fence_after();
-      if (it > 0 && !mbar_wait(pds_empty, (it - 1) & 1, p.status)) {
-        ok = false;
-        break;
-      }
+      named_bar(1, kSoftThreads);
+      if (ok && !mbar_wait(sdp_full, it & 1, p.status)) ok = false;
+      if (ok) tc_fence_after();
+      if (ok && it > 0 && !mbar_wait(pds_empty, (it - 1) & 1, p.status)) ok = false;
+      if (!ok) continue;
       const bool diag = (qb == kb);
       uint32_t vs[32], vd[32];
 #pragma unroll 1
-      for (int c = 0; c < BM; c += 32) {
+      for (int c = half * 64; c < half * 64 + 64; c += 32) {
         tmem_ld_32x32b_x32(tS + c + lane_off, vs);
         tmem_ld_32x32b_x32(tdP + c + lane_off, vd);
         tmem_wait_ld();
@@ -454,8 +469,8 @@ dkdv_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUte
       tc_fence_after();
       uint32_t v[32];
       float* wrow = p.ws + ((((static_cast<long>(b) * p.Hkv + kvh) * p.hsplit + part) * p.S) + key) * (2 * D);
-#pragma unroll
-      for (int c = 0; c < D; c += 32) {
+      {
+        const int c = half * 32;
         tmem_ld_32x32b_x32(tdK + c + lane_off, v);
         tmem_wait_ld();
 #pragma unroll
@@ -475,8 +490,8 @@ dkdv_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUte
       uint32_t v[32];
       __nv_bfloat16* krow = p.dqkv + static_cast<long>(tok0 + key) * p.dqkv_stride + (p.Hq + kvh) * D;
       __nv_bfloat16* vrow = p.dqkv + static_cast<long>(tok0 + key) * p.dqkv_stride + (p.Hq + p.Hkv + kvh) * D;
-#pragma unroll
-      for (int c = 0; c < D; c += 32) {
+      {
+        const int c = half * 32;
         float f[32];
         tmem_ld_32x32b_x32(tdK + c + lane_off, v);
         tmem_wait_ld();
@@ -537,7 +552,7 @@ dq_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtens
       mbar_init(&kv_empty[s], 1);
     }
     mbar_init(sdp_full, 1);
-    mbar_init(ds_full, 128);
+    mbar_init(ds_full, kSoftThreads);
     mbar_init(ds_empty, 1);
     mbar_init(acc_done, 1);
     mbar_init(drain, 1);
@@ -600,6 +615,7 @@ dq_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtens
     }
   } else {
     const int quarter = warp % 4;
+    const int half = (warp - 2) / 4;          // key columns [64*half, +64); dQ columns [32*half, +32)
     const int row = quarter * 32 + lane;
     const int q = q0 + row;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
@@ -620,7 +636,7 @@ dq_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtens
       const bool diag = (j == qb);
       uint32_t vs[32], vd[32];
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
+      for (int c = half * 64; c < half * 64 + 64; c += 32) {
         tmem_ld_32x32b_x32(tS + c + lane_off, vs);
         tmem_ld_32x32b_x32(tdP + c + lane_off, vd);
         tmem_wait_ld();
@@ -646,8 +662,8 @@ dq_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtens
       tc_fence_after();
       uint32_t v[32];
       __nv_bfloat16* qrow = p.dqkv + static_cast<long>(tok0 + q) * p.dqkv_stride + h * D;
-#pragma unroll
-      for (int c = 0; c < D; c += 32) {
+      {
+        const int c = half * 32;
         float f[32];
         tmem_ld_32x32b_x32(tdQ + c + lane_off, v);
         tmem_wait_ld();

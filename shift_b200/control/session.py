@@ -137,6 +137,58 @@ class Session:
         self.log("fault_recovered", **rec)
         return rec
 
+    def unplanned_fault(self, rid: int, timeout: float = 300.0):
+        """A fault the replica injects into itself (``--inject sigkill_bwd@STEP``
+        of the model-parallel worker: one rank SIGKILLs itself mid-backward):
+        expect the replica's exit, wait for the survivors' solo commits, restart
+        it (on its ``restart_devices``), and time fault -> restored -> first
+        joint commit."""
+        gen = self.generation[rid]
+        survivors = [r for r in range(self.replicas) if r != rid]
+        self.marker(f"EXPECT_PEER_FAILURE_g{gen}_r{rid}")
+        self.await_(lambda: self.reader.rows("injected_sigkill", rid=rid, generation=gen), timeout, "self-kill")
+        kill = self.reader.rows("injected_sigkill", rid=rid, generation=gen)[0]
+        base = kill["step"]
+        self.await_(lambda: self.reader.rows("peer_fault_exit", rid=rid), timeout, "replica exit")
+        self.await_(lambda: all(any(c["participants"] == len(survivors) and c["step"] > base
+                                    for c in self.commits(s)) for s in survivors), timeout, "solo commits")
+        t_solo = time.time()
+        self.marker(f"RESTART_g{gen + 1}_r{rid}")
+        self.generation[rid] = gen + 1
+        self.await_(lambda: len({r["rank"] for r in self.reader.rows("restored", rid=rid, generation=gen + 1)})
+                    == self.ranks(), timeout, "restored ranks")
+        restored = self.reader.rows("restored", rid=rid, generation=gen + 1)
+        rstep = max(r["step"] for r in restored)
+        self.await_(lambda: any(c["participants"] == self.replicas and c["step"] > rstep
+                                for c in self.commits(rid, gen + 1)), timeout, "joint commit")
+        joint = [c for c in self.commits(rid, gen + 1) if c["participants"] == self.replicas and c["step"] > rstep][0]
+        placement = {r["rank"]: r.get("placement") for r in self.reader.rows("ready", rid=rid, generation=gen + 1)}
+        old_placement = {r["rank"]: r.get("placement") for r in self.reader.rows("ready", rid=rid, generation=gen)}
+        rec = dict(rid=rid, fault_kind="sigkill_mid_backward", generation=gen, killed_rank=kill["rank"],
+                   killed_stage=kill.get("stage"), killed_tp_rank=kill.get("tp_rank"), fault_step=base,
+                   fault_time=kill["fault_time"], solo_time=t_solo, restored_time=max(r["time"] for r in restored),
+                   joint_time=joint["time"], restored_step=rstep, joint_step=joint["step"],
+                   time_to_recovery=joint["time"] - kill["fault_time"],
+                   restored_hashes_match=all(r["hashes_match"] for r in restored),
+                   placement_before=old_placement, placement_after=placement)
+        self.timings.append(rec)
+        self.log("fault_recovered", **rec)
+        return rec
+
+    def throughput_window(self, rid: int, first_step: int, steps: int = 100) -> dict:
+        """Tokens/s of the job per 10-step window from ``first_step`` on, from
+        a surviving replica's commits (``tokens`` = tokens of all participants)."""
+        rows = sorted((c for c in self.reader.rows("commit", rid=rid, rank=0) if c.get("tokens")),
+                      key=lambda c: c["time"])
+        rows = [c for c in rows if first_step <= c["step"] <= first_step + steps]
+        out = []
+        for i in range(0, len(rows) - 10, 10):
+            w = rows[i:i + 11]
+            dt = w[-1]["time"] - w[0]["time"]
+            out.append({"steps": [w[0]["step"], w[-1]["step"]], "tokens_per_s": sum(c["tokens"] for c in w[1:]) / dt,
+                        "participants": sorted({c["participants"] for c in w[1:]})})
+        return {"windows": out, "steps": len(rows)}
+
     def finish(self, stop_at_step: int | None = None, timeout: float = 120.0):
         self.marker("STOP", "" if stop_at_step is None else str(stop_at_step))
         for r, p in self.sup.items():

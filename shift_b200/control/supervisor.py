@@ -52,6 +52,7 @@ DEFAULTS = {
     "recycle_after_worker_fault": False,
     "nproc_per_node": 1,
     "devices": [],                 # per replica: list of GPU index lists, or [] for CPU
+    "restart_devices": [],         # per replica: GPUs of a relaunched generation (stage migration to spares)
     "store_port_base": 29700,
 }
 REQUIRED = ("train_args",)
@@ -142,7 +143,7 @@ def main(argv=None):
             time.sleep(0.02)
 
     def devices_for_replica():
-        d = cfg["devices"]
+        d = cfg["restart_devices"] if (generation > 0 and cfg["restart_devices"]) else cfg["devices"]
         if not d:
             return ""
         return ",".join(str(x) for x in d[args.replica % len(d)])

@@ -214,10 +214,26 @@ def main(argv=None):
     ap.add_argument("--worker-kill", type=int, default=None, help="kill one rank instead of the launcher tree")
     ap.add_argument("--joint-commits", type=int, default=3)
     ap.add_argument("--seconds", type=float, default=900)
+    ap.add_argument("--unplanned", type=int, default=None,
+                    help="replica that injects its own fault (the config's --inject / --inject-rank); "
+                         "report time-to-recovery and the tokens/s windows over --window steps")
+    ap.add_argument("--window", type=int, default=100)
     a = ap.parse_args(argv)
     s = Session(a.root, a.session, a.config, a.replicas, seconds=a.seconds)
     s.start()
     results = []
+    if a.unplanned is not None:
+        try:
+            survivor = next(r for r in range(a.replicas) if r != a.unplanned)
+            rec = s.unplanned_fault(a.unplanned)
+            first = max(0, rec["fault_step"] - a.window // 4)
+            s.await_(lambda: s.last_step(survivor) >= first + a.window, 1800, f"{a.window}-step window")
+            rec["throughput"] = s.throughput_window(survivor, first, a.window)
+        finally:
+            s.finish()
+        (s.dir / "unplanned_summary.json").write_text(json.dumps(rec, indent=1, default=str))
+        print(json.dumps(rec, indent=1, default=str))
+        return
     try:
         for i in range(a.faults):
             target = a.fault_step * (i + 1)

@@ -155,16 +155,28 @@ rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __
   }
 }
 
-// out[c] (+)= sum_b partial[b, c] in block order (deterministic).
-__global__ void column_reduce_kernel(const float* __restrict__ partial, int nblocks, int cols,
-                                     float* __restrict__ out_f32, __nv_bfloat16* __restrict__ out_bf16,
-                                     int accumulate) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= cols) return;
+// out[c] (+)= sum_b partial[b, c], deterministic: a CTA owns 32 columns;
+// warp w sums rows w, w+8, ... (lane = column, coalesced), then warp 0 adds
+// the 8 warp sums in warp order.  256 threads per CTA.
+__global__ void __launch_bounds__(256)
+column_reduce_kernel(const float* __restrict__ partial, int nblocks, int cols, float* __restrict__ out_f32,
+                     __nv_bfloat16* __restrict__ out_bf16, int accumulate) {
+  __shared__ float red[8][32];
+  const int lane = threadIdx.x % 32, w = threadIdx.x / 32;
+  const int c = blockIdx.x * 32 + lane;
   float s = 0.f;
-  for (int b = 0; b < nblocks; ++b) s += partial[static_cast<long>(b) * cols + c];
-  if (out_f32) out_f32[c] = accumulate ? out_f32[c] + s : s;
-  if (out_bf16) out_bf16[c] = __float2bfloat16(accumulate ? __bfloat162float(out_bf16[c]) + s : s);
+  if (c < cols) {
+#pragma unroll 4
+    for (int b = w; b < nblocks; b += 8) s += partial[static_cast<long>(b) * cols + c];
+  }
+  red[w][lane] = s;
+  __syncthreads();
+  if (w != 0 || c >= cols) return;
+  float t = 0.f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) t += red[k][lane];
+  if (out_f32) out_f32[c] = accumulate ? out_f32[c] + t : t;
+  if (out_bf16) out_bf16[c] = __float2bfloat16(accumulate ? __bfloat162float(out_bf16[c]) + t : t);
 }
 
 static int blocks_for(int rows) {
@@ -172,7 +184,7 @@ static int blocks_for(int rows) {
   cudaGetDevice(&dev);
   int sms;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  return std::max(1, std::min((rows + kWarps - 1) / kWarps, sms * 4));
+  return std::max(1, std::min((rows + kWarps - 1) / kWarps, sms * 2));
 }
 
 #define SB_NORM_DISPATCH(H, MACRO) \
@@ -275,7 +287,7 @@ at::Tensor rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tens
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   float* of = dw_out.scalar_type() == at::kFloat ? dw_out.data_ptr<float>() : nullptr;
   __nv_bfloat16* ob = dw_out.scalar_type() == at::kBFloat16 ? reinterpret_cast<__nv_bfloat16*>(dw_out.data_ptr()) : nullptr;
-  column_reduce_kernel<<<(H + 255) / 256, 256, 0, stream>>>(partial.data_ptr<float>(), blocks, H, of, ob, accumulate ? 1 : 0);
+  column_reduce_kernel<<<(H + 31) / 32, 256, 0, stream>>>(partial.data_ptr<float>(), blocks, H, of, ob, accumulate ? 1 : 0);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return dx;
 }
@@ -286,7 +298,7 @@ void column_reduce(const at::Tensor& partial, at::Tensor& out, bool accumulate) 
   const int nb = static_cast<int>(partial.size(0));
   float* of = out.scalar_type() == at::kFloat ? out.data_ptr<float>() : nullptr;
   __nv_bfloat16* ob = out.scalar_type() == at::kBFloat16 ? reinterpret_cast<__nv_bfloat16*>(out.data_ptr()) : nullptr;
-  column_reduce_kernel<<<(cols + 255) / 256, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+  column_reduce_kernel<<<(cols + 31) / 32, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       partial.data_ptr<float>(), nb, cols, of, ob, accumulate ? 1 : 0);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

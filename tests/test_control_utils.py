@@ -101,3 +101,14 @@ def test_supervisor_config_validation(tmp_path):
     unknown.write_text(json.dumps({"train_args": [], "bogus": 1}))
     with pytest.raises(ValueError, match="unknown config keys"):
         load_config(unknown)
+
+
+def test_shipped_configs_validate():
+    """Every supervisor config in configs/ passes the supervisor's validation."""
+    from pathlib import Path
+    from shift_b200.control.supervisor import load_config
+    files = sorted((Path(__file__).resolve().parents[1] / "configs").glob("*.json"))
+    assert files
+    for f in files:
+        cfg = load_config(f)
+        assert cfg["train_args"], f

@@ -15,7 +15,8 @@ reduction), votes, and commits -- the reference's SHIFT step
 
 Unplanned fault (BASELINE config 5 semantics): ``--inject sigkill_bwd@STEP``
 with ``--inject-rank K`` makes local rank K SIGKILL itself in the middle of
-the backward of STEP's last microbatch.  The launcher then stops the rest of
+the backward of STEP's last microbatch (``sigkill_step@STEP``: right after
+STEP's commit, the form used on GPUs).  The launcher then stops the rest of
 the replica, the survivors' quorum reconfigures and they continue alone; the
 relaunched replica (possibly on other devices: the supervisor's
 ``restart_devices``) heals every rank from the same-coordinate rank of a live
@@ -209,9 +210,9 @@ class MPWorker(Worker):
         return total
 
     # ------------------------------------------------------------------ fault injection
-    def _kill_now(self, step) -> bool:
+    def _kill_now(self, step, kind_wanted: str = "sigkill_bwd") -> bool:
         kind, _, arg = self.args.inject.partition("@")
-        return (kind == "sigkill_bwd" and step == int(arg) and self.rank == self.args.inject_rank
+        return (kind == kind_wanted and step == int(arg) and self.rank == self.args.inject_rank
                 and self.args.replica == self.args.inject_replica and self.args.generation == 0)
 
     def _die(self, layer):
@@ -289,6 +290,12 @@ class MPWorker(Worker):
                            tokens=tokens_per_replica * mgr.num_participants(), seconds=time.monotonic() - it0)
             else:
                 self.event("skipped", step=step, error=str(mgr.errored()))
+            if commit and self._kill_now(step, "sigkill_step"):
+                # GPU form of the fault: the rank leaves between steps, with
+                # none of its kernels or collectives in flight
+                if self.device.type == "cuda":
+                    torch.cuda.synchronize(self.device)
+                self._die(-1)
         self.event("stopped", step=self.progress["updates"])
         mgr.shutdown()
         self.event.close()

@@ -58,3 +58,16 @@ def test_planned_handoff_on_gpus(tmp_path, variant):
     res = s.run(post_steps=3)
     assert res["returncodes"] == {"A": 0, "B": 0, "C": 0}
     assert res["pass"], {k: v for k, v in res["checks"].items() if not v["pass"]}
+
+
+@pytest.mark.parametrize("variant", ["p1f", "p2"])
+def test_rotation_cycles_on_gpus(tmp_path, variant):
+    """Three consecutive B/C rotation rounds on three GPUs (the spare of each
+    round is relaunched on the GPU the retired donor left)."""
+    if torch.cuda.device_count() < 3:
+        pytest.skip("needs 3 GPUs (A, B, C)")
+    s = PlannedSession(tmp_path, f"rot_{variant}", variant=variant, device="cuda",
+                       devices={"A": [0], "B": [1], "C": [2]})
+    res = s.run_cycles(cycles=3, post_steps=6)
+    assert res["pass"], {k: v for k, v in res["checks"].items() if not v["pass"]}
+    assert all(rc == 0 for rc in res["returncodes"].values()), res["returncodes"]

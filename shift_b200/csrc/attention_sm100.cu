@@ -223,20 +223,25 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm, Params p) {
       if (ok) tc_fence_after();
       const uint32_t ts = tbase + (j & 1) * BN + lane_off;
       const bool diag = (j == qb);
-      // pass 1: row max over this warp's 64 columns, combined with the partner's
-      float mx = m_run;
+      // pass 1: row max of the raw scores over this warp's 64 columns (the
+      // causal mask only exists on the diagonal tile), scaled once, then
+      // combined with the partner warp's
+      float mraw = -INFINITY;
       uint32_t v[32];
 #pragma unroll 1
       for (int c = half * 64; ok && c < half * 64 + 64; c += 32) {
         tmem_ld_32x32b_x32(ts + c, v);
         tmem_wait_ld();
+        if (diag) {
 #pragma unroll
-        for (int t = 0; t < 32; ++t) {
-          const int key = j * BN + c + t;
-          const float s = (diag && key > q) ? -INFINITY : __uint_as_float(v[t]) * p.scale_log2;
-          mx = fmaxf(mx, s);
+          for (int t = 0; t < 32; ++t)
+            if (j * BN + c + t <= q) mraw = fmaxf(mraw, __uint_as_float(v[t]));
+        } else {
+#pragma unroll
+          for (int t = 0; t < 32; ++t) mraw = fmaxf(mraw, __uint_as_float(v[t]));
         }
       }
+      float mx = fmaxf(m_run, mraw * p.scale_log2);
       s_max[((j & 1) * 2 + half) * BM + row] = mx;
       named_bar(pair_bar, 64);
       if (!ok) continue;
@@ -251,12 +256,19 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm, Params p) {
         tmem_ld_32x32b_x32(ts + c, v);
         tmem_wait_ld();
         float pr[32];
+        const float nmx = -mx;
+        if (diag) {
 #pragma unroll
-        for (int t = 0; t < 32; ++t) {
-          const int key = j * BN + c + t;
-          const float s = __uint_as_float(v[t]) * p.scale_log2;
-          pr[t] = (diag && key > q) ? 0.f : ex2(s - mx);
-          l_run += pr[t];
+          for (int t = 0; t < 32; ++t) {
+            pr[t] = (j * BN + c + t > q) ? 0.f : ex2(fmaf(__uint_as_float(v[t]), p.scale_log2, nmx));
+            l_run += pr[t];
+          }
+        } else {
+#pragma unroll
+          for (int t = 0; t < 32; ++t) {
+            pr[t] = ex2(fmaf(__uint_as_float(v[t]), p.scale_log2, nmx));
+            l_run += pr[t];
+          }
         }
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
@@ -447,11 +459,14 @@ dkdv_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUte
         float pt[32], dst[32];
 #pragma unroll
         for (int t = 0; t < 32; ++t) {
-          const int qq = q0 + c + t;
-          float pv = ex2(__uint_as_float(vs[t]) * p.scale_log2 - s_lse[c + t]);
-          if (diag && key > qq) pv = 0.f;
+          float pv = ex2(fmaf(__uint_as_float(vs[t]), p.scale_log2, -s_lse[c + t]));
           pt[t] = pv;
           dst[t] = pv * (__uint_as_float(vd[t]) - s_del[c + t]);
+        }
+        if (diag) {             // causal mask only on the diagonal tile
+#pragma unroll
+          for (int t = 0; t < 32; ++t)
+            if (key > q0 + c + t) pt[t] = dst[t] = 0.f;
         }
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
@@ -641,12 +656,14 @@ dq_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtens
         tmem_ld_32x32b_x32(tdP + c + lane_off, vd);
         tmem_wait_ld();
         float ds[32];
+        const float nlse = -lse;
 #pragma unroll
-        for (int t = 0; t < 32; ++t) {
-          const int key = j * BN + c + t;
-          float pv = ex2(__uint_as_float(vs[t]) * p.scale_log2 - lse);
-          if (diag && key > q) pv = 0.f;
-          ds[t] = pv * (__uint_as_float(vd[t]) - del);
+        for (int t = 0; t < 32; ++t)
+          ds[t] = ex2(fmaf(__uint_as_float(vs[t]), p.scale_log2, nlse)) * (__uint_as_float(vd[t]) - del);
+        if (diag) {             // causal mask only on the diagonal tile
+#pragma unroll
+          for (int t = 0; t < 32; ++t)
+            if (j * BN + c + t > q) ds[t] = 0.f;
         }
 #pragma unroll
         for (int u = 0; u < 4; ++u) {

@@ -115,7 +115,9 @@ __device__ __forceinline__ bool decode_tile(const Params& p, const int* s_prefix
   return true;
 }
 
-__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
+// x * sigmoid(x) with the fast reciprocal-based division (the epilogue is
+// issue-bound; an IEEE division per activation dominated it)
+__device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
 template <int BN, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)

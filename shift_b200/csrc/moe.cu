@@ -796,7 +796,7 @@ at::Tensor embedding_fwd(const at::Tensor& W, const at::Tensor& ids, int64_t voc
 // SwiGLU on interleaved gate/up blocks of 16 (layout produced by the GEMM
 // epilogue): h[:, 32b + i] = gate_{16b+i}, h[:, 32b + 16 + i] = up_{16b+i}.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ float silu(float x) { return x / (1.f + __expf(-x)); }
+__device__ __forceinline__ float silu(float x) { return __fdividef(x, 1.f + __expf(-x)); }
 
 __global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ h, long rows, int F, __nv_bfloat16* __restrict__ a) {
   const long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x;  // over rows * F/16 blocks of 16
@@ -835,7 +835,7 @@ __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ h, const __n
   bf16x8_to_float(reinterpret_cast<const bf16x8*>(da + r * F + b * 16)[1], d + 8);
 #pragma unroll
   for (int q = 0; q < 16; ++q) {
-    const float sg = 1.f / (1.f + __expf(-g[q]));
+    const float sg = __fdividef(1.f, 1.f + __expf(-g[q]));
     const float s = g[q] * sg;
     du[q] = d[q] * s;
     dg[q] = d[q] * u[q] * sg * (1.f + g[q] * (1.f - sg));

@@ -322,9 +322,9 @@ dkdv_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUte
   uint8_t* sO = sQ + kBwdStages * kTile;          // dO, stages x kTile
   uint8_t* sP = sO + kBwdStages * kTile;          // P^T  (2 halves)
   uint8_t* sS = sP + 2 * kTile;                   // dS^T (2 halves)
-  float* s_lse = reinterpret_cast<float*>(sS + 2 * kTile);
-  float* s_del = s_lse + BM;
-  uint64_t* bar = reinterpret_cast<uint64_t*>(s_del + BM);
+  float* s_lse = reinterpret_cast<float*>(sS + 2 * kTile);   // [2][BM], by iteration parity
+  float* s_del = s_lse + 2 * BM;                               // [2][BM]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(s_del + 2 * BM);
   uint64_t* kv_full = bar;
   uint64_t* qo_full = bar + 1;
   uint64_t* qo_empty = qo_full + kBwdStages;
@@ -433,35 +433,48 @@ dkdv_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUte
     // every softmax warp runs both named barriers of every iteration, also
     // after a bounded wait failed (it then skips the work): no warp can be
     // left blocked on a barrier its peers never reach
+    // lse / delta of the query block of iteration it live in buffer it & 1;
+    // the next iteration's values are loaded into registers at the top of an
+    // iteration and stored after its compute, so the global-load latency is
+    // hidden behind the tile; one barrier per iteration publishes them.
+    auto li_of = [&](int it) -> long {
+      const int hh = h_first + it / per_head;
+      const int qq = kb + it % per_head;
+      return (static_cast<long>(b) * p.Hq + hh) * p.S + qq * BM + sm_tid;
+    };
+    if (sm_tid < BM) {
+      s_lse[sm_tid] = p.lse[li_of(0)];
+      s_del[sm_tid] = p.delta[li_of(0)];
+    }
+    named_bar(1, kSoftThreads);
     for (int it = 0; it < n_it; ++it) {
-      const int h = h_first + it / per_head;
       const int qb = kb + it % per_head;
       const int q0 = qb * BM;
-      // stage this block's lse / delta (one value per thread), then wait for S^T / dP^T
-      named_bar(1, kSoftThreads);  // previous iteration finished reading s_lse / s_del
-      if (sm_tid < BM) {
-        const long li = (static_cast<long>(b) * p.Hq + h) * p.S + q0 + sm_tid;
-        s_lse[sm_tid] = p.lse[li];
-        s_del[sm_tid] = p.delta[li];
+      const int buf = it & 1;
+      float nl = 0.f, nd = 0.f;
+      const bool pre = sm_tid < BM && it + 1 < n_it;
+      if (pre) {
+        nl = p.lse[li_of(it + 1)];
+        nd = p.delta[li_of(it + 1)];
       }
-      named_bar(1, kSoftThreads);
       if (ok && !mbar_wait(sdp_full, it & 1, p.status)) ok = false;
       if (ok) tc_fence_after();
       if (ok && it > 0 && !mbar_wait(pds_empty, (it - 1) & 1, p.status)) ok = false;
-      if (!ok) continue;
+      const float* cl = s_lse + buf * BM;
+      const float* cd = s_del + buf * BM;
       const bool diag = (qb == kb);
       uint32_t vs[32], vd[32];
 #pragma unroll 1
-      for (int c = half * 64; c < half * 64 + 64; c += 32) {
+      for (int c = half * 64; ok && c < half * 64 + 64; c += 32) {
         tmem_ld_32x32b_x32(tS + c + lane_off, vs);
         tmem_ld_32x32b_x32(tdP + c + lane_off, vd);
         tmem_wait_ld();
         float pt[32], dst[32];
 #pragma unroll
         for (int t = 0; t < 32; ++t) {
-          float pv = ex2(fmaf(__uint_as_float(vs[t]), p.scale_log2, -s_lse[c + t]));
+          float pv = ex2(fmaf(__uint_as_float(vs[t]), p.scale_log2, -cl[c + t]));
           pt[t] = pv;
-          dst[t] = pv * (__uint_as_float(vd[t]) - s_del[c + t]);
+          dst[t] = pv * (__uint_as_float(vd[t]) - cd[c + t]);
         }
         if (diag) {             // causal mask only on the diagonal tile
 #pragma unroll
@@ -476,9 +489,16 @@ dkdv_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUte
           *reinterpret_cast<uint4*>(swz_chunk(sS, row, (c >> 3) + u)) = make_uint4(d.w[0], d.w[1], d.w[2], d.w[3]);
         }
       }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      mbar_arrive(ds_full);
+      if (ok) {
+        fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(ds_full);
+      }
+      if (pre) {
+        s_lse[(buf ^ 1) * BM + sm_tid] = nl;
+        s_del[(buf ^ 1) * BM + sm_tid] = nd;
+      }
+      named_bar(1, kSoftThreads);   // next buffer written; everyone done with this one
     }
     if (ok && p.hsplit > 1 && mbar_wait(acc_done, 0, p.status)) {
       tc_fence_after();

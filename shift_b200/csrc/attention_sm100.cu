@@ -307,8 +307,16 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm, Params p) {
 }
 
 // ============================ backward: dK, dV ============================
+// One CTA per (key block of 128, kv head [, head split], batch).  The query
+// blocks of every head of the group are walked in 64-query sub-blocks k:
+//   S^T_k = K Q_k^T and dP^T_k = V dO_k^T  -> TMEM buffer k & 1 (64 columns each)
+//   softmax warps: P^T = exp2(S^T * scale - lse), dS^T = P^T (dP^T - delta)
+//                  -> swizzled smem buffer k & 1 (bf16, 128 keys x 64 queries)
+//   dV += P^T dO_k, dK += dS^T Q_k  (accumulated in TMEM across all k)
+// With two S/dP buffers the tensor core computes S_{k+1} while the softmax
+// warps work on k, and the dV/dK update of k-1 overlaps the softmax of k.
 constexpr int kBwdStages = 2;
-constexpr int kDkdvSmem = 1024 + 2 * kTile /*K,V*/ + 2 * kBwdStages * kTile /*Q,dO*/ + 4 * kTile /*P^T,dS^T*/ +
+constexpr int kDkdvSmem = 1024 + 2 * kTile /*K,V*/ + 2 * kBwdStages * kTile /*Q,dO*/ + 4 * kTile /*P^T,dS^T x2*/ +
                           2 * BM * 4 * 2 /*lse,delta*/ + 256;
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -318,20 +326,21 @@ dkdv_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUte
   uint8_t* sm = smem_raw + (((raw + 1023) & ~1023u) - raw);
   uint8_t* sK = sm;
   uint8_t* sV = sK + kTile;
-  uint8_t* sQ = sV + kTile;                       // stages x kTile
+  uint8_t* sQ = sV + kTile;                       // stages x kTile (128 queries x 64 d)
   uint8_t* sO = sQ + kBwdStages * kTile;          // dO, stages x kTile
-  uint8_t* sP = sO + kBwdStages * kTile;          // P^T  (2 halves)
-  uint8_t* sS = sP + 2 * kTile;                   // dS^T (2 halves)
+  uint8_t* sP = sO + kBwdStages * kTile;          // P^T  [2 buffers] x (128 keys x 64 queries)
+  uint8_t* sS = sP + 2 * kTile;                   // dS^T [2 buffers]
   float* s_lse = reinterpret_cast<float*>(sS + 2 * kTile);   // [2][BM], by iteration parity
   float* s_del = s_lse + 2 * BM;                               // [2][BM]
   uint64_t* bar = reinterpret_cast<uint64_t*>(s_del + 2 * BM);
   uint64_t* kv_full = bar;
   uint64_t* qo_full = bar + 1;
   uint64_t* qo_empty = qo_full + kBwdStages;
-  uint64_t* sdp_full = qo_empty + kBwdStages;
-  uint64_t* ds_full = sdp_full + 1;
-  uint64_t* pds_empty = ds_full + 1;
-  uint64_t* acc_done = pds_empty + 1;
+  uint64_t* sdp_full = qo_empty + kBwdStages;     // [2]
+  uint64_t* sdp_empty = sdp_full + 2;             // [2]
+  uint64_t* ds_full = sdp_empty + 2;              // [2]
+  uint64_t* pds_empty = ds_full + 2;              // [2]
+  uint64_t* acc_done = pds_empty + 2;
   uint64_t* drain = acc_done + 1;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(drain + 1);
 
@@ -347,7 +356,8 @@ dkdv_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUte
   const int tok0 = b * p.S;
   const int n_q = p.S / BM;
   const int per_head = n_q - kb;
-  const int n_it = group * per_head;
+  const int n_it = group * per_head;              // 128-query blocks
+  const int n_sub = 2 * n_it;                     // 64-query sub-blocks
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
@@ -355,9 +365,12 @@ dkdv_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUte
       mbar_init(&qo_full[s], 1);
       mbar_init(&qo_empty[s], 1);
     }
-    mbar_init(sdp_full, 1);
-    mbar_init(ds_full, kSoftThreads);
-    mbar_init(pds_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sdp_full[i], 1);
+      mbar_init(&sdp_empty[i], kSoftThreads);
+      mbar_init(&ds_full[i], kSoftThreads);
+      mbar_init(&pds_empty[i], 1);
+    }
     mbar_init(acc_done, 1);
     mbar_init(drain, 1);
     fence_barrier_init();
@@ -370,7 +383,8 @@ dkdv_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUte
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tslot;
-  const uint32_t tS = tbase, tdP = tbase + 128, tdV = tbase + 256, tdK = tbase + 320;
+  // S^T / dP^T double buffers of 64 columns, then the dV / dK accumulators
+  const uint32_t tS0 = tbase, tdP0 = tbase + 128, tdV = tbase + 256, tdK = tbase + 320;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -391,32 +405,41 @@ dkdv_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUte
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idS = make_idesc_bf16(BN, BM, 0, 0);   // [keys x queries], K = d
-      constexpr uint32_t idG = make_idesc_bf16(BN, D, 0, 1);    // [keys x d], K = queries
+      constexpr uint32_t idS = make_idesc_bf16(BN, 64, 0, 0);   // [keys x 64 queries], K = d
+      constexpr uint32_t idG = make_idesc_bf16(BN, D, 0, 1);    // [keys x d], K = 64 queries
       const uint32_t ka = smem_u32(sK), va = smem_u32(sV);
-      const uint32_t pa = smem_u32(sP), da = smem_u32(sS);
       bool ok = mbar_wait(kv_full, 0, p.status);
-      for (int it = 0; it < n_it && ok; ++it) {
-        const int st = it % kBwdStages;
-        if (!mbar_wait(&qo_full[st], (it / kBwdStages) & 1, p.status)) break;
-        tc_fence_after();
-        const uint32_t qa = smem_u32(sQ + st * kTile), oa = smem_u32(sO + st * kTile);
+      // k: issue S/dP of sub-block k (k < n_sub), then dV/dK of sub-block k-1
+      for (int k = 0; k <= n_sub && ok; ++k) {
+        if (k < n_sub) {
+          const int it = k >> 1, hh = k & 1, st = it % kBwdStages;
+          if (hh == 0 && !mbar_wait(&qo_full[st], (it / kBwdStages) & 1, p.status)) break;
+          if (k >= 2 && !mbar_wait(&sdp_empty[k & 1], ((k - 2) >> 1) & 1, p.status)) break;
+          tc_fence_after();
+          const uint32_t qa = smem_u32(sQ + st * kTile) + hh * 8192, oa = smem_u32(sO + st * kTile) + hh * 8192;
+          const uint32_t ts = tS0 + (k & 1) * 64, tp = tdP0 + (k & 1) * 64;
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          umma_f16(tS, kdesc(ka + kk * 32), kdesc(qa + kk * 32), idS, kk > 0);
-          umma_f16(tdP, kdesc(va + kk * 32), kdesc(oa + kk * 32), idS, kk > 0);
+          for (int kk = 0; kk < D / 16; ++kk) {
+            umma_f16(ts, kdesc(ka + kk * 32), kdesc(qa + kk * 32), idS, kk > 0);
+            umma_f16(tp, kdesc(va + kk * 32), kdesc(oa + kk * 32), idS, kk > 0);
+          }
+          umma_commit(&sdp_full[k & 1]);
         }
-        umma_commit(sdp_full);
-        if (!mbar_wait(ds_full, it & 1, p.status)) break;
-        tc_fence_after();
+        if (k >= 1) {
+          const int kp = k - 1, it = kp >> 1, hh = kp & 1, st = it % kBwdStages;
+          if (!mbar_wait(&ds_full[kp & 1], (kp >> 1) & 1, p.status)) break;
+          tc_fence_after();
+          const uint32_t qa = smem_u32(sQ + st * kTile), oa = smem_u32(sO + st * kTile);
+          const uint32_t pa = smem_u32(sP + (kp & 1) * kTile), da = smem_u32(sS + (kp & 1) * kTile);
 #pragma unroll
-        for (int kk = 0; kk < BM / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * kTile + (kk & 3) * 32;
-          umma_f16(tdV, kdesc(pa + off), mndesc(oa + kk * 2048), idG, (it > 0 || kk > 0) ? 1u : 0u);
-          umma_f16(tdK, kdesc(da + off), mndesc(qa + kk * 2048), idG, (it > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < 64 / 16; ++kk) {
+            const uint32_t acc = (kp > 0 || kk > 0) ? 1u : 0u;
+            umma_f16(tdV, kdesc(pa + kk * 32), mndesc(oa + (hh * 4 + kk) * 2048), idG, acc);
+            umma_f16(tdK, kdesc(da + kk * 32), mndesc(qa + (hh * 4 + kk) * 2048), idG, acc);
+          }
+          umma_commit(&pds_empty[kp & 1]);
+          if (hh == 1) umma_commit(&qo_empty[st]);     // both halves of this Q / dO stage consumed
         }
-        umma_commit(&qo_empty[st]);
-        umma_commit(pds_empty);
       }
       umma_commit(acc_done);
       umma_commit(drain);
@@ -424,19 +447,17 @@ dkdv_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUte
     }
   } else {
     const int quarter = warp % 4;
-    const int half = (warp - 2) / 4;         // query columns [64*half, +64); dK/dV columns [32*half, +32)
+    const int half = (warp - 2) / 4;         // columns [32*half, +32) of a 64-query sub-block; of dK/dV
     const int row = quarter * 32 + lane;     // key row within the block
     const int key = k0 + row;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const int sm_tid = threadIdx.x - 64;     // 0..255
     bool ok = true;
-    // every softmax warp runs both named barriers of every iteration, also
-    // after a bounded wait failed (it then skips the work): no warp can be
-    // left blocked on a barrier its peers never reach
-    // lse / delta of the query block of iteration it live in buffer it & 1;
-    // the next iteration's values are loaded into registers at the top of an
-    // iteration and stored after its compute, so the global-load latency is
-    // hidden behind the tile; one barrier per iteration publishes them.
+    // lse / delta of the 128-query block of iteration it live in buffer it & 1;
+    // the next iteration's values are loaded into registers during the
+    // current one and published by the barrier that ends it.  Every softmax
+    // warp runs every barrier, also after a bounded wait failed (it then
+    // skips the work), so no warp is left blocked on a barrier.
     auto li_of = [&](int it) -> long {
       const int hh = h_first + it / per_head;
       const int qq = kb + it % per_head;
@@ -449,7 +470,6 @@ dkdv_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUte
     named_bar(1, kSoftThreads);
     for (int it = 0; it < n_it; ++it) {
       const int qb = kb + it % per_head;
-      const int q0 = qb * BM;
       const int buf = it & 1;
       float nl = 0.f, nd = 0.f;
       const bool pre = sm_tid < BM && it + 1 < n_it;
@@ -457,42 +477,49 @@ dkdv_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUte
         nl = p.lse[li_of(it + 1)];
         nd = p.delta[li_of(it + 1)];
       }
-      if (ok && !mbar_wait(sdp_full, it & 1, p.status)) ok = false;
-      if (ok) tc_fence_after();
-      if (ok && it > 0 && !mbar_wait(pds_empty, (it - 1) & 1, p.status)) ok = false;
       const float* cl = s_lse + buf * BM;
       const float* cd = s_del + buf * BM;
-      const bool diag = (qb == kb);
-      uint32_t vs[32], vd[32];
-#pragma unroll 1
-      for (int c = half * 64; ok && c < half * 64 + 64; c += 32) {
-        tmem_ld_32x32b_x32(tS + c + lane_off, vs);
-        tmem_ld_32x32b_x32(tdP + c + lane_off, vd);
+      for (int hh = 0; hh < 2; ++hh) {
+        const int k = 2 * it + hh;
+        const int q0 = qb * BM + hh * 64;              // first query of the sub-block
+        if (ok && !mbar_wait(&sdp_full[k & 1], (k >> 1) & 1, p.status)) ok = false;
+        if (!ok) continue;
+        tc_fence_after();
+        uint32_t vs[32], vd[32];
+        tmem_ld_32x32b_x32(tS0 + (k & 1) * 64 + half * 32 + lane_off, vs);
+        tmem_ld_32x32b_x32(tdP0 + (k & 1) * 64 + half * 32 + lane_off, vd);
         tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(&sdp_empty[k & 1]);                 // S/dP buffer may be overwritten by S_{k+2}
+        const int c0 = hh * 64 + half * 32;             // column of the 128-query block
         float pt[32], dst[32];
 #pragma unroll
         for (int t = 0; t < 32; ++t) {
-          float pv = ex2(fmaf(__uint_as_float(vs[t]), p.scale_log2, -cl[c + t]));
+          const float pv = ex2(fmaf(__uint_as_float(vs[t]), p.scale_log2, -cl[c0 + t]));
           pt[t] = pv;
-          dst[t] = pv * (__uint_as_float(vd[t]) - cd[c + t]);
+          dst[t] = pv * (__uint_as_float(vd[t]) - cd[c0 + t]);
         }
-        if (diag) {             // causal mask only on the diagonal tile
+        if (qb == kb) {             // causal mask only on the diagonal block
 #pragma unroll
           for (int t = 0; t < 32; ++t)
-            if (key > q0 + c + t) pt[t] = dst[t] = 0.f;
+            if (key > q0 + half * 32 + t) pt[t] = dst[t] = 0.f;
         }
+        if (k >= 2 && !mbar_wait(&pds_empty[k & 1], ((k - 2) >> 1) & 1, p.status)) {
+          ok = false;
+          continue;
+        }
+        uint8_t* pb = sP + (k & 1) * kTile;
+        uint8_t* db = sS + (k & 1) * kTile;
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           bf16x8 a = float_to_bf16x8(pt + 8 * u);
           bf16x8 d = float_to_bf16x8(dst + 8 * u);
-          *reinterpret_cast<uint4*>(swz_chunk(sP, row, (c >> 3) + u)) = make_uint4(a.w[0], a.w[1], a.w[2], a.w[3]);
-          *reinterpret_cast<uint4*>(swz_chunk(sS, row, (c >> 3) + u)) = make_uint4(d.w[0], d.w[1], d.w[2], d.w[3]);
+          *reinterpret_cast<uint4*>(swz_chunk(pb, row, half * 4 + u)) = make_uint4(a.w[0], a.w[1], a.w[2], a.w[3]);
+          *reinterpret_cast<uint4*>(swz_chunk(db, row, half * 4 + u)) = make_uint4(d.w[0], d.w[1], d.w[2], d.w[3]);
         }
-      }
-      if (ok) {
         fence_proxy_async_smem();
         tc_fence_before();
-        mbar_arrive(ds_full);
+        mbar_arrive(&ds_full[k & 1]);
       }
       if (pre) {
         s_lse[(buf ^ 1) * BM + sm_tid] = nl;

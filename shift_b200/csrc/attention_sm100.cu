@@ -577,7 +577,11 @@ dkdv_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUte
 }
 
 // ============================ backward: dQ ============================
-constexpr int kDqSmem = 1024 + 2 * kTile /*Q,dO*/ + 2 * kBwdStages * kTile /*K,V*/ + 2 * kTile /*dS*/ + 256;
+// One CTA per (query block of 128, head, batch), walking the causal key
+// blocks in 64-key sub-blocks k with double-buffered S / dP in TMEM:
+//   S_k = Q K_k^T, dP_k = dO V_k^T -> buffer k & 1;  dS_k -> smem buffer k & 1;
+//   dQ += dS_k K_k (TMEM accumulator)
+constexpr int kDqSmem = 1024 + 2 * kTile /*Q,dO*/ + 2 * kBwdStages * kTile /*K,V*/ + 2 * kTile /*dS x2*/ + 256;
 
 __global__ void __launch_bounds__(kThreads, 1)
 dq_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtensorMap tmo, Params p) {
@@ -588,15 +592,16 @@ dq_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtens
   uint8_t* sO = sQ + kTile;
   uint8_t* sK = sO + kTile;
   uint8_t* sV = sK + kBwdStages * kTile;
-  uint8_t* sS = sV + kBwdStages * kTile;
+  uint8_t* sS = sV + kBwdStages * kTile;          // dS [2 buffers] x (128 queries x 64 keys)
   uint64_t* bar = reinterpret_cast<uint64_t*>(sS + 2 * kTile);
   uint64_t* q_full = bar;
   uint64_t* kv_full = bar + 1;
   uint64_t* kv_empty = kv_full + kBwdStages;
-  uint64_t* sdp_full = kv_empty + kBwdStages;
-  uint64_t* ds_full = sdp_full + 1;
-  uint64_t* ds_empty = ds_full + 1;
-  uint64_t* acc_done = ds_empty + 1;
+  uint64_t* sdp_full = kv_empty + kBwdStages;     // [2]
+  uint64_t* sdp_empty = sdp_full + 2;             // [2]
+  uint64_t* ds_full = sdp_empty + 2;              // [2]
+  uint64_t* ds_empty = ds_full + 2;               // [2]
+  uint64_t* acc_done = ds_empty + 2;
   uint64_t* drain = acc_done + 1;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(drain + 1);
 
@@ -606,6 +611,7 @@ dq_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtens
   const int q0 = qb * BM;
   const int tok0 = b * p.S;
   const int n_kv = qb + 1;
+  const int n_sub = 2 * n_kv;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -613,9 +619,12 @@ dq_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtens
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    mbar_init(sdp_full, 1);
-    mbar_init(ds_full, kSoftThreads);
-    mbar_init(ds_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sdp_full[i], 1);
+      mbar_init(&sdp_empty[i], kSoftThreads);
+      mbar_init(&ds_full[i], kSoftThreads);
+      mbar_init(&ds_empty[i], 1);
+    }
     mbar_init(acc_done, 1);
     mbar_init(drain, 1);
     fence_barrier_init();
@@ -628,7 +637,7 @@ dq_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtens
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tslot;
-  const uint32_t tS = tbase, tdP = tbase + 128, tdQ = tbase + 256;
+  const uint32_t tS0 = tbase, tdP0 = tbase + 128, tdQ = tbase + 256;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -647,29 +656,36 @@ dq_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtens
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idS = make_idesc_bf16(BM, BN, 0, 0);
-      constexpr uint32_t idG = make_idesc_bf16(BM, D, 0, 1);
-      const uint32_t qa = smem_u32(sQ), oa = smem_u32(sO), da = smem_u32(sS);
+      constexpr uint32_t idS = make_idesc_bf16(BM, 64, 0, 0);   // [queries x 64 keys], K = d
+      constexpr uint32_t idG = make_idesc_bf16(BM, D, 0, 1);    // [queries x d], K = 64 keys
+      const uint32_t qa = smem_u32(sQ), oa = smem_u32(sO);
       bool ok = mbar_wait(q_full, 0, p.status);
-      for (int j = 0; j < n_kv && ok; ++j) {
-        const int st = j % kBwdStages;
-        if (!mbar_wait(&kv_full[st], (j / kBwdStages) & 1, p.status)) break;
-        tc_fence_after();
-        const uint32_t ka = smem_u32(sK + st * kTile), va = smem_u32(sV + st * kTile);
+      for (int k = 0; k <= n_sub && ok; ++k) {
+        if (k < n_sub) {
+          const int j = k >> 1, hh = k & 1, st = j % kBwdStages;
+          if (hh == 0 && !mbar_wait(&kv_full[st], (j / kBwdStages) & 1, p.status)) break;
+          if (k >= 2 && !mbar_wait(&sdp_empty[k & 1], ((k - 2) >> 1) & 1, p.status)) break;
+          tc_fence_after();
+          const uint32_t ka = smem_u32(sK + st * kTile) + hh * 8192, va = smem_u32(sV + st * kTile) + hh * 8192;
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          umma_f16(tS, kdesc(qa + kk * 32), kdesc(ka + kk * 32), idS, kk > 0);
-          umma_f16(tdP, kdesc(oa + kk * 32), kdesc(va + kk * 32), idS, kk > 0);
+          for (int kk = 0; kk < D / 16; ++kk) {
+            umma_f16(tS0 + (k & 1) * 64, kdesc(qa + kk * 32), kdesc(ka + kk * 32), idS, kk > 0);
+            umma_f16(tdP0 + (k & 1) * 64, kdesc(oa + kk * 32), kdesc(va + kk * 32), idS, kk > 0);
+          }
+          umma_commit(&sdp_full[k & 1]);
         }
-        umma_commit(sdp_full);
-        if (!mbar_wait(ds_full, j & 1, p.status)) break;
-        tc_fence_after();
+        if (k >= 1) {
+          const int kp = k - 1, j = kp >> 1, hh = kp & 1, st = j % kBwdStages;
+          if (!mbar_wait(&ds_full[kp & 1], (kp >> 1) & 1, p.status)) break;
+          tc_fence_after();
+          const uint32_t ka = smem_u32(sK + st * kTile), da = smem_u32(sS + (kp & 1) * kTile);
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk)
-          umma_f16(tdQ, kdesc(da + (kk >> 2) * kTile + (kk & 3) * 32), mndesc(ka + kk * 2048), idG,
-                   (j > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&kv_empty[st]);
-        umma_commit(ds_empty);
+          for (int kk = 0; kk < 64 / 16; ++kk)
+            umma_f16(tdQ, kdesc(da + kk * 32), mndesc(ka + (hh * 4 + kk) * 2048), idG,
+                     (kp > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&ds_empty[kp & 1]);
+          if (hh == 1) umma_commit(&kv_empty[st]);     // both halves of this K / V stage consumed
+        }
       }
       umma_commit(acc_done);
       umma_commit(drain);
@@ -677,50 +693,50 @@ dq_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtens
     }
   } else {
     const int quarter = warp % 4;
-    const int half = (warp - 2) / 4;          // key columns [64*half, +64); dQ columns [32*half, +32)
+    const int half = (warp - 2) / 4;          // columns [32*half, +32) of a 64-key sub-block; of dQ
     const int row = quarter * 32 + lane;
     const int q = q0 + row;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const long li = (static_cast<long>(b) * p.Hq + h) * p.S + q;
-    const float lse = p.lse[li];
+    const float nlse = -p.lse[li];
     const float del = p.delta[li];
     bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
-      if (!mbar_wait(sdp_full, j & 1, p.status)) {
+    for (int k = 0; k < n_sub; ++k) {
+      const int j = k >> 1, hh = k & 1;
+      if (!mbar_wait(&sdp_full[k & 1], (k >> 1) & 1, p.status)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      if (j > 0 && !mbar_wait(ds_empty, (j - 1) & 1, p.status)) {
+      uint32_t vs[32], vd[32];
+      tmem_ld_32x32b_x32(tS0 + (k & 1) * 64 + half * 32 + lane_off, vs);
+      tmem_ld_32x32b_x32(tdP0 + (k & 1) * 64 + half * 32 + lane_off, vd);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&sdp_empty[k & 1]);
+      float ds[32];
+#pragma unroll
+      for (int t = 0; t < 32; ++t)
+        ds[t] = ex2(fmaf(__uint_as_float(vs[t]), p.scale_log2, nlse)) * (__uint_as_float(vd[t]) - del);
+      if (j == qb) {             // causal mask only on the diagonal block
+        const int key0 = j * BN + hh * 64 + half * 32;
+#pragma unroll
+        for (int t = 0; t < 32; ++t)
+          if (key0 + t > q) ds[t] = 0.f;
+      }
+      if (k >= 2 && !mbar_wait(&ds_empty[k & 1], ((k - 2) >> 1) & 1, p.status)) {
         ok = false;
         break;
       }
-      const bool diag = (j == qb);
-      uint32_t vs[32], vd[32];
-#pragma unroll 1
-      for (int c = half * 64; c < half * 64 + 64; c += 32) {
-        tmem_ld_32x32b_x32(tS + c + lane_off, vs);
-        tmem_ld_32x32b_x32(tdP + c + lane_off, vd);
-        tmem_wait_ld();
-        float ds[32];
-        const float nlse = -lse;
+      uint8_t* db = sS + (k & 1) * kTile;
 #pragma unroll
-        for (int t = 0; t < 32; ++t)
-          ds[t] = ex2(fmaf(__uint_as_float(vs[t]), p.scale_log2, nlse)) * (__uint_as_float(vd[t]) - del);
-        if (diag) {             // causal mask only on the diagonal tile
-#pragma unroll
-          for (int t = 0; t < 32; ++t)
-            if (j * BN + c + t > q) ds[t] = 0.f;
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          bf16x8 d = float_to_bf16x8(ds + 8 * u);
-          *reinterpret_cast<uint4*>(swz_chunk(sS, row, (c >> 3) + u)) = make_uint4(d.w[0], d.w[1], d.w[2], d.w[3]);
-        }
+      for (int u = 0; u < 4; ++u) {
+        bf16x8 d = float_to_bf16x8(ds + 8 * u);
+        *reinterpret_cast<uint4*>(swz_chunk(db, row, half * 4 + u)) = make_uint4(d.w[0], d.w[1], d.w[2], d.w[3]);
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(ds_full);
+      mbar_arrive(&ds_full[k & 1]);
     }
     if (ok && mbar_wait(acc_done, 0, p.status)) {
       tc_fence_after();

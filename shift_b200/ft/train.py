@@ -76,6 +76,13 @@ def parse_args(argv=None):
     p.add_argument("--standby", choices=("cpu", "gpu"))
     p.add_argument("--bucket-size", type=int, default=64 * 1024 * 1024)
     p.add_argument("--inject", default="", help="test fault: nonfinite@STEP | exit@STEP | slow@MS")
+    p.add_argument("--mode", choices=["shift", "flat"], default="shift",
+                   help="flat: one process trains the whole global batch of --flat-replicas data ranks, "
+                        "no Manager (the non-fault-tolerant numerical baseline)")
+    p.add_argument("--flat-replicas", type=int, default=2)
+    p.add_argument("--reference-dump", default="",
+                   help="comma-separated committed steps after which the averaged gradient, model, optimizer and "
+                        "scheduler are saved to reference_step<k>_r<rank>.pt (group reduction or flat mode)")
     p.add_argument("--seed", type=int, default=2026)
     return p.parse_args(argv)
 
@@ -189,15 +196,51 @@ class Worker:
     # ------------------------------------------------------------------ data
     def batches(self, step):
         a = self.args
-        data_rank = a.replica
+        ranks = range(a.flat_replicas) if a.mode == "flat" else [a.replica]
         out, ids = [], []
-        for micro in range(a.microbatches):
-            sample = step * (a.microbatches * 4) + micro * 4 + data_rank
-            ids.append(sample)
-            data = synthetic_batch(self.cfg, sample, a.batch, a.seq_len, a.data, seed_base=100_000 + a.data_seed * 1_000_000)
-            data = data.to(self.device, non_blocking=True)
-            out.append((data[:, :-1].contiguous(), data[:, 1:].contiguous()))
+        for data_rank in ranks:
+            for micro in range(a.microbatches):
+                sample = step * (a.microbatches * 4) + micro * 4 + data_rank
+                ids.append(sample)
+                data = synthetic_batch(self.cfg, sample, a.batch, a.seq_len, a.data,
+                                       seed_base=100_000 + a.data_seed * 1_000_000)
+                data = data.to(self.device, non_blocking=True)
+                out.append((data[:, :-1].contiguous(), data[:, 1:].contiguous()))
         return out, ids
+
+    def reference_dump(self, grad):
+        """Per-step numerical reference (shift_full/train.py:584-587 semantics):
+        the averaged gradient and the committed state after the step."""
+        steps = {int(x) for x in self.args.reference_dump.split(",") if x.strip()}
+        if self.progress["updates"] not in steps:
+            return
+        sd = self.engine.state_dict()
+        payload = cpu_tree(dict(step=self.progress["updates"], gradients=grad.detach().float(),
+                                model=sd["model"], optimizer=sd["optimizer"], scheduler=sd["scheduler"]))
+        torch.save(payload, self.out / f"reference_step{self.progress['updates']}_r{self.rank}.pt")
+        self.event("reference_dump", step=self.progress["updates"])
+
+    def run_flat(self):
+        """The flat baseline: no quorum, no Manager; one replica trains every
+        data rank's microbatches (the same global batch as the shift run)."""
+        a = self.args
+        self.event("ready", model=a.model, mode="flat", params=self.engine.store.numel)
+        eng = self.engine
+        while self.progress["updates"] < a.steps and not self.requested_stop():
+            it0 = time.monotonic()
+            batches, ids = self.batches(self.progress["updates"])
+            loss = eng.forward_backward(batches, a.batch, a.seq_len)
+            g = eng.store.grad
+            eng.optimizer_step([g], 1.0)
+            grad_copy = g.detach().clone() if a.reference_dump else None
+            eng.commit()
+            self.progress["updates"] += 1
+            if a.reference_dump:
+                self.reference_dump(grad_copy)
+            self.event("commit", step=self.progress["updates"], participants=1, loss=float(loss), sample_ids=ids,
+                       seconds=time.monotonic() - it0)
+        self.event("stopped", step=self.progress["updates"])
+        self.event.close()
 
     # ------------------------------------------------------------------ main
     def run(self):
@@ -212,6 +255,8 @@ class Worker:
         self.engine.scheduler.base_lrs = [a.lr]
         self.engine.scheduler._last_lr = [a.lr]
         started = self.phase("model_load", started)
+        if a.mode == "flat":
+            return self.run_flat()
         if a.standby == "gpu":
             self.standby_gate("gpu")
         backend = a.backend or ("nccl" if self.device.type == "cuda" else "gloo")
@@ -349,6 +394,8 @@ class Worker:
             assert mgr.current_step() == self.progress["updates"]
             if a.checkpoint_step and self.progress["updates"] == a.checkpoint_step and commit:
                 self.save_checkpoint()
+            if commit and a.reference_dump and a.reduce == "group":
+                self.reference_dump(eng.store.grad)
         self.event("stopped", step=self.progress["updates"], attempts=attempts)
         mgr.shutdown()
         self.event.close()

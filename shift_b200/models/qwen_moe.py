@@ -326,6 +326,9 @@ class QwenMoE:
         B, S = saved["B"], saved["S"]
         T = B * S
         accumulate = getattr(self, "_accumulate", False)
+        # the auxiliary loss of a microbatch enters the step's mean with the
+        # microbatch's token share (1 with a single microbatch)
+        self._aux_scale = saved["loss_scale"] * T
         if self.part.has_head:
             dlogits = saved["dlogits"]
             y = saved["final_y"]
@@ -423,7 +426,7 @@ class QwenMoE:
                 counts = torch.zeros(cfg.experts, dtype=torch.float32, device=ids.device)
                 counts.scatter_add_(0, ids, torch.ones_like(ids, dtype=torch.float32))   # exact (integers)
             f = counts / float(T * cfg.top_k)
-            aux_grad = (f * (cfg.aux_coef * cfg.experts / float(T))).contiguous()
+            aux_grad = (f * (cfg.aux_coef * cfg.experts / float(T) * getattr(self, "_aux_scale", 1.0))).contiguous()
         Fn.router_bwd(c["m_in"], st.w(p + "mlp.router"), c["probs"], c["idx"], c["w"], dw_topk.contiguous(),
                       aux_grad, cfg.norm_topk, dx, st.g(p + "mlp.router"), accumulate, peer_rows, xchg)
         return dx

@@ -1,0 +1,57 @@
+"""Numerical oracle on CPU: the flat baseline (one process, whole global
+batch, no Manager) and the fault-tolerant run (2 replicas, quorum, group
+average) agree per step within the reference's tolerances; a perturbed run
+does not."""
+import json
+import socket
+import subprocess as sp
+import sys
+from pathlib import Path
+
+import torch
+
+from shift_b200.analysis.compare_reference import compare_runs
+from shift_b200.control.session import Session
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _ports(n):
+    socks, out = [], []
+    for _ in range(n):
+        s = socket.socket()
+        s.bind(("127.0.0.1", 0))
+        socks.append(s)
+        out.append(s.getsockname()[1])
+    for s in socks:
+        s.close()
+    return out
+
+
+def test_flat_vs_shift_reference_dumps(tmp_path):
+    common = ["--model", "tiny", "--device", "cpu", "--seq-len", "64", "--batch", "2", "--data", "random",
+              "--reference-dump", "1,2,3", "--communication-timeout", "20"]
+    flat_dir = tmp_path / "flat"
+    sp.run([sys.executable, "-m", "shift_b200.ft.train", "--session", "flat", "--replica", "0", "--root",
+            str(tmp_path), "--lighthouse", "127.0.0.1:1", "--mode", "flat", "--steps", "3", *common],
+           check=True, cwd=ROOT, timeout=300)
+    lh, mp, spb = _ports(3)
+    cfg = {"train_args": common, "lighthouse_port": lh, "master_port": mp,
+           "store_port_base": spb + 1000 if spb < 60000 else 20000, "min_replicas": 2,
+           "heartbeat_timeout_ms": 1000, "join_timeout_ms": 1000, "quorum_tick_ms": 20, "target_steps": 3}
+    cpath = tmp_path / "cfg.json"
+    cpath.write_text(json.dumps(cfg))
+    s = Session(tmp_path, "shift", cpath, replicas=2, seconds=300)
+    s.start(timeout=200)
+    try:
+        s.await_(lambda: all(s.last_step(r) >= 3 for r in (0, 1)), 200, "3 steps")
+    finally:
+        s.finish()
+    res = compare_runs(flat_dir, tmp_path / "shift", steps=[1, 2, 3])
+    assert res["pass"], json.dumps(res, default=str)[:2000]
+    # the oracle is sensitive: a perturbed model fails it
+    p = torch.load(flat_dir / "reference_step3_r0.pt", weights_only=False)
+    name = next(iter(p["model"]))
+    p["model"][name] = p["model"][name] + 1e-3
+    torch.save(p, flat_dir / "reference_step3_r0.pt")
+    assert not compare_runs(flat_dir, tmp_path / "shift", steps=[3])["pass"]

@@ -44,3 +44,7 @@ def test_kill_at_step_5_heal_and_audit(tmp_path):
     res = verify(tmp_path / "tiny", replicas=2, ranks=1)
     failed = {k: v for k, v in res["checks"].items() if not v["pass"]}
     assert res["pass"], failed
+    from shift_b200.analysis.latency import summarize
+    lat = summarize(tmp_path / "tiny")
+    assert lat["faults"] == 1 and lat["fault_to_joint_s"]["median"] > 0
+    assert lat["commit_intervals"]["0"]["commits"] > 5

@@ -61,3 +61,6 @@ def test_three_rotation_cycles_with_audits(tmp_path, variant):
     assert res["pass"], failed
     assert len(res["rounds"]) == 3 and all(r.get("handoff_interval_s", 0) > 0 for r in res["rounds"])
     assert all(rc == 0 for rc in res["returncodes"].values()), res["returncodes"]
+    from shift_b200.analysis.verify_rotation import verify
+    ver = verify(s.dir, variant=variant)
+    assert ver["pass"], {k: v for k, v in ver["checks"].items() if not v["pass"]}

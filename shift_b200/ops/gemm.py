@@ -25,18 +25,37 @@ ROW_GROUPS, K_GROUPS = 0, 1
 EPI_BF16, EPI_F32, EPI_ACC_BF16, EPI_ACC_F32, EPI_SWIGLU = 0, 1, 2, 3, 4
 
 
-def pick_bn(n: int) -> int:
-    """Tile width with the least padding of N (ties -> wider tile)."""
-    best, waste = 256, None
+_SMS = 148
+# relative mainloop efficiency of a tile width (shared-memory operand traffic
+# per MMA flop grows as tiles narrow)
+_BN_COST = {256: 1.0, 192: 0.97, 128: 0.93}
+
+
+def pick_bn(n: int, tiles_m: int | None = None, sms: int = _SMS) -> int:
+    """Tile width maximising (useful columns / padded columns) x (full waves
+    / started waves of the persistent grid) x the width's own efficiency.
+    Without the row-tile count only the column padding is considered."""
+    best, score = 256, -1.0
     for bn in (256, 192, 128):
-        w = -(-n // bn) * bn - n
-        if waste is None or w < waste:
-            best, waste = bn, w
+        tn = -(-n // bn)
+        s = n / (tn * bn) * _BN_COST[bn]
+        if tiles_m:
+            tiles = tiles_m * tn
+            waves = tiles / sms
+            s *= waves / (-(-tiles // sms))
+        if s > score + 1e-9:
+            best, score = bn, s
     return best
 
 
 def _run(A, B, D, D2, offs, M, N, K, G, mode, a_mn, b_mn, epi, alpha, max_rows, xchg=(), tp=()):
-    ext().gemm(A, B, D, D2, offs, M, N, K, G, mode, a_mn, b_mn, epi, float(alpha), pick_bn(N),
+    tiles_m = -(-max_rows // 128) if mode == ROW_GROUPS else G * -(-M // 128)
+    if mode == ROW_GROUPS and G > 1:
+        tiles_m = None                  # grouped: the row split is data dependent
+    bn = pick_bn(N, tiles_m)
+    if epi == EPI_SWIGLU and bn == 256 and N % 192 == 0:
+        bn = 192                        # the SwiGLU activation is staged for TMA stores below 256
+    ext().gemm(A, B, D, D2, offs, M, N, K, G, mode, a_mn, b_mn, epi, float(alpha), bn,
                status_word(A.device), max_rows, list(xchg), list(tp))
 
 

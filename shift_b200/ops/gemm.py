@@ -28,7 +28,7 @@ EPI_BF16, EPI_F32, EPI_ACC_BF16, EPI_ACC_F32, EPI_SWIGLU = 0, 1, 2, 3, 4
 _SMS = 148
 # relative mainloop efficiency of a tile width (shared-memory operand traffic
 # per MMA flop grows as tiles narrow)
-_BN_COST = {256: 1.0, 192: 0.97, 128: 0.93}
+_BN_COST = {256: 1.0, 192: 0.95, 128: 0.7}     # measured: 128-wide tiles lose ~25 % at K = 1024
 
 
 def pick_bn(n: int, tiles_m: int | None = None, sms: int = _SMS) -> int:

@@ -460,6 +460,33 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             reinterpret_cast<bf16x8*>(out2)[0] = float_to_bf16x8(a);
             reinterpret_cast<bf16x8*>(out2)[1] = float_to_bf16x8(a + 8);
           } break;
+          case kEpiSwiGLUBwd: {
+            // accumulator columns [col, col+32) = d(activation) of features col..col+31,
+            // i.e. h / dh columns [2 col, 2 col + 64): two 16-feature groups of
+            // (16 gate, 16 up)
+            const __nv_bfloat16* hrow = reinterpret_cast<const __nv_bfloat16*>(p.D2) + row * p.ldd2 + 2 * col;
+            __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(Dst) + row * p.ldd + 2 * col;
+#pragma unroll
+            for (int gq = 0; gq < 2; ++gq) {
+              float g[16], u[16], dg[16], du[16];
+              bf16x8_to_float(reinterpret_cast<const bf16x8*>(hrow + 32 * gq)[0], g);
+              bf16x8_to_float(reinterpret_cast<const bf16x8*>(hrow + 32 * gq)[1], g + 8);
+              bf16x8_to_float(reinterpret_cast<const bf16x8*>(hrow + 32 * gq)[2], u);
+              bf16x8_to_float(reinterpret_cast<const bf16x8*>(hrow + 32 * gq)[3], u + 8);
+#pragma unroll
+              for (int q = 0; q < 16; ++q) {
+                const float d = f[16 * gq + q];
+                const float sg = __fdividef(1.f, 1.f + __expf(-g[q]));
+                du[q] = d * g[q] * sg;
+                dg[q] = d * u[q] * sg * (1.f + g[q] * (1.f - sg));
+              }
+              bf16x8* o = reinterpret_cast<bf16x8*>(out + 32 * gq);
+              o[0] = float_to_bf16x8(dg);
+              o[1] = float_to_bf16x8(dg + 8);
+              o[2] = float_to_bf16x8(du);
+              o[3] = float_to_bf16x8(du + 8);
+            }
+          } break;
           default: break;
         }
       }

@@ -193,6 +193,11 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const c10::op
   if (epi == kEpiSwiGLU) {
     TORCH_CHECK(D2.has_value() && N % 32 == 0 && mode == kRowGroups, "gemm: SwiGLU epilogue needs D2, N%32==0");
   }
+  if (epi == kEpiSwiGLUBwd) {
+    TORCH_CHECK(D2.has_value() && N % 32 == 0 && mode == kRowGroups && D.size(-1) == 2 * N &&
+                    D2->size(-1) == 2 * N && D2->stride(-1) == 1,
+                "gemm: SwiGLU-backward epilogue needs h [rows, 2N] (D2) and dh [rows, 2N] (D), N % 32 == 0");
+  }
   const bool f32_out = (epi == kEpiF32 || epi == kEpiAccF32);
   TORCH_CHECK(D.scalar_type() == (f32_out ? at::kFloat : at::kBFloat16), "gemm: output dtype does not match epilogue");
   const at::cuda::CUDAGuard guard(A.device());

@@ -12,6 +12,7 @@ enum Epilogue : int {
   kEpiAccBF16 = 2,  // D = bf16(D + alpha * acc)
   kEpiAccF32 = 3,   // D += alpha * acc (fp32)
   kEpiSwiGLU = 4,   // D = bf16(acc) (interleaved gate/up), D2 = silu(gate) * up
+  kEpiSwiGLUBwd = 5,  // acc = dact [rows, F]; D2 = h (interleaved gate/up, input) -> D = dh [rows, 2F]
 };
 
 void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const c10::optional<at::Tensor>& D2,

@@ -22,7 +22,7 @@ import torch
 from ._ext import ext, status_word
 
 ROW_GROUPS, K_GROUPS = 0, 1
-EPI_BF16, EPI_F32, EPI_ACC_BF16, EPI_ACC_F32, EPI_SWIGLU = 0, 1, 2, 3, 4
+EPI_BF16, EPI_F32, EPI_ACC_BF16, EPI_ACC_F32, EPI_SWIGLU, EPI_SWIGLU_BWD = 0, 1, 2, 3, 4, 5
 
 
 _SMS = 148
@@ -172,6 +172,20 @@ def grouped_dgrad(dy: torch.Tensor, w: torch.Tensor, offs: torch.Tensor) -> torc
     out = torch.empty(R, K, dtype=dy.dtype, device=dy.device)
     _run(dy, w.view(G * N, K), out, None, offs, R, K, N, G, ROW_GROUPS, False, True, EPI_BF16, 1.0, R)
     return out
+
+
+def grouped_dgrad_swiglu(dy: torch.Tensor, w: torch.Tensor, offs: torch.Tensor, h: torch.Tensor) -> torch.Tensor:
+    """dh = swiglu'(h) applied to dact = dy[r] @ w[g], in the GEMM epilogue:
+    dy [R, N], w [G, N, F], h [R, 2F] (interleaved gate/up) -> dh [R, 2F].
+    The activation gradient never leaves the chip."""
+    G, N, F = w.shape
+    R = dy.shape[0]
+    if not dy.is_cuda:
+        from . import functional as Fn
+        return Fn.swiglu_bwd(h, grouped_dgrad(dy, w, offs))
+    dh = torch.empty(R, 2 * F, dtype=dy.dtype, device=dy.device)
+    _run(dy, w.view(G * N, F), dh, h, offs, R, F, N, G, ROW_GROUPS, False, True, EPI_SWIGLU_BWD, 1.0, R)
+    return dh
 
 
 def grouped_wgrad(dy: torch.Tensor, x: torch.Tensor, offs: torch.Tensor, dw: torch.Tensor,

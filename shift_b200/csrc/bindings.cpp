@@ -75,8 +75,6 @@ void peer_copy(int64_t src_ptr, int64_t dst_ptr, int64_t nbytes);
 void xcopy(int64_t src_ptr, int64_t dst_ptr, int64_t nbytes, const std::vector<int64_t>& xchg,
            const at::Tensor& status);
 std::string fingerprint(const at::Tensor& t);
-void pair_reduce_scatter(int64_t a_ptr, int64_t b_ptr, at::Tensor& out, const std::vector<int64_t>& flag_ptrs,
-                         int64_t target, const at::Tensor& status, double timeout_s);
 }  // namespace coll
 }  // namespace sb
 
@@ -128,7 +126,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("reduce_slice_scatter", &sb::coll::reduce_slice_scatter, "K1 phase A: reduce-scatter + all-gather via P2P");
   m.def("flag_wait", &sb::coll::flag_wait);
   m.def("peer_copy", &sb::coll::peer_copy, "K10: SM-driven peer-memory copy");
-  m.def("pair_reduce_scatter", &sb::coll::pair_reduce_scatter);
   m.def("xcopy", &sb::coll::xcopy, "copy to a local and a peer destination with TP exchange wait/signal");
   m.def("fingerprint", &sb::coll::fingerprint, "deterministic 64-bit fingerprint of a tensor's bytes");
 }

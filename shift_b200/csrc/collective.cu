@@ -253,25 +253,6 @@ __global__ void xcopy_kernel(const uint4* __restrict__ src, uint4* __restrict__ 
   xchg_signal(xc);
 }
 
-// Two-rank reduce-scatter of bf16 rows over peer memory: out = mine[half] + peer[half]
-// (fixed order: rank-0 operand first), optional flag wait on the peer.
-__global__ void pair_reduce_scatter_kernel(const __nv_bfloat16* __restrict__ a, const __nv_bfloat16* __restrict__ b,
-                                           __nv_bfloat16* __restrict__ out, long n8, FlagPtrs f, int n_flags,
-                                           int target, int* status, uint64_t timeout_ns) {
-  if (n_flags > 0 && !cta_wait_flags(f, n_flags, target, status, timeout_ns)) return;
-  const long stride = static_cast<long>(gridDim.x) * blockDim.x;
-  for (long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8; i += stride) {
-    float x[8], y[8];
-    bf16x8_to_float(reinterpret_cast<const bf16x8*>(a)[i], x);
-    const uint4 u = __ldcv(reinterpret_cast<const uint4*>(b) + i);
-    bf16x8 bv;
-    bv.w[0] = u.x; bv.w[1] = u.y; bv.w[2] = u.z; bv.w[3] = u.w;
-    bf16x8_to_float(bv, y);
-#pragma unroll
-    for (int q = 0; q < 8; ++q) x[q] += y[q];
-    reinterpret_cast<bf16x8*>(out)[i] = float_to_bf16x8(x);
-  }
-}
 
 // ---------------------------------------------------------------------------
 // Deterministic 64-bit fingerprint of a byte range (FNV-1a over 32-bit words):
@@ -496,18 +477,6 @@ std::string fingerprint(const at::Tensor& t) {
   return std::string(buf);
 }
 
-void pair_reduce_scatter(int64_t a_ptr, int64_t b_ptr, at::Tensor& out, const std::vector<int64_t>& flag_ptrs,
-                         int64_t target, const at::Tensor& status, double timeout_s) {
-  const long n = out.numel();
-  TORCH_CHECK(n % 8 == 0, "pair_reduce_scatter: numel % 8");
-  const long blocks = std::min<long>((n / 8 + 255) / 256, static_cast<long>(sm_count()) * 4);
-  pair_reduce_scatter_kernel<<<std::max<long>(1, blocks), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      reinterpret_cast<const __nv_bfloat16*>(a_ptr), reinterpret_cast<const __nv_bfloat16*>(b_ptr),
-      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), n / 8, make_flags(flag_ptrs),
-      static_cast<int>(flag_ptrs.size()), static_cast<int>(target), status.data_ptr<int>(),
-      static_cast<uint64_t>(timeout_s * 1e9));
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
-}
 
 }  // namespace coll
 }  // namespace sb

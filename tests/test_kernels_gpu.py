@@ -76,12 +76,15 @@ def _segments(x, counts, offs):
     return x
 
 
-def test_grouped_fwd_dgrad_wgrad():
+# (1344, 1024): the expert w1 shape; (1024, 672): w2, whose data gradient has 672
+# columns (a partial last tile, clipped TMA stores)
+@pytest.mark.parametrize("N,K", [(1344, 1024), (1024, 672)])
+def test_grouped_fwd_dgrad_wgrad(N, K):
     torch.manual_seed(3)
     counts = [130, 0, 5, 256, 77]
     offs = _offsets(counts)
     R = int(offs[-1])
-    Gn, N, K = len(counts), 1344, 1024
+    Gn = len(counts)
     x = _segments(_bf(R, K), counts, offs)
     w = _bf(Gn, N, K, std=0.05)
     y = G.grouped_fwd(x, w, offs)

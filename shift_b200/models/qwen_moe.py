@@ -408,8 +408,7 @@ class QwenMoE:
         slot_of_row = Fn.invert_pos(c["pos"], cap)
         dy, dw_topk = Fn.combine_bwd(dout, c["y"], c["pos"], c["w"], c["row_src"], slot_of_row, c["total"])
         G.grouped_wgrad(dy, c["act"], c["offs"], st.g(p + "mlp.w2"), accumulate)
-        dact = G.grouped_dgrad(dy, st.w(p + "mlp.w2"), c["offs"])
-        dh = Fn.swiglu_bwd(c["hgu"], dact)
+        dh = G.grouped_dgrad_swiglu(dy, st.w(p + "mlp.w2"), c["offs"], c["hgu"])
         G.grouped_wgrad(dh, c["xp"], c["offs"], st.g(p + "mlp.w1"), accumulate)
         dxp = G.grouped_dgrad(dh, st.w(p + "mlp.w1"), c["offs"])
         dx = torch.empty_like(c["m_in"])

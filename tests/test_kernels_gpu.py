@@ -378,3 +378,25 @@ def test_norm_exchange_forms_single_gpu():
     _close(dw, gw)
     assert torch.equal(dx_out, dx_peer) and int(flags[3]) == 9
 
+
+
+def test_grouped_dgrad_with_swiglu_backward_epilogue():
+    """dh = swiglu'(h) . (dy @ w2) computed in the dgrad epilogue equals the
+    two-step form (dgrad, then the SwiGLU backward kernel)."""
+    torch.manual_seed(23)
+    counts = [200, 0, 130, 256]
+    offs = _offsets(counts)
+    R = int(offs[-1])
+    Gn, H, F = len(counts), 1024, 672
+    dy = _bf(R, H)
+    w2 = _bf(Gn, H, F, std=0.05)
+    h = _bf(R, 2 * F)
+    dh = G.grouped_dgrad_swiglu(dy, w2, offs, h)
+    ref_dh = Fn.swiglu_bwd(h, G.grouped_dgrad(dy, w2, offs))
+    torch.cuda.synchronize()
+    check_status()
+    o = offs.tolist()
+    for g in range(Gn):
+        s, e = o[g], o[g + 1]
+        if e > s:
+            _close(dh[s:e], ref_dh[s:e])

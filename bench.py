@@ -29,13 +29,14 @@ import json
 import os
 import statistics
 import subprocess
+import tempfile
 import sys
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-BASELINE_TOKENS_PER_S = 5591.0   # reference SHIFT 2x8 H800, 8 x 512 tokens / 0.7326 s median step
+REFERENCE_PUBLISHED_TOKENS_PER_S = 5591.0   # reference SHIFT 2x8 H800, 8 x 512 tokens / 0.7326 s median step
 GLOBAL_BATCH = 8
 SEQ = 2048
 METRIC = "tokens/s (device-timed, max over ranks)"
@@ -64,7 +65,7 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_bench_{os.getpid()}.csv")
+        self.path = os.path.join(tempfile.gettempdir(), f"shift_b200_clocks_{os.getpid()}.csv")
 
     def start(self):
         try:
@@ -228,7 +229,7 @@ def main():
             "ms_per_step": round(ms, 3),
             "higher_is_better": True,
             "scaling": "strong",
-            "vs_baseline": round(value / BASELINE_TOKENS_PER_S, 2),
+            "vs_baseline": round(value / REFERENCE_PUBLISHED_TOKENS_PER_S, 2),
             "dtype": "bf16",
             "data": "synthetic (uniform random token ids, random N(0,0.02) init)",
             "config": {"model": "qwen-moe-0.494b (12L, h1024, 16q/4kv x64, 16 experts top-4 ffn672, vocab 32768)",

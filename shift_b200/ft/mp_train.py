@@ -13,7 +13,7 @@ other replicas through its Manager (the cross-replica, fault-tolerant
 reduction), votes, and commits -- the reference's SHIFT step
 (shift_full/train.py:506-627) for a replica that is itself model-parallel.
 
-Unplanned fault (BASELINE config 5 semantics): ``--inject sigkill_bwd@STEP``
+Unplanned fault (one TP rank killed mid-backward): ``--inject sigkill_bwd@STEP``
 with ``--inject-rank K`` makes local rank K SIGKILL itself in the middle of
 the backward of STEP's last microbatch (``sigkill_step@STEP``: right after
 STEP's commit, the form used on GPUs).  The launcher then stops the rest of

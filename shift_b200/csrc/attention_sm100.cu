@@ -223,23 +223,28 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm, Params p) {
       if (ok) tc_fence_after();
       const uint32_t ts = tbase + (j & 1) * BN + lane_off;
       const bool diag = (j == qb);
-      // pass 1: row max of the raw scores over this warp's 64 columns (the
-      // causal mask only exists on the diagonal tile), scaled once, then
-      // combined with the partner warp's
+      // pass 1: this warp's 64 columns of S come out of TMEM once (two loads,
+      // one wait) and stay in registers for pass 2.  Row max over them (the
+      // causal mask only exists on the diagonal tile) in four independent
+      // chains, scaled once, then combined with the partner warp's.
+      uint32_t v[64];
       float mraw = -INFINITY;
-      uint32_t v[32];
-#pragma unroll 1
-      for (int c = half * 64; ok && c < half * 64 + 64; c += 32) {
-        tmem_ld_32x32b_x32(ts + c, v);
+      const int c_lo = half * 64;
+      if (ok) {
+        tmem_ld_32x32b_x32(ts + c_lo, v);
+        tmem_ld_32x32b_x32(ts + c_lo + 32, v + 32);
         tmem_wait_ld();
+        float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
         if (diag) {
+          const int lim = q - j * BN - c_lo;       // columns t <= lim are visible
 #pragma unroll
-          for (int t = 0; t < 32; ++t)
-            if (j * BN + c + t <= q) mraw = fmaxf(mraw, __uint_as_float(v[t]));
+          for (int t = 0; t < 64; ++t)
+            if (t <= lim) m4[t & 3] = fmaxf(m4[t & 3], __uint_as_float(v[t]));
         } else {
 #pragma unroll
-          for (int t = 0; t < 32; ++t) mraw = fmaxf(mraw, __uint_as_float(v[t]));
+          for (int t = 0; t < 64; ++t) m4[t & 3] = fmaxf(m4[t & 3], __uint_as_float(v[t]));
         }
+        mraw = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
       }
       float mx = fmaxf(m_run, mraw * p.scale_log2);
       s_max[((j & 1) * 2 + half) * BM + row] = mx;
@@ -247,36 +252,37 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm, Params p) {
       if (!ok) continue;
       mx = fmaxf(mx, s_max[((j & 1) * 2 + (half ^ 1)) * BM + row]);
       const float m_prev = m_run;
-      l_run = (m_prev == -INFINITY) ? 0.f : l_run * ex2(m_prev - mx);
       m_run = mx;
-      // pass 2: probabilities -> shared memory (bf16, swizzled)
+      // pass 2: probabilities -> shared memory (bf16, swizzled); the row sum
+      // of this tile in four independent chains
       uint8_t* pbuf = sP + (j & 1) * 2 * kTile;
-#pragma unroll 1
-      for (int c = half * 64; c < half * 64 + 64; c += 32) {
-        tmem_ld_32x32b_x32(ts + c, v);
-        tmem_wait_ld();
+      const float nmx = -mx;
+      float l4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
         float pr[32];
-        const float nmx = -mx;
         if (diag) {
+          const int lim = q - j * BN - c_lo - cc * 32;
 #pragma unroll
           for (int t = 0; t < 32; ++t) {
-            pr[t] = (j * BN + c + t > q) ? 0.f : ex2(fmaf(__uint_as_float(v[t]), p.scale_log2, nmx));
-            l_run += pr[t];
+            pr[t] = (t > lim) ? 0.f : ex2(fmaf(__uint_as_float(v[cc * 32 + t]), p.scale_log2, nmx));
+            l4[t & 3] += pr[t];
           }
         } else {
 #pragma unroll
           for (int t = 0; t < 32; ++t) {
-            pr[t] = ex2(fmaf(__uint_as_float(v[t]), p.scale_log2, nmx));
-            l_run += pr[t];
+            pr[t] = ex2(fmaf(__uint_as_float(v[cc * 32 + t]), p.scale_log2, nmx));
+            l4[t & 3] += pr[t];
           }
         }
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           bf16x8 pk = float_to_bf16x8(pr + 8 * u);
-          *reinterpret_cast<uint4*>(swz_chunk(pbuf, row, (c >> 3) + u)) =
+          *reinterpret_cast<uint4*>(swz_chunk(pbuf, row, ((c_lo + cc * 32) >> 3) + u)) =
               make_uint4(pk.w[0], pk.w[1], pk.w[2], pk.w[3]);
         }
       }
+      l_run = ((m_prev == -INFINITY) ? 0.f : l_run * ex2(m_prev - mx)) + ((l4[0] + l4[1]) + (l4[2] + l4[3]));
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&p_full[j & 1]);
@@ -493,11 +499,21 @@ dkdv_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUte
         mbar_arrive(&sdp_empty[k & 1]);                 // S/dP buffer may be overwritten by S_{k+2}
         const int c0 = hh * 64 + half * 32;             // column of the 128-query block
         float pt[32], dst[32];
+        // lse / delta of the 32 queries: eight 16-byte broadcast loads each
+        // (c0 is a multiple of 32 floats; the arrays start 1024-byte aligned)
+        const float4* cl4 = reinterpret_cast<const float4*>(cl + c0);
+        const float4* cd4 = reinterpret_cast<const float4*>(cd + c0);
 #pragma unroll
-        for (int t = 0; t < 32; ++t) {
-          const float pv = ex2(fmaf(__uint_as_float(vs[t]), p.scale_log2, -cl[c0 + t]));
-          pt[t] = pv;
-          dst[t] = pv * (__uint_as_float(vd[t]) - cd[c0 + t]);
+        for (int u = 0; u < 8; ++u) {
+          const float4 l = cl4[u], d = cd4[u];
+          const float la[4] = {l.x, l.y, l.z, l.w}, da[4] = {d.x, d.y, d.z, d.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int t = 4 * u + e;
+            const float pv = ex2(fmaf(__uint_as_float(vs[t]), p.scale_log2, -la[e]));
+            pt[t] = pv;
+            dst[t] = pv * (__uint_as_float(vd[t]) - da[e]);
+          }
         }
         if (qb == kb) {             // causal mask only on the diagonal block
 #pragma unroll

@@ -85,6 +85,17 @@ SB_DEVICE bf16x8 float_to_bf16x8(const float* f) {
 // ---------------------------------------------------------------------------
 // Shared-memory addressing
 // ---------------------------------------------------------------------------
+// 16-byte read-only load that the compiler may neither hoist out of a loop
+// nor merge with another: for small loop-invariant operands (a norm weight)
+// that should come from L1 each time instead of occupying registers.
+SB_DEVICE bf16x8 ld_nc_bf16x8(const void* p) {
+  bf16x8 v;
+  asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.w[0]), "=r"(v.w[1]), "=r"(v.w[2]), "=r"(v.w[3])
+               : "l"(p));
+  return v;
+}
+
 SB_DEVICE uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -84,8 +84,15 @@ rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __r
 // Tensor-parallel forms as in the forward: dy2 (a peer-written partial,
 // waited for through xc) is added to dy, and dx is also written to
 // xc.peer_out (a peer's gather buffer), then the kernel signals.
-template <int NV, bool kRes>
-__global__ void __launch_bounds__(kWarps * 32)
+//
+// A row's inputs stay in registers as packed bf16 (x, dy, dy2, dres all
+// loaded up front, so one memory latency per row), the fp32 values are
+// recomputed in the second pass, and each thread's dw partial sums live in
+// its own slots of the CTA's reduction buffer in shared memory, and the
+// weight is re-read from L1: at H = 1024 that keeps the kernel under 128
+// registers, two CTAs (16 warps) per SM instead of one.
+template <int NV, bool kRes, bool kDy2>
+__global__ void __launch_bounds__(kWarps * 32, 2)
 rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ dy2,
                    const __nv_bfloat16* __restrict__ x, const float* __restrict__ rstd,
                    const __nv_bfloat16* __restrict__ w, const __nv_bfloat16* __restrict__ dres,
@@ -98,54 +105,73 @@ rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __
   const int wib = threadIdx.x / 32;
   const int warp = blockIdx.x * kWarps + wib;
   const int nwarps = gridDim.x * kWarps;
-  float wv[NV][8], dwacc[NV][8];
+  // this thread's dw partials: red[wib][(i * 32 + lane) * 8 + j], touched by no other thread until the end
+  float4* dwacc = reinterpret_cast<float4*>(&red[wib][lane * 8]);
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
-    bf16x8_to_float(reinterpret_cast<const bf16x8*>(w)[i * 32 + lane], wv[i]);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) dwacc[i][j] = 0.f;
+    dwacc[i * 64] = make_float4(0.f, 0.f, 0.f, 0.f);
+    dwacc[i * 64 + 1] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
   for (int r = go ? warp : rows; r < rows; r += nwarps) {
     const float rs = rstd[r];
-    float xh[NV][8], g[NV][8];
-    float dot = 0.f;
+    const long ro = static_cast<long>(r) * H;
+    bf16x8 xp[NV], dp[NV], d2p[kDy2 ? NV : 1], rp[kRes ? NV : 1];
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
-      float dv[8];
-      bf16x8_to_float(reinterpret_cast<const bf16x8*>(x + static_cast<long>(r) * H)[i * 32 + lane], xh[i]);
-      bf16x8_to_float(reinterpret_cast<const bf16x8*>(dy + static_cast<long>(r) * H)[i * 32 + lane], dv);
-      if (dy2 != nullptr) {
+      xp[i] = reinterpret_cast<const bf16x8*>(x + ro)[i * 32 + lane];
+      dp[i] = reinterpret_cast<const bf16x8*>(dy + ro)[i * 32 + lane];
+      if constexpr (kDy2) d2p[i] = reinterpret_cast<const bf16x8*>(dy2 + ro)[i * 32 + lane];
+      if constexpr (kRes) rp[i] = reinterpret_cast<const bf16x8*>(dres + ro)[i * 32 + lane];
+    }
+    // the fp32 values of chunk i: xhat, dy (+ dy2), g = dy * w
+    auto chunk = [&](int i, float* xh, float* dv, float* g) {
+      float wv[8];
+      bf16x8_to_float(xp[i], xh);
+      bf16x8_to_float(dp[i], dv);
+      bf16x8_to_float(ld_nc_bf16x8(reinterpret_cast<const bf16x8*>(w) + i * 32 + lane), wv);
+      if constexpr (kDy2) {
         float d2[8];
-        bf16x8_to_float(reinterpret_cast<const bf16x8*>(dy2 + static_cast<long>(r) * H)[i * 32 + lane], d2);
+        bf16x8_to_float(d2p[i], d2);
 #pragma unroll
         for (int j = 0; j < 8; ++j) dv[j] += d2[j];
       }
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        xh[i][j] *= rs;
-        g[i][j] = dv[j] * wv[i][j];
-        dot += g[i][j] * xh[i][j];
-        dwacc[i][j] += dv[j] * xh[i][j];
+        xh[j] *= rs;
+        g[j] = dv[j] * wv[j];
+      }
+    };
+    float dot = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      float xh[8], dv[8], g[8];
+      chunk(i, xh, dv, g);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) dot += g[j] * xh[j];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        float4 a = dwacc[i * 64 + u];
+        a.x += dv[4 * u] * xh[4 * u];
+        a.y += dv[4 * u + 1] * xh[4 * u + 1];
+        a.z += dv[4 * u + 2] * xh[4 * u + 2];
+        a.w += dv[4 * u + 3] * xh[4 * u + 3];
+        dwacc[i * 64 + u] = a;
       }
     }
     dot = warp_sum(dot) / H;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
-      float o[8];
-      float rr[8];
-      if (kRes) bf16x8_to_float(reinterpret_cast<const bf16x8*>(dres + static_cast<long>(r) * H)[i * 32 + lane], rr);
+      float xh[8], dv[8], g[8], o[8], rr[8];
+      chunk(i, xh, dv, g);
+      if constexpr (kRes) bf16x8_to_float(rp[i], rr);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) o[j] = rs * (g[i][j] - xh[i][j] * dot) + (kRes ? rr[j] : 0.f);
+      for (int j = 0; j < 8; ++j) o[j] = rs * (g[j] - xh[j] * dot) + (kRes ? rr[j] : 0.f);
       const bf16x8 ov = float_to_bf16x8(o);
-      reinterpret_cast<bf16x8*>(dx + static_cast<long>(r) * H)[i * 32 + lane] = ov;
-      if (dx_peer != nullptr) reinterpret_cast<bf16x8*>(dx_peer + static_cast<long>(r) * H)[i * 32 + lane] = ov;
+      reinterpret_cast<bf16x8*>(dx + ro)[i * 32 + lane] = ov;
+      if (dx_peer != nullptr) reinterpret_cast<bf16x8*>(dx_peer + ro)[i * 32 + lane] = ov;
     }
   }
   xchg_signal(xc);
-#pragma unroll
-  for (int i = 0; i < NV; ++i)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) red[wib][(i * 32 + lane) * 8 + j] = dwacc[i][j];
   __syncthreads();
   for (int c = threadIdx.x; c < H; c += blockDim.x) {
     float s = 0.f;
@@ -279,11 +305,16 @@ at::Tensor rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tens
   auto wp = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
   auto rp = res ? reinterpret_cast<const __nv_bfloat16*>(dres->data_ptr()) : nullptr;
   auto dxp = reinterpret_cast<__nv_bfloat16*>(dx.data_ptr());
-#define SB_LAUNCH(NV)                                                                                       \
-  if (res) rmsnorm_bwd_kernel<NV, true><<<blocks, kWarps * 32, 0, stream>>>(dyp, dy2p, xp, rstd.data_ptr<float>(), wp, rp, dxp, partial.data_ptr<float>(), rows, xc, st); \
-  else rmsnorm_bwd_kernel<NV, false><<<blocks, kWarps * 32, 0, stream>>>(dyp, dy2p, xp, rstd.data_ptr<float>(), wp, rp, dxp, partial.data_ptr<float>(), rows, xc, st);
+#define SB_BWD(NV, R, D2) \
+  rmsnorm_bwd_kernel<NV, R, D2><<<blocks, kWarps * 32, 0, stream>>>(dyp, dy2p, xp, rstd.data_ptr<float>(), wp, rp, dxp, partial.data_ptr<float>(), rows, xc, st)
+#define SB_LAUNCH(NV)                  \
+  if (res && dy2p) SB_BWD(NV, true, true);      \
+  else if (res) SB_BWD(NV, true, false);        \
+  else if (dy2p) SB_BWD(NV, false, true);       \
+  else SB_BWD(NV, false, false);
   SB_NORM_DISPATCH(H, SB_LAUNCH)
 #undef SB_LAUNCH
+#undef SB_BWD
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   float* of = dw_out.scalar_type() == at::kFloat ? dw_out.data_ptr<float>() : nullptr;
   __nv_bfloat16* ob = dw_out.scalar_type() == at::kBFloat16 ? reinterpret_cast<__nv_bfloat16*>(dw_out.data_ptr()) : nullptr;

@@ -18,28 +18,37 @@ namespace xent {
 
 // One block per row.  loss[r] = logsumexp(z) - z[label]; dz = (softmax - onehot) * scale
 // written over the logits (bf16) in place.  Rows with label < 0 get loss 0, dz 0.
+// The row is staged as bf16 in shared memory (each thread only reads back the
+// vectors it stored, so no barrier is needed for it) and exp(z - max) is
+// evaluated twice (row sum, then gradient) instead of being kept in fp32
+// registers: three CTAs per SM overlap one row's reductions with the other
+// rows' loads and stores.  Max and sum run in four independent chains.
 template <int VPT>  // bf16x8 vectors per thread
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 3)
 xent_kernel(__nv_bfloat16* __restrict__ logits, const int* __restrict__ labels, int V, float scale,
             float* __restrict__ loss, int label_lo) {
+  extern __shared__ bf16x8 srow[];   // V / 8 vectors
   const long r = blockIdx.x;
   __nv_bfloat16* row = logits + r * V;
   const int label = labels[r];
   const int vecs = V / 8;
-  float z[VPT][8];
-  float mx = -INFINITY;
+  float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int v = threadIdx.x + i * blockDim.x;
+    if (v < vecs) srow[v] = reinterpret_cast<const bf16x8*>(row)[v];
+  }
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int v = threadIdx.x + i * blockDim.x;
     if (v < vecs) {
-      bf16x8_to_float(reinterpret_cast<const bf16x8*>(row)[v], z[i]);
+      float z[8];
+      bf16x8_to_float(srow[v], z);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) mx = fmaxf(mx, z[i][j]);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) z[i][j] = -INFINITY;
+      for (int j = 0; j < 8; ++j) m4[j & 3] = fmaxf(m4[j & 3], z[j]);
     }
   }
+  float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
   __shared__ float red[32];
   __shared__ float bcast;
   mx = warp_max(mx);
@@ -52,14 +61,18 @@ xent_kernel(__nv_bfloat16* __restrict__ logits, const int* __restrict__ labels, 
   }
   __syncthreads();
   mx = bcast;
-  float s = 0.f;
+  float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-  for (int i = 0; i < VPT; ++i)
+  for (int i = 0; i < VPT; ++i) {
+    const int v = threadIdx.x + i * blockDim.x;
+    if (v < vecs) {
+      float z[8];
+      bf16x8_to_float(srow[v], z);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      z[i][j] = __expf(z[i][j] - mx);
-      s += z[i][j];
+      for (int j = 0; j < 8; ++j) s4[j & 3] += __expf(z[j] - mx);
     }
+  }
+  float s = (s4[0] + s4[1]) + (s4[2] + s4[3]);
   s = warp_sum(s);
   __syncthreads();
   if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = s;
@@ -88,11 +101,12 @@ xent_kernel(__nv_bfloat16* __restrict__ logits, const int* __restrict__ labels, 
   for (int i = 0; i < VPT; ++i) {
     const int v = threadIdx.x + i * blockDim.x;
     if (v < vecs) {
-      float g[8];
+      float z[8], g[8];
+      bf16x8_to_float(srow[v], z);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const int col = v * 8 + j;
-        g[j] = (z[i][j] * inv - ((valid && col == lab) ? 1.f : 0.f)) * sc;
+        g[j] = (__expf(z[j] - mx) * inv - ((valid && col == lab) ? 1.f : 0.f)) * sc;
       }
       reinterpret_cast<bf16x8*>(row)[v] = float_to_bf16x8(g);
     }
@@ -112,10 +126,19 @@ at::Tensor xent_fwd_bwd(at::Tensor& logits, const at::Tensor& labels, double sca
   auto stream = at::cuda::getCurrentCUDAStream();
   auto lp = reinterpret_cast<__nv_bfloat16*>(logits.data_ptr());
   if (rows == 0) return loss;
-  if (vecs <= 256 * 2) xent_kernel<2><<<rows, 256, 0, stream>>>(lp, labels.data_ptr<int>(), V, (float)scale, loss.data_ptr<float>(), (int)label_lo);
-  else if (vecs <= 256 * 8) xent_kernel<8><<<rows, 256, 0, stream>>>(lp, labels.data_ptr<int>(), V, (float)scale, loss.data_ptr<float>(), (int)label_lo);
-  else if (vecs <= 256 * 16) xent_kernel<16><<<rows, 256, 0, stream>>>(lp, labels.data_ptr<int>(), V, (float)scale, loss.data_ptr<float>(), (int)label_lo);
+  const size_t smem = static_cast<size_t>(V) * sizeof(__nv_bfloat16);
+#define SB_XENT(VPT)                                                                                  \
+  do {                                                                                                \
+    C10_CUDA_CHECK(cudaFuncSetAttribute(xent_kernel<VPT>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                        256 * 8 * VPT * static_cast<int>(sizeof(__nv_bfloat16))));    \
+    xent_kernel<VPT><<<rows, 256, smem, stream>>>(lp, labels.data_ptr<int>(), V, (float)scale,         \
+                                                  loss.data_ptr<float>(), (int)label_lo);             \
+  } while (0)
+  if (vecs <= 256 * 2) SB_XENT(2);
+  else if (vecs <= 256 * 8) SB_XENT(8);
+  else if (vecs <= 256 * 16) SB_XENT(16);
   else TORCH_CHECK(false, "xent: vocabulary too large for one block (max 32768)");
+#undef SB_XENT
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return loss;
 }

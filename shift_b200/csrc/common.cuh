@@ -27,6 +27,11 @@ enum Status : int {
   kBadShape = 3,          // a kernel met a size it was not built for
 };
 
+// Host-side check for kernels that move 16-byte vectors: the base address
+// (and therefore, with a row length that is a multiple of 8 bf16, every row)
+// must be 16-byte aligned, or the vector accesses would fault.
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
 SB_DEVICE uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));

@@ -39,11 +39,21 @@ router_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restri
   const int lane = threadIdx.x % 32;
   const int warp = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int nwarps = gridDim.x * (blockDim.x / 32);
+  // the next token's row is loaded while this one is computed
+  bf16x8 xn[NV];
+  if (warp < T) {
+#pragma unroll
+    for (int i = 0; i < NV; ++i) xn[i] = reinterpret_cast<const bf16x8*>(x + static_cast<long>(warp) * H)[i * 32 + lane];
+  }
   for (int t = warp; t < T; t += nwarps) {
     float xv[NV][8];
 #pragma unroll
-    for (int i = 0; i < NV; ++i)
-      bf16x8_to_float(reinterpret_cast<const bf16x8*>(x + static_cast<long>(t) * H)[i * 32 + lane], xv[i]);
+    for (int i = 0; i < NV; ++i) bf16x8_to_float(xn[i], xv[i]);
+    if (t + nwarps < T) {
+#pragma unroll
+      for (int i = 0; i < NV; ++i)
+        xn[i] = reinterpret_cast<const bf16x8*>(x + static_cast<long>(t + nwarps) * H)[i * 32 + lane];
+    }
     float logit[E];
 #pragma unroll
     for (int e = 0; e < E; ++e) {
@@ -69,33 +79,33 @@ router_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restri
     const float inv = 1.f / s;
 #pragma unroll
     for (int e = 0; e < E; ++e) p[e] *= inv;
-    if (lane < E) {
-      float v = 0.f;
+    // lane e < E holds p[e] and its rank: the number of experts before it in
+    // the order (larger probability first, lower index on ties); the top k are
+    // the lanes of rank < k, and lane j < k writes the pick of rank j.
+    float mine = 0.f;
 #pragma unroll
-      for (int e = 0; e < E; ++e) if (e == lane) v = p[e];
-      probs[static_cast<long>(t) * E + lane] = v;
+    for (int e = 0; e < E; ++e) if (e == lane) mine = p[e];
+    int rank = 0;
+#pragma unroll
+    for (int e = 0; e < E; ++e) rank += (p[e] > mine || (p[e] == mine && e < lane)) ? 1 : 0;
+    if (lane < E) probs[static_cast<long>(t) * E + lane] = mine;
+    // picks in rank order, and their sum in that order in every lane
+    float wsum = 0.f, my_sel = 0.f;
+    int my_idx = 0;
+    for (int j = 0; j < k; ++j) {
+      const unsigned m = __ballot_sync(0xffffffffu, lane < E && rank == j);
+      const int src = __ffs(m) - 1;
+      const float v = __shfl_sync(0xffffffffu, mine, src);
+      wsum += v;
+      if (lane == j) {
+        my_sel = v;
+        my_idx = src;
+      }
     }
-    if (lane == 0) {
-      unsigned used = 0;
-      float wsum = 0.f;
-      float sel[16];
-      int idx[16];
-      for (int j = 0; j < k; ++j) {
-        int best = -1;
-        float bv = -1.f;
-#pragma unroll
-        for (int e = 0; e < E; ++e)
-          if (!((used >> e) & 1u) && p[e] > bv) { bv = p[e]; best = e; }
-        used |= 1u << best;
-        idx[j] = best;
-        sel[j] = bv;
-        wsum += bv;
-      }
-      const float norm = normalize ? 1.f / wsum : 1.f;
-      for (int j = 0; j < k; ++j) {
-        topk_idx[static_cast<long>(t) * k + j] = idx[j];
-        topk_w[static_cast<long>(t) * k + j] = sel[j] * norm;
-      }
+    const float norm = normalize ? 1.f / wsum : 1.f;
+    if (lane < k) {
+      topk_idx[static_cast<long>(t) * k + lane] = my_idx;
+      topk_w[static_cast<long>(t) * k + lane] = my_sel * norm;
     }
   }
 }
@@ -202,12 +212,25 @@ router_dgrad_kernel(const __nv_bfloat16* __restrict__ wr, const float* __restric
   const int lane = threadIdx.x % 32;
   const int warp = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int nwarps = gridDim.x * (blockDim.x / 32);
+  // the next token's dx row and dlogits are loaded while this one is computed
+  bf16x8 dn[NV];
+  float dl_next = 0.f;
+  if (warp < T) {
+#pragma unroll
+    for (int i = 0; i < NV; ++i) dn[i] = reinterpret_cast<const bf16x8*>(dx + static_cast<long>(warp) * H)[i * 32 + lane];
+    dl_next = lane < E ? dlogits[static_cast<long>(warp) * E + lane] : 0.f;
+  }
   for (int t = warp; t < T; t += nwarps) {
     float dxv[NV][8];
 #pragma unroll
-    for (int i = 0; i < NV; ++i)
-      bf16x8_to_float(reinterpret_cast<const bf16x8*>(dx + static_cast<long>(t) * H)[i * 32 + lane], dxv[i]);
-    const float my_dl = lane < E ? dlogits[static_cast<long>(t) * E + lane] : 0.f;
+    for (int i = 0; i < NV; ++i) bf16x8_to_float(dn[i], dxv[i]);
+    const float my_dl = dl_next;
+    if (t + nwarps < T) {
+#pragma unroll
+      for (int i = 0; i < NV; ++i)
+        dn[i] = reinterpret_cast<const bf16x8*>(dx + static_cast<long>(t + nwarps) * H)[i * 32 + lane];
+      dl_next = lane < E ? dlogits[static_cast<long>(t + nwarps) * E + lane] : 0.f;
+    }
 #pragma unroll
     for (int e = 0; e < E; ++e) {
       const float dl = __shfl_sync(0xffffffffu, my_dl, e);
@@ -249,16 +272,27 @@ router_wgrad_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict
     for (int e = 0; e < E; ++e)
 #pragma unroll
       for (int q = 0; q < 4; ++q) acc[e][q] = 0.f;
-    for (int tt = 0; tt < nt; ++tt) {
-      const uint2 raw = *reinterpret_cast<const uint2*>(x + static_cast<long>(t0 + tt) * H + h);
-      const float2 a = unpack_bf16x2(raw.x), b = unpack_bf16x2(raw.y);
+    // eight tokens' loads in flight at a time (the accumulation order over
+    // tokens is unchanged)
+    constexpr int U = 8;
+    for (int tb = 0; tb < nt; tb += U) {
+      uint2 raw[U];
 #pragma unroll
-      for (int e = 0; e < E; ++e) {
-        const float dl = sdl[tt][e];
-        acc[e][0] += dl * a.x;
-        acc[e][1] += dl * a.y;
-        acc[e][2] += dl * b.x;
-        acc[e][3] += dl * b.y;
+      for (int u = 0; u < U; ++u)
+        raw[u] = tb + u < nt ? *reinterpret_cast<const uint2*>(x + static_cast<long>(t0 + tb + u) * H + h)
+                             : make_uint2(0u, 0u);
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (tb + u >= nt) break;
+        const float2 a = unpack_bf16x2(raw[u].x), b = unpack_bf16x2(raw[u].y);
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const float dl = sdl[tb + u][e];
+          acc[e][0] += dl * a.x;
+          acc[e][1] += dl * a.y;
+          acc[e][2] += dl * b.x;
+          acc[e][3] += dl * b.y;
+        }
       }
     }
     float* out = partial + static_cast<long>(blockIdx.x) * E * H;
@@ -348,18 +382,38 @@ __global__ void sort_rank_kernel(const int* __restrict__ keys, int n, int lo, in
   if (last) chunk_counts[static_cast<long>(c) * nbins + key] = r + 1;
 }
 
-__global__ void sort_chunk_scan_kernel(int* __restrict__ chunk_counts, int nchunks, int nbins,
-                                       int* __restrict__ bin_totals) {
-  const int b = blockIdx.x * blockDim.x + threadIdx.x;
-  if (b >= nbins) return;
-  int run = 0;
-  for (int c = 0; c < nchunks; ++c) {
+// One CTA per bin: exclusive scan of the bin's column of chunk counts, in
+// tiles of 256 chunks (warp shuffles + 8 warp totals), carried across tiles.
+__global__ void __launch_bounds__(256)
+sort_chunk_scan_kernel(int* __restrict__ chunk_counts, int nchunks, int nbins, int* __restrict__ bin_totals) {
+  __shared__ int warp_tot[8];
+  const int b = blockIdx.x;
+  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
+  int carry = 0;
+  for (int base = 0; base < nchunks; base += 256) {
+    const int c = base + threadIdx.x;
     const long o = static_cast<long>(c) * nbins + b;
-    const int v = chunk_counts[o];
-    chunk_counts[o] = run;
-    run += v;
+    const int v = c < nchunks ? chunk_counts[o] : 0;
+    int x = v;   // inclusive scan within the warp
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, d);
+      if (lane >= d) x += y;
+    }
+    if (lane == 31) warp_tot[warp] = x;
+    __syncthreads();
+    int before = 0, tile = 0;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      const int t = warp_tot[w];
+      if (w < warp) before += t;
+      tile += t;
+    }
+    if (c < nchunks) chunk_counts[o] = carry + before + x - v;
+    carry += tile;
+    __syncthreads();   // warp_tot is rewritten by the next tile
   }
-  bin_totals[b] = run;
+  if (threadIdx.x == 0) bin_totals[b] = carry;
 }
 
 // Single block exclusive scan of padded bin totals -> offs[nbins+1].
@@ -437,8 +491,8 @@ std::vector<at::Tensor> bucket_sort(const at::Tensor& keys, int64_t lo, int64_t 
     sort_rank_kernel<<<nchunks, kChunk, 0, stream>>>(keys.data_ptr<int>(), n, (int)lo, (int)hi, rank.data_ptr<int>(),
                                                      chunk.data_ptr<int>(), nbins);
   }
-  sort_chunk_scan_kernel<<<(nbins + 255) / 256, 256, 0, stream>>>(chunk.data_ptr<int>(), nchunks, nbins,
-                                                                 totals.data_ptr<int>());
+  if (nbins > 0)
+    sort_chunk_scan_kernel<<<nbins, 256, 0, stream>>>(chunk.data_ptr<int>(), nchunks, nbins, totals.data_ptr<int>());
   sort_bin_scan_kernel<<<1, 1024, 0, stream>>>(totals.data_ptr<int>(), nbins, (int)pad, offs.data_ptr<int>(),
                                                counts.data_ptr<int>());
   if (n > 0) {

@@ -26,7 +26,7 @@ constexpr int kWarps = 8;
 // all-gather into the norm that produces its input, and the reduce-scatter's
 // reduction into the norm that consumes it.
 template <int NV, bool kAdd>
-__global__ void __launch_bounds__(kWarps * 32)
+__global__ void __launch_bounds__(kWarps * 32, 3)
 rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ delta,
                    const __nv_bfloat16* __restrict__ delta2, const __nv_bfloat16* __restrict__ w,
                    __nv_bfloat16* __restrict__ h_out, __nv_bfloat16* __restrict__ y, float* __restrict__ rstd_out,
@@ -205,12 +205,14 @@ column_reduce_kernel(const float* __restrict__ partial, int nblocks, int cols, f
   if (out_bf16) out_bf16[c] = __float2bfloat16(accumulate ? __bfloat162float(out_bf16[c]) + t : t);
 }
 
-static int blocks_for(int rows) {
+// Grid of a row-per-warp norm kernel: every row gets a warp, capped at the
+// CTAs that are resident at once (per_sm per SM), which then loop over rows.
+static int blocks_for(int rows, int per_sm) {
   int dev;
   cudaGetDevice(&dev);
   int sms;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  return std::max(1, std::min((rows + kWarps - 1) / kWarps, sms * 2));
+  return std::max(1, std::min((rows + kWarps - 1) / kWarps, sms * per_sm));
 }
 
 #define SB_NORM_DISPATCH(H, MACRO) \
@@ -255,7 +257,11 @@ std::vector<at::Tensor> rmsnorm_fwd(const at::Tensor& x, const c10::optional<at:
     TORCH_CHECK(delta->is_contiguous() && delta->sizes() == x.sizes(), "rmsnorm: delta shape");
     h = at::empty_like(x);
   }
-  const int blocks = blocks_for(rows);
+  TORCH_CHECK(aligned16(x.data_ptr()) && aligned16(w.data_ptr()) && aligned16(y.data_ptr()) &&
+                  (!add || (aligned16(delta->data_ptr()) && aligned16(h.data_ptr()))) &&
+                  (d2p == nullptr || aligned16(d2p)) && (xc.peer_out == nullptr || aligned16(xc.peer_out)),
+              "rmsnorm: every row buffer must be 16-byte aligned");
+  const int blocks = blocks_for(rows, 3);
   auto stream = at::cuda::getCurrentCUDAStream();
   auto xp = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
   auto dp = add ? reinterpret_cast<const __nv_bfloat16*>(delta->data_ptr()) : nullptr;
@@ -296,7 +302,11 @@ at::Tensor rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tens
   TORCH_CHECK(xc.wait_flag == nullptr || status.has_value(), "rmsnorm_bwd: a wait needs a status word");
   int* st = status.has_value() ? status->data_ptr<int>() : nullptr;
   auto dy2p = dy2.has_value() ? reinterpret_cast<const __nv_bfloat16*>(dy2->data_ptr()) : nullptr;
-  const int blocks = blocks_for(rows);
+  TORCH_CHECK(aligned16(dy.data_ptr()) && aligned16(x.data_ptr()) && aligned16(w.data_ptr()) &&
+                  aligned16(dx.data_ptr()) && (!dres.has_value() || aligned16(dres->data_ptr())) &&
+                  (dy2p == nullptr || aligned16(dy2p)) && (xc.peer_out == nullptr || aligned16(xc.peer_out)),
+              "rmsnorm_bwd: every row buffer must be 16-byte aligned");
+  const int blocks = blocks_for(rows, 2);
   auto partial = at::empty({blocks, H}, x.options().dtype(at::kFloat));
   auto stream = at::cuda::getCurrentCUDAStream();
   const bool res = dres.has_value();
@@ -344,27 +354,58 @@ template <int D>
 __global__ void rope_kernel(__nv_bfloat16* __restrict__ qkv, const float* __restrict__ cos_t,
                             const float* __restrict__ sin_t, int T, int S, int n_rot_heads, int row_stride,
                             int pos0, float sign) {
+  // General form for any row stride / base offset: every access is a single
+  // element (2-byte bf16, 4-byte fp32), so no alignment beyond the element's
+  // own is assumed.  One thread rotates the pair (x1[i], x2[i]).
   constexpr int HALF = D / 2;
-  // one thread handles 2 element pairs (x1[i], x2[i]) for i in [2j, 2j+1]
   const long idx = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const long per_row = static_cast<long>(n_rot_heads) * (HALF / 2);
+  const long per_row = static_cast<long>(n_rot_heads) * HALF;
   if (idx >= per_row * T) return;
   const int t = static_cast<int>(idx / per_row);
   const int rem = static_cast<int>(idx % per_row);
-  const int head = rem / (HALF / 2);
-  const int i = (rem % (HALF / 2)) * 2;
+  const int head = rem / HALF;
+  const int i = rem % HALF;
   const int pos = pos0 + (t % S);
   __nv_bfloat16* base = qkv + static_cast<long>(t) * row_stride + head * D;
-  const float2 c = *reinterpret_cast<const float2*>(cos_t + static_cast<long>(pos) * HALF + i);
-  float2 s = *reinterpret_cast<const float2*>(sin_t + static_cast<long>(pos) * HALF + i);
-  s.x *= sign;
-  s.y *= sign;
-  const float2 a = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(base + i));
-  const float2 b = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(base + HALF + i));
-  const float2 oa = make_float2(a.x * c.x - b.x * s.x, a.y * c.y - b.y * s.y);
-  const float2 ob = make_float2(b.x * c.x + a.x * s.x, b.y * c.y + a.y * s.y);
-  *reinterpret_cast<__nv_bfloat162*>(base + i) = __floats2bfloat162_rn(oa.x, oa.y);
-  *reinterpret_cast<__nv_bfloat162*>(base + HALF + i) = __floats2bfloat162_rn(ob.x, ob.y);
+  const float c = cos_t[static_cast<long>(pos) * HALF + i];
+  const float s = sin_t[static_cast<long>(pos) * HALF + i] * sign;
+  const float a = __bfloat162float(base[i]);
+  const float b = __bfloat162float(base[HALF + i]);
+  base[i] = __float2bfloat16(a * c - b * s);
+  base[HALF + i] = __float2bfloat16(b * c + a * s);
+}
+
+// The same rotation with 16-byte accesses: thread (x, y) of a block rotates
+// eight pairs (x1[i..i+7], x2[i..i+7]) of one head in row blockIdx.x * R + y,
+// with x = head * (D / 16) + i / 8.  No division; the row pointer and stride
+// must be 16-byte aligned (checked by the launcher).
+template <int D>
+__global__ void __launch_bounds__(512)
+rope_vec_kernel(__nv_bfloat16* __restrict__ qkv, const float* __restrict__ cos_t, const float* __restrict__ sin_t,
+                int T, int S, int row_stride, int pos0, float sign) {
+  constexpr int HALF = D / 2;
+  const int t = blockIdx.x * blockDim.y + threadIdx.y;
+  if (t >= T) return;
+  const int head = threadIdx.x / (HALF / 8);
+  const int i = (threadIdx.x % (HALF / 8)) * 8;
+  const int pos = pos0 + (t % S);
+  __nv_bfloat16* base = qkv + static_cast<long>(t) * row_stride + head * D;
+  const float4* cp = reinterpret_cast<const float4*>(cos_t + static_cast<long>(pos) * HALF + i);
+  const float4* sp = reinterpret_cast<const float4*>(sin_t + static_cast<long>(pos) * HALF + i);
+  const float4 c0 = cp[0], c1 = cp[1], s0 = sp[0], s1 = sp[1];
+  const float c[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+  const float sn[8] = {s0.x * sign, s0.y * sign, s0.z * sign, s0.w * sign,
+                       s1.x * sign, s1.y * sign, s1.z * sign, s1.w * sign};
+  float a[8], b[8], oa[8], ob[8];
+  bf16x8_to_float(*reinterpret_cast<const bf16x8*>(base + i), a);
+  bf16x8_to_float(*reinterpret_cast<const bf16x8*>(base + HALF + i), b);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    oa[k] = a[k] * c[k] - b[k] * sn[k];
+    ob[k] = b[k] * c[k] + a[k] * sn[k];
+  }
+  *reinterpret_cast<bf16x8*>(base + i) = float_to_bf16x8(oa);
+  *reinterpret_cast<bf16x8*>(base + HALF + i) = float_to_bf16x8(ob);
 }
 
 void rope_(at::Tensor& qkv, const at::Tensor& cos_t, const at::Tensor& sin_t, int64_t S, int64_t n_rot_heads,
@@ -373,13 +414,31 @@ void rope_(at::Tensor& qkv, const at::Tensor& cos_t, const at::Tensor& sin_t, in
   TORCH_CHECK(head_dim == 64 || head_dim == 128, "rope: head_dim 64 or 128");
   const at::cuda::CUDAGuard guard(qkv.device());
   const int T = static_cast<int>(qkv.numel() / qkv.size(-1));
-  const int row_stride = static_cast<int>(qkv.size(-1));
-  const long work = static_cast<long>(T) * n_rot_heads * (head_dim / 4);
-  const int threads = 256;
-  const int blocks = static_cast<int>((work + threads - 1) / threads);
+  const int row_stride = static_cast<int>(qkv.dim() >= 2 ? qkv.stride(-2) : qkv.size(-1));
   auto stream = at::cuda::getCurrentCUDAStream();
   auto p = reinterpret_cast<__nv_bfloat16*>(qkv.data_ptr());
   const float sign = inverse ? -1.f : 1.f;
+  const int per_row = static_cast<int>(n_rot_heads * head_dim / 16);   // threads of one row
+  if (T == 0) return;
+  const bool aligned = reinterpret_cast<uintptr_t>(p) % 16 == 0 && row_stride % 8 == 0 &&
+                       reinterpret_cast<uintptr_t>(cos_t.data_ptr()) % 16 == 0 &&
+                       reinterpret_cast<uintptr_t>(sin_t.data_ptr()) % 16 == 0;
+  if (aligned && per_row <= 512) {
+    const int R = std::max(1, 256 / per_row);                           // rows per block
+    const dim3 block(per_row, R);
+    const int blocks = (T + R - 1) / R;
+    if (head_dim == 64)
+      rope_vec_kernel<64><<<blocks, block, 0, stream>>>(p, cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), T,
+                                                        (int)S, row_stride, (int)pos0, sign);
+    else
+      rope_vec_kernel<128><<<blocks, block, 0, stream>>>(p, cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), T,
+                                                         (int)S, row_stride, (int)pos0, sign);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
+  }
+  const long work = static_cast<long>(T) * n_rot_heads * (head_dim / 2);
+  const int threads = 256;
+  const int blocks = static_cast<int>((work + threads - 1) / threads);
   if (head_dim == 64)
     rope_kernel<64><<<blocks, threads, 0, stream>>>(p, cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), T, (int)S,
                                                     (int)n_rot_heads, row_stride, (int)pos0, sign);

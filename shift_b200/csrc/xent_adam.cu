@@ -121,6 +121,7 @@ at::Tensor xent_fwd_bwd(at::Tensor& logits, const at::Tensor& labels, double sca
   const int V = static_cast<int>(logits.size(-1));
   const long rows = logits.numel() / V;
   TORCH_CHECK(V % 8 == 0, "xent: V % 8");
+  TORCH_CHECK(aligned16(logits.data_ptr()), "xent: logits must be 16-byte aligned");
   auto loss = at::empty({rows}, logits.options().dtype(at::kFloat));
   const int vecs = V / 8;
   auto stream = at::cuda::getCurrentCUDAStream();

@@ -183,6 +183,13 @@ def run_mem(iters, T=16384, H=1024):
     nbytes = T * 32768 * 2 * 2
     rows.append({"case": "xent fwd+bwd", "ms": round(t, 4), "gbs": round(nbytes / t / 1e6, 1),
                  "frac_of_peak": round(nbytes / t / 1e6 / pk["hbm_gbs"], 3)})
+    from .reference import rope_tables
+    cos, sin = rope_tables(2048, 64, 1e6, "cuda")
+    qkv = bf(T, 24 * 64)
+    t = timeit(lambda: Fn.rope_(qkv, cos, sin, 2048, 20, 64), iters)
+    nbytes = T * 20 * 64 * 2 * 2
+    rows.append({"case": f"rope {T}x20 heads d64", "ms": round(t, 4), "gbs": round(nbytes / t / 1e6, 1),
+                 "frac_of_peak": round(nbytes / t / 1e6 / pk["hbm_gbs"], 3)})
     return rows
 
 

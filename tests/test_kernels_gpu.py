@@ -148,11 +148,13 @@ def test_rmsnorm_fwd_bwd(H, res):
     assert torch.equal(dx, dx2) and torch.equal(dw, dw2)
 
 
-def test_rope_roundtrip_and_reference():
+@pytest.mark.parametrize("B,S,Hq,Hkv,D,pad", [(2, 128, 4, 2, 64, 0), (3, 101, 16, 4, 64, 0), (2, 64, 8, 2, 128, 0),
+                                              (2, 128, 4, 2, 64, 1)])
+def test_rope_roundtrip_and_reference(B, S, Hq, Hkv, D, pad):
+    """pad = 1: rows of an odd stride (a column view), the unvectorised path."""
     torch.manual_seed(6)
-    B, S, Hq, Hkv, D = 2, 128, 4, 2, 64
     cos, sin = ref.rope_tables(512, D, 1e6, DEV)
-    qkv = _bf(B * S, (Hq + 2 * Hkv) * D)
+    qkv = _bf(B * S, (Hq + 2 * Hkv) * D + pad)[:, pad:]
     orig = qkv.clone()
     Fn.rope_(qkv, cos, sin, S, Hq + Hkv, D)
     rot = ref.rope(orig[:, : (Hq + Hkv) * D].view(B * S, Hq + Hkv, D).float(), cos, sin, S)
@@ -221,6 +223,56 @@ def test_router_sort_gather_combine():
     for j in range(k):
         expect += w[:, j:j + 1] * y[pos.view(T, k)[:, j].long()].float()
     _close(out, expect)
+
+
+def test_router_backward_matches_cpu():
+    """dx += d(router)/dx and dWr (sorted top-k weights + auxiliary term) against
+    the autograd restatement; T large enough for several token chunks and a
+    partial eight-token group in the weight-gradient kernel."""
+    torch.manual_seed(12)
+    T, H, E, k = 5003, 1024, 16, 4
+    x = _bf(T, H)
+    wr = _bf(E, H, std=0.05)
+    probs, idx, w = Fn.router_fwd(x, wr, k, True)
+    dw_topk = torch.randn(T, k, device=DEV)
+    aux = torch.randn(E, device=DEV) * 1e-3
+    dx = _bf(T, H)
+    dx_cpu = dx.cpu().clone()
+    dwr = torch.zeros(E, H, device=DEV)
+    Fn.router_bwd(x, wr, probs, idx, w, dw_topk, aux, True, dx, dwr)
+    dwr_cpu = torch.zeros(E, H)
+    Fn.router_bwd(x.cpu(), wr.cpu(), probs.cpu(), idx.cpu(), w.cpu(), dw_topk.cpu(), aux.cpu(), True, dx_cpu,
+                  dwr_cpu)
+    _close(dx, dx_cpu)
+    _close(dwr, dwr_cpu, tol=1e-2)
+
+
+def test_bucket_sort_many_chunks_stable():
+    """80,000 keys: the per-bin chunk scan runs over several 256-chunk tiles."""
+    torch.manual_seed(13)
+    n, E, pad = 80_000, 16, 128
+    keys = torch.randint(0, E, (n,), device=DEV, dtype=torch.int32)
+    keys[::97] = E + 3            # outside [0, E): ignored
+    pos, offs, counts, row_src = Fn.bucket_sort(keys, 0, E, pad, 4)
+    kc = keys.long().cpu()
+    valid = kc < E
+    cnt = torch.bincount(kc[valid], minlength=E)
+    assert torch.equal(counts.cpu().long(), cnt)
+    padded = (cnt + pad - 1) // pad * pad
+    o = torch.zeros(E + 1, dtype=torch.long)
+    o[1:] = torch.cumsum(padded, 0)
+    assert torch.equal(offs.cpu().long(), o)
+    # expected slot: bin offset + number of earlier keys of the same bin
+    order = torch.argsort(kc.masked_fill(~valid, E), stable=True)
+    sk = kc.masked_fill(~valid, E)[order]
+    first = torch.searchsorted(sk, torch.arange(E + 1))
+    rank_sorted = torch.arange(n) - first[sk]
+    expect = torch.full((n,), -1, dtype=torch.long)
+    vs = sk < E
+    expect[order[vs]] = o[sk[vs]] + rank_sorted[vs]
+    assert torch.equal(pos.cpu().long(), expect)
+    rs = row_src.cpu().long()
+    assert torch.equal(rs[expect[valid]], torch.arange(n)[valid] // 4)
 
 
 @pytest.mark.parametrize("T,V", [(64, 32768), (700, 32768), (300, 1000), (129, 12288)])

@@ -243,8 +243,8 @@ def test_router_backward_matches_cpu():
     dwr_cpu = torch.zeros(E, H)
     Fn.router_bwd(x.cpu(), wr.cpu(), probs.cpu(), idx.cpu(), w.cpu(), dw_topk.cpu(), aux.cpu(), True, dx_cpu,
                   dwr_cpu)
-    _close(dx, dx_cpu)
-    _close(dwr, dwr_cpu, tol=1e-2)
+    _close(dx.cpu(), dx_cpu)
+    _close(dwr.cpu(), dwr_cpu, tol=1e-2)
 
 
 def test_bucket_sort_many_chunks_stable():

@@ -83,6 +83,9 @@ def parse_args(argv=None):
     p.add_argument("--reference-dump", default="",
                    help="comma-separated committed steps after which the averaged gradient, model, optimizer and "
                         "scheduler are saved to reference_step<k>_r<rank>.pt (group reduction or flat mode)")
+    p.add_argument("--trace-routing", action="store_true",
+                   help="also log a 'routing' event per step, sample and MoE layer with the digest of the router's "
+                        "top-k expert indices (read by shift_b200.analysis.trajectory)")
     p.add_argument("--seed", type=int, default=2026)
     return p.parse_args(argv)
 
@@ -208,6 +211,28 @@ class Worker:
                 out.append((data[:, :-1].contiguous(), data[:, 1:].contiguous()))
         return out, ids
 
+    def forward_backward(self, batches, ids, step):
+        """One step's forward/backward over its microbatches, with the
+        evidence the trajectory summary compares across runs: a 'batch_plan'
+        event (the sample ids of the step, before the update) and, with
+        --trace-routing, one 'routing' event per sample and MoE layer holding
+        the digest of the router's top-k expert indices."""
+        a, eng = self.args, self.engine
+        self.event("batch_plan", step=step, sample_ids=ids)
+        if not a.trace_routing:
+            return eng.forward_backward(batches, a.batch, a.seq_len)
+        seen = []
+        eng.model.routing_hook = lambda layer, idx: seen.append((layer, digest(idx)))
+        try:
+            loss = eng.forward_backward(batches, a.batch, a.seq_len)
+        finally:
+            eng.model.routing_hook = None
+        per = len(seen) // max(1, len(ids))      # microbatch m runs sample ids[m] through every layer
+        for m, sample in enumerate(ids):
+            for layer, h in seen[m * per:(m + 1) * per]:
+                self.event("routing", step=step, sample=sample, layer=layer, topk_hash=h)
+        return loss
+
     def reference_dump(self, grad):
         """Per-step numerical reference (shift_full/train.py:584-587 semantics):
         the averaged gradient and the committed state after the step."""
@@ -224,12 +249,13 @@ class Worker:
         """The flat baseline: no quorum, no Manager; one replica trains every
         data rank's microbatches (the same global batch as the shift run)."""
         a = self.args
-        self.event("ready", model=a.model, mode="flat", params=self.engine.store.numel)
+        self.event("ready", model=a.model, mode="flat", params=self.engine.store.numel,
+                   hashes=self.current_hashes() if a.audit_state else {})
         eng = self.engine
         while self.progress["updates"] < a.steps and not self.requested_stop():
             it0 = time.monotonic()
             batches, ids = self.batches(self.progress["updates"])
-            loss = eng.forward_backward(batches, a.batch, a.seq_len)
+            loss = self.forward_backward(batches, ids, self.progress["updates"])
             g = eng.store.grad
             eng.optimizer_step([g], 1.0)
             grad_copy = g.detach().clone() if a.reference_dump else None
@@ -347,7 +373,7 @@ class Worker:
             if self.reducer is not None:
                 eng.nonfinite.zero_()
                 self.reducer.fused.begin_step(step)
-            loss = eng.forward_backward(batches, a.batch, a.seq_len)
+            loss = self.forward_backward(batches, sample_ids, step)
             if inject_kind == "slow":
                 time.sleep(float(inject_arg) / 1000.0)
             if inject_kind == "nonfinite" and step == int(inject_arg):

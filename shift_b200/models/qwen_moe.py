@@ -139,6 +139,7 @@ class QwenMoE:
         self.dt = store.compute_dtype
         self._saved: list = []
         self.layer_done_hook = None   # callable(layer_index) after its grads are written
+        self.routing_hook = None      # callable(layer_prefix, topk_idx) after each router forward
 
     @property
     def layers(self):
@@ -304,6 +305,8 @@ class QwenMoE:
     def _moe_fwd(self, p, x, T, combine_out=None, split=(), xchg=()):
         cfg, st = self.cfg, self.store
         probs, idx, w = Fn.router_fwd(x, st.w(p + "mlp.router"), cfg.top_k, cfg.norm_topk)
+        if self.routing_hook is not None:
+            self.routing_hook(p, idx)
         e_n = self.e_hi - self.e_lo
         pos, offs, counts, row_src = Fn.bucket_sort(idx, self.e_lo, self.e_hi, 128 if x.is_cuda else 1, cfg.top_k)
         cap = row_src.shape[0]

@@ -1,7 +1,8 @@
 """Numerical oracle on CPU: the flat baseline (one process, whole global
 batch, no Manager) and the fault-tolerant run (2 replicas, quorum, group
 average) agree per step within the reference's tolerances; a perturbed run
-does not."""
+does not.  The trajectory summary of the same two runs finds the same initial
+state, batch plans and per-layer routing; a tampered routing row fails it."""
 import json
 import socket
 import subprocess as sp
@@ -11,6 +12,7 @@ from pathlib import Path
 import torch
 
 from shift_b200.analysis.compare_reference import compare_runs
+from shift_b200.analysis.trajectory import summarize
 from shift_b200.control.session import Session
 
 ROOT = Path(__file__).resolve().parents[1]
@@ -30,7 +32,7 @@ def _ports(n):
 
 def test_flat_vs_shift_reference_dumps(tmp_path):
     common = ["--model", "tiny", "--device", "cpu", "--seq-len", "64", "--batch", "2", "--data", "random",
-              "--reference-dump", "1,2,3", "--communication-timeout", "20"]
+              "--reference-dump", "1,2,3", "--communication-timeout", "20", "--audit-state", "--trace-routing"]
     flat_dir = tmp_path / "flat"
     sp.run([sys.executable, "-m", "shift_b200.ft.train", "--session", "flat", "--replica", "0", "--root",
             str(tmp_path), "--lighthouse", "127.0.0.1:1", "--mode", "flat", "--steps", "3", *common],
@@ -49,6 +51,20 @@ def test_flat_vs_shift_reference_dumps(tmp_path):
         s.finish()
     res = compare_runs(flat_dir, tmp_path / "shift", steps=[1, 2, 3])
     assert res["pass"], json.dumps(res, default=str)[:2000]
+    traj = summarize(flat_dir, tmp_path / "shift", comparison=res)
+    assert traj["pass"], json.dumps(traj, default=str)[:3000]
+    assert traj["checks"]["same_routing"]["keys"] == 3 * 2 * 2     # steps x samples x MoE layers
+    # a routing digest that differs is caught
+    ev = sorted(flat_dir.glob("events_g0_r*.jsonl"))[0]
+    rows = [json.loads(x) for x in ev.read_text().splitlines() if x.strip()]
+    for r in rows:
+        if r.get("kind") == "routing":
+            r["topk_hash"] = "0" * 64
+            break
+    ev.write_text("".join(json.dumps(r, sort_keys=True) + "\n" for r in rows))
+    bad = summarize(flat_dir, tmp_path / "shift", comparison=res)
+    assert not bad["pass"] and not bad["checks"]["same_routing"]["pass"]
+    assert bad["checks"]["same_batch_plans"]["pass"]
     # the oracle is sensitive: a perturbed model fails it
     p = torch.load(flat_dir / "reference_step3_r0.pt", weights_only=False)
     name = next(iter(p["model"]))

@@ -13,10 +13,27 @@ manager.allreduce, Adam).  Events: ready (state bytes), commit (quorum /
 reduce / optimizer seconds), stopped.  Runs under the same supervisors and
 markers as the trainer, so a kill / heal of the probe exercises the same
 recovery path with a 1-parameter state.
+
+It also probes two building blocks of the planned handoff in isolation (the
+reference's linear-layer probes sf/planned_probe.py and sf/planned_overlap.py):
+
+* ``--world-size-mode fixed_with_spares --min-replicas K``: replicas beyond
+  the first K at the quorum's step are spares -- they take part in every
+  reduction with a zero contribution and apply the average, so a spare's
+  state follows the participants' bit for bit without changing the result
+  (the shadow a planned spare keeps before it takes over);
+* ``--snapshot-overlap``: every step copies the committed generation of the
+  state (parameters, fp32 master, both moments) into a snapshot buffer
+  while the step's gradient, reduction and AdamW run -- on a side CUDA stream,
+  or a host thread on CPU.  The flat ping-pong buffers make that generation
+  read-only during the step (AdamW writes the other one); the probe checks it
+  (tensor version counters) and that the snapshot equals the state it copied
+  (the pre-copy window of the P2 handoff).
 """
 from __future__ import annotations
 
 import os
+import threading
 import time
 from datetime import timedelta
 
@@ -35,10 +52,62 @@ def parse_args(argv=None):
     import argparse
     extra = argparse.ArgumentParser(add_help=False, allow_abbrev=False)
     extra.add_argument("--numel", type=int, default=125_000_000)
+    extra.add_argument("--snapshot-overlap", action="store_true")
     known, rest = extra.parse_known_args(argv)
     args = base_parse(rest)
     args.numel = known.numel
+    args.snapshot_overlap = known.snapshot_overlap
     return args
+
+
+class _Snapshot:
+    """Copy of one generation of the flat state, taken concurrently with a step."""
+
+    def __init__(self, store, device):
+        self.store, self.device = store, device
+        self.bufs = None
+        self.stream = torch.cuda.Stream(device) if device.type == "cuda" else None
+
+    def _sources(self):
+        st, c = self.store, self.store.cur
+        return [st.param[c], st.master[c], st.exp_avg[c], st.exp_avg_sq[c]]
+
+    def begin(self):
+        src = self._sources()
+        if self.bufs is None:
+            self.bufs = [torch.empty_like(t) for t in src]
+        self.versions = [t._version for t in src]
+        self.t0 = time.monotonic()
+        if self.stream is not None:
+            self.stream.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(self.stream):
+                for b, t in zip(self.bufs, src):
+                    b.copy_(t, non_blocking=True)
+                self.done = torch.cuda.Event()
+                self.done.record(self.stream)
+            self.thread = None
+        else:
+            def work():
+                for b, t in zip(self.bufs, src):
+                    b.copy_(t)
+                self.copy_end = time.monotonic()
+            self.thread = threading.Thread(target=work, daemon=True)
+            self.thread.start()
+        return src
+
+    def finish(self, src) -> dict:
+        """After the step (before commit flips the generation)."""
+        if self.thread is not None:
+            self.thread.join()
+            copy_s = self.copy_end - self.t0
+        else:
+            self.done.synchronize()
+            copy_s = time.monotonic() - self.t0
+        unchanged = [t._version for t in src] == self.versions
+        equal = all(torch.equal(b, t) for b, t in zip(self.bufs, src))
+        return {"copy_seconds": copy_s, "window_seconds": time.monotonic() - self.t0,
+                "source_unchanged": unchanged, "snapshot_equal": equal,
+                "bytes": sum(t.numel() * t.element_size() for t in src)}
 
 
 class ProbeWorker(Worker):
@@ -66,7 +135,10 @@ class ProbeWorker(Worker):
                                a.lighthouse, rank=self.rank, world_size=self.local_world,
                                store_addr=f"{a.host_ip}:{store_port}", hostname=a.host_ip,
                                checkpoint_transport=transport, timeout=timedelta(seconds=a.communication_timeout),
-                               world_size_mode=WorldSizeMode.DYNAMIC, event=self.event)
+                               world_size_mode=(WorldSizeMode.FIXED_WITH_SPARES
+                                                if a.world_size_mode == "fixed_with_spares"
+                                                else WorldSizeMode.DYNAMIC), event=self.event)
+        snap = _Snapshot(st, self.device) if a.snapshot_overlap else None
         state_bytes = st.numel * (st.param[0].element_size() + 3 * 4)
         self.event("ready", probe=True, numel=st.numel, state_bytes=state_bytes, device=str(self.device),
                    hashes=self.current_hashes() if a.audit_state else {})
@@ -82,6 +154,7 @@ class ProbeWorker(Worker):
             mgr.start_quorum()
             step = self.progress["updates"]
             t1 = time.monotonic()
+            src = snap.begin() if snap is not None else None
             st.grad.copy_(self.gradient(step))
             mgr.allreduce(st.grad).wait()
             if self.device.type == "cuda":
@@ -91,10 +164,13 @@ class ProbeWorker(Worker):
             if self.device.type == "cuda":
                 torch.cuda.current_stream().synchronize()
             t3 = time.monotonic()
+            if snap is not None:
+                self.event("snapshot_overlap", step=step, **snap.finish(src))
             if mgr.should_commit():
                 self.engine.commit()
                 self.progress["updates"] += 1
                 self.event("commit", step=self.progress["updates"], participants=mgr.num_participants(),
+                           contributed=mgr.is_participating(),
                            quorum_seconds=t1 - t0, reduce_seconds=t2 - t1, optimizer_seconds=t3 - t2,
                            seconds=time.monotonic() - t0,
                            hashes=self.current_hashes() if (a.hash_every and a.audit_state) else {})

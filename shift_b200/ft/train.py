@@ -83,6 +83,9 @@ def parse_args(argv=None):
     p.add_argument("--reference-dump", default="",
                    help="comma-separated committed steps after which the averaged gradient, model, optimizer and "
                         "scheduler are saved to reference_step<k>_r<rank>.pt (group reduction or flat mode)")
+    p.add_argument("--profile-timings", action="store_true",
+                   help="split the cross-replica phase of each step: device time between CUDA events around it "
+                        "(cross_gpu_seconds) and host time to copy, dispatch and wait")
     p.add_argument("--trace-routing", action="store_true",
                    help="also log a 'routing' event per step, sample and MoE layer with the digest of the router's "
                         "top-k expert indices (read by shift_b200.analysis.trajectory)")
@@ -370,6 +373,7 @@ class Worker:
                 os._exit(17)
             batches, sample_ids = self.batches(step)
             t_compute = time.monotonic()
+            schedule_s = t_compute - it0
             if self.reducer is not None:
                 eng.nonfinite.zero_()
                 self.reducer.fused.begin_step(step)
@@ -379,19 +383,42 @@ class Worker:
             if inject_kind == "nonfinite" and step == int(inject_arg):
                 eng.store.grad.view(-1)[0] = float("nan")
             # cross-replica average (participants only)
+            prof = {}
+            cuda_prof = a.profile_timings and self.device.type == "cuda"
+            if cuda_prof:
+                ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                ev0.record()
+            t_cross = time.monotonic()
             if a.reduce == "group":
                 g = eng.store.grad
                 if self.transport_on_cpu:
                     gc = g.float().cpu()
-                    mgr.allreduce(gc).wait()
+                    t_copied = time.monotonic()
+                    work = mgr.allreduce(gc)
+                    t_issued = time.monotonic()
+                    work.wait()
                     g.copy_(gc)
                 else:
-                    mgr.allreduce(g).wait()
+                    t_copied = time.monotonic()
+                    work = mgr.allreduce(g)
+                    t_issued = time.monotonic()
+                    work.wait()
+                t_waited = time.monotonic()
+                prof = dict(d2h_seconds=t_copied - t_cross, dispatch_seconds=t_issued - t_copied,
+                            wait_seconds=t_waited - t_issued)
                 nonfinite = eng.optimizer_step([g], 1.0)
             else:
                 # reduction + AdamW already ran per bucket inside the fused kernel
                 nonfinite = self.reducer.fused.finish_step()
+            if cuda_prof:
+                ev1.record()
+            t_check = time.monotonic()
             finite = int(nonfinite.item()) == 0
+            gradient_check_s = time.monotonic() - t_check
+            if cuda_prof:
+                prof["cross_gpu_seconds"] = ev0.elapsed_time(ev1) / 1000.0
+            if a.profile_timings:
+                prof["cross_host_seconds"] = t_check - t_cross
             if not finite:
                 mgr.report_error(RuntimeError("nonfinite gradients"))
             if self.reducer is not None:
@@ -413,7 +440,8 @@ class Worker:
                            model_hash=hashes.get("model"), optimizer_hash=hashes.get("optimizer"),
                            scheduler_hash=hashes.get("scheduler"), sample_ids=sample_ids, finite_gradients=finite,
                            loss=float(loss), seconds=time.monotonic() - it0, compute_seconds=t_decide - t_compute,
-                           decision_seconds=time.monotonic() - t_decide,
+                           decision_seconds=time.monotonic() - t_decide, schedule_seconds=schedule_s,
+                           gradient_check_seconds=gradient_check_s, **prof,
                            global_batch=a.batch * a.microbatches * mgr.num_participants())
             else:
                 self.event("skipped", step=step, error=str(mgr.errored()), finite_gradients=finite)

@@ -32,7 +32,7 @@ def _ports(n):
 
 def test_flat_vs_shift_reference_dumps(tmp_path):
     common = ["--model", "tiny", "--device", "cpu", "--seq-len", "64", "--batch", "2", "--data", "random",
-              "--reference-dump", "1,2,3", "--communication-timeout", "20", "--audit-state", "--trace-routing"]
+              "--reference-dump", "1,2,3", "--communication-timeout", "20", "--audit-state", "--trace-routing", "--profile-timings"]
     flat_dir = tmp_path / "flat"
     sp.run([sys.executable, "-m", "shift_b200.ft.train", "--session", "flat", "--replica", "0", "--root",
             str(tmp_path), "--lighthouse", "127.0.0.1:1", "--mode", "flat", "--steps", "3", *common],
@@ -51,6 +51,12 @@ def test_flat_vs_shift_reference_dumps(tmp_path):
         s.finish()
     res = compare_runs(flat_dir, tmp_path / "shift", steps=[1, 2, 3])
     assert res["pass"], json.dumps(res, default=str)[:2000]
+    commits = [json.loads(x) for f in sorted((tmp_path / "shift").glob("events_g0_r*.jsonl"))
+               for x in f.read_text().splitlines() if '"commit"' in x]
+    commits = [c for c in commits if c.get("kind") == "commit"]
+    assert commits and all(c["schedule_seconds"] >= 0 and c["gradient_check_seconds"] >= 0 and
+                           {"d2h_seconds", "dispatch_seconds", "wait_seconds", "cross_host_seconds"} <= c.keys()
+                           for c in commits)
     traj = summarize(flat_dir, tmp_path / "shift", comparison=res)
     assert traj["pass"], json.dumps(traj, default=str)[:3000]
     assert traj["checks"]["same_routing"]["keys"] == 3 * 2 * 2     # steps x samples x MoE layers

@@ -32,6 +32,24 @@ enum Status : int {
 // must be 16-byte aligned, or the vector accesses would fault.
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Debug builds (SHIFT_DEBUG_BOUNDS=1 in the environment of `setup.py build_ext`
+// adds -DSHIFT_DEBUG_BOUNDS=1) check the row indices that kernels read from
+// data -- routing slots, token ids -- before using them as addresses.  A bad
+// index is printed with the source line and the access is skipped (the row
+// reads as zeros / is not written); nothing traps, so the context survives and
+// the run can be inspected.  Release builds compile the check away.
+#if defined(SHIFT_DEBUG_BOUNDS) && SHIFT_DEBUG_BOUNDS
+#include <cstdio>
+#define SB_IN_RANGE(i, n) ::sb::debug_in_range(static_cast<long long>(i), static_cast<long long>(n), __LINE__)
+__device__ __noinline__ inline bool debug_in_range(long long i, long long n, int line) {
+  if (i >= 0 && i < n) return true;
+  printf("shift_b200 bounds check: line %d: index %lld not in [0, %lld)\n", line, i, n);
+  return false;
+}
+#else
+#define SB_IN_RANGE(i, n) true
+#endif
+
 SB_DEVICE uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));

@@ -509,13 +509,15 @@ std::vector<at::Tensor> bucket_sort(const at::Tensor& keys, int64_t lo, int64_t 
 // ---------------------------------------------------------------------------
 // out[r] = src[row_src[r]] (row_src < 0 or r >= *total -> zeros)
 __global__ void gather_rows_kernel(const bf16x8* __restrict__ src, const int* __restrict__ row_src,
-                                   const int* __restrict__ total, int cap, int vecs, bf16x8* __restrict__ out) {
+                                   const int* __restrict__ total, int cap, int vecs, bf16x8* __restrict__ out,
+                                   int src_rows) {
   const int lane = threadIdx.x % 32;
   const int warp = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int nwarps = gridDim.x * (blockDim.x / 32);
   const int lim = total ? min(cap, *total) : cap;
   for (int r = warp; r < lim; r += nwarps) {
-    const int s = row_src[r];
+    int s = row_src[r];
+    if (s >= 0 && !SB_IN_RANGE(s, src_rows)) s = -1;
     for (int v = lane; v < vecs; v += 32) {
       bf16x8 val;
       if (s >= 0) val = src[static_cast<long>(s) * vecs + v];
@@ -534,7 +536,8 @@ void gather_rows(const at::Tensor& src, const at::Tensor& row_src, const c10::op
   const int blocks = std::max(1, std::min((cap + 7) / 8, 148 * 8));
   gather_rows_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const bf16x8*>(src.data_ptr()), row_src.data_ptr<int>(),
-      total.has_value() ? total->data_ptr<int>() : nullptr, cap, H / 8, reinterpret_cast<bf16x8*>(out.data_ptr()));
+      total.has_value() ? total->data_ptr<int>() : nullptr, cap, H / 8, reinterpret_cast<bf16x8*>(out.data_ptr()),
+      static_cast<int>(src.size(0)));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -542,7 +545,7 @@ void gather_rows(const at::Tensor& src, const at::Tensor& row_src, const c10::op
 template <int NV>
 __global__ void combine_kernel(const __nv_bfloat16* __restrict__ y, const int* __restrict__ pos,
                                const float* __restrict__ w, int T, int k, __nv_bfloat16* __restrict__ out,
-                               int peer_lo, int peer_hi, int own_off, Xchg xc) {
+                               int peer_lo, int peer_hi, int own_off, Xchg xc, int y_rows) {
   // Tensor-parallel form: token rows in [peer_lo, peer_hi) go to the peer's
   // receive buffer (xc.peer_out, row t - peer_lo) over NVLink, the others to
   // out at row t - own_off; then the kernel signals.  The expert combine's
@@ -560,7 +563,7 @@ __global__ void combine_kernel(const __nv_bfloat16* __restrict__ y, const int* _
       for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
     for (int j = 0; j < k; ++j) {
       const int p = pos[static_cast<long>(t) * k + j];
-      if (p < 0) continue;
+      if (p < 0 || !SB_IN_RANGE(p, y_rows)) continue;
       const float wj = w[static_cast<long>(t) * k + j];
 #pragma unroll
       for (int i = 0; i < NV; ++i) {
@@ -585,14 +588,16 @@ __global__ void combine_kernel(const __nv_bfloat16* __restrict__ y, const int* _
 template <int NV>
 __global__ void combine_bwd_rows_kernel(const __nv_bfloat16* __restrict__ dout, const int* __restrict__ row_src,
                                         const int* __restrict__ slot_of_row, const float* __restrict__ w,
-                                        const int* __restrict__ total, int cap, __nv_bfloat16* __restrict__ dy) {
+                                        const int* __restrict__ total, int cap, __nv_bfloat16* __restrict__ dy,
+                                        int dout_rows, int n_slots) {
   constexpr int H = NV * 256;
   const int lane = threadIdx.x % 32;
   const int warp = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int nwarps = gridDim.x * (blockDim.x / 32);
   const int lim = min(cap, *total);
   for (int r = warp; r < lim; r += nwarps) {
-    const int t = row_src[r];
+    int t = row_src[r];
+    if (t >= 0 && !(SB_IN_RANGE(t, dout_rows) && SB_IN_RANGE(slot_of_row[r], n_slots))) t = -1;
     const float wr = t >= 0 ? w[slot_of_row[r]] : 0.f;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
@@ -612,7 +617,8 @@ __global__ void combine_bwd_rows_kernel(const __nv_bfloat16* __restrict__ dout, 
 
 template <int NV>
 __global__ void combine_bwd_weights_kernel(const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* __restrict__ y,
-                                           const int* __restrict__ pos, int T, int k, float* __restrict__ dw) {
+                                           const int* __restrict__ pos, int T, int k, float* __restrict__ dw,
+                                           int y_rows) {
   constexpr int H = NV * 256;
   const int lane = threadIdx.x % 32;
   const int warp = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
@@ -625,7 +631,7 @@ __global__ void combine_bwd_weights_kernel(const __nv_bfloat16* __restrict__ dou
     for (int j = 0; j < k; ++j) {
       const int p = pos[static_cast<long>(t) * k + j];
       float s = 0.f;
-      if (p >= 0) {
+      if (p >= 0 && SB_IN_RANGE(p, y_rows)) {
 #pragma unroll
         for (int i = 0; i < NV; ++i) {
           float v[8];
@@ -643,7 +649,7 @@ __global__ void combine_bwd_weights_kernel(const __nv_bfloat16* __restrict__ dou
 // dx[t] (+)= sum_j dperm[pos[t,j]]
 template <int NV>
 __global__ void scatter_back_kernel(const __nv_bfloat16* __restrict__ dperm, const int* __restrict__ pos, int T,
-                                    int k, __nv_bfloat16* __restrict__ dx, int accumulate) {
+                                    int k, __nv_bfloat16* __restrict__ dx, int accumulate, int perm_rows) {
   constexpr int H = NV * 256;
   const int lane = threadIdx.x % 32;
   const int warp = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
@@ -660,7 +666,7 @@ __global__ void scatter_back_kernel(const __nv_bfloat16* __restrict__ dperm, con
     }
     for (int j = 0; j < k; ++j) {
       const int p = pos[static_cast<long>(t) * k + j];
-      if (p < 0) continue;
+      if (p < 0 || !SB_IN_RANGE(p, perm_rows)) continue;
 #pragma unroll
       for (int i = 0; i < NV; ++i) {
         float v[8];
@@ -705,7 +711,7 @@ at::Tensor combine(const at::Tensor& y, const at::Tensor& pos, const at::Tensor&
   auto stream = at::cuda::getCurrentCUDAStream();
   auto yp = reinterpret_cast<const __nv_bfloat16*>(y.data_ptr());
   auto op = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
-#define SB_L(NV) combine_kernel<NV><<<warp_blocks((int)T), 256, 0, stream>>>(yp, pos.data_ptr<int>(), w.data_ptr<float>(), (int)T, k, op, peer_lo, peer_hi, own_off, xc)
+#define SB_L(NV) combine_kernel<NV><<<warp_blocks((int)T), 256, 0, stream>>>(yp, pos.data_ptr<int>(), w.data_ptr<float>(), (int)T, k, op, peer_lo, peer_hi, own_off, xc, static_cast<int>(y.size(0)))
   SB_H_DISPATCH(H, SB_L)
 #undef SB_L
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -728,8 +734,9 @@ std::vector<at::Tensor> combine_bwd(const at::Tensor& dout, const at::Tensor& y,
   auto dyp = reinterpret_cast<__nv_bfloat16*>(dy.data_ptr());
 #define SB_L(NV)                                                                                                   \
   combine_bwd_rows_kernel<NV><<<warp_blocks(cap), 256, 0, stream>>>(dp, row_src.data_ptr<int>(),                  \
-      slot_of_row.data_ptr<int>(), w.data_ptr<float>(), total.data_ptr<int>(), cap, dyp);                          \
-  combine_bwd_weights_kernel<NV><<<warp_blocks(T), 256, 0, stream>>>(dp, yp, pos.data_ptr<int>(), T, k, dw.data_ptr<float>())
+      slot_of_row.data_ptr<int>(), w.data_ptr<float>(), total.data_ptr<int>(), cap, dyp,                       \
+      static_cast<int>(dout.size(0)), static_cast<int>(w.numel()));                          \
+  combine_bwd_weights_kernel<NV><<<warp_blocks(T), 256, 0, stream>>>(dp, yp, pos.data_ptr<int>(), T, k, dw.data_ptr<float>(), cap)
   SB_H_DISPATCH(H, SB_L)
 #undef SB_L
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -743,7 +750,7 @@ void scatter_back(const at::Tensor& dperm, const at::Tensor& pos, at::Tensor& dx
   auto stream = at::cuda::getCurrentCUDAStream();
   auto pp = reinterpret_cast<const __nv_bfloat16*>(dperm.data_ptr());
   auto xp = reinterpret_cast<__nv_bfloat16*>(dx.data_ptr());
-#define SB_L(NV) scatter_back_kernel<NV><<<warp_blocks(T), 256, 0, stream>>>(pp, pos.data_ptr<int>(), T, k, xp, accumulate ? 1 : 0)
+#define SB_L(NV) scatter_back_kernel<NV><<<warp_blocks(T), 256, 0, stream>>>(pp, pos.data_ptr<int>(), T, k, xp, accumulate ? 1 : 0, static_cast<int>(dperm.size(0)))
   SB_H_DISPATCH(H, SB_L)
 #undef SB_L
   C10_CUDA_KERNEL_LAUNCH_CHECK();

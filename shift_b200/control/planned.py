@@ -360,11 +360,20 @@ def main(argv=None):
     ap.add_argument("--nproc", type=int, default=1)
     ap.add_argument("--gpus", default="", help="A,B,C device lists, e.g. '0;1;2'")
     ap.add_argument("--train-args", default="", help="extra trainer flags, e.g. '--seq-len 2048 --batch 4'")
+    ap.add_argument("--no-preflight", action="store_true",
+                    help="skip the check that no other compute process holds the session's GPUs")
     a = ap.parse_args(argv)
     devices = {}
     if a.gpus:
         for role, lst in zip("ABC", a.gpus.split(";")):
             devices[role] = [int(x) for x in lst.split(",")]
+    if a.device == "cuda" and not a.no_preflight:
+        from .preflight import check_gpus_idle
+        wanted = sorted({g for lst in devices.values() for g in lst}) or None
+        pre = check_gpus_idle(wanted)
+        if not pre["pass"]:
+            print(json.dumps({"pass": False, "preflight": pre}, default=str))
+            return 2
     import shlex
     s = PlannedSession(a.root, a.name, a.variant, a.scenario, a.model, a.device, a.nproc, devices=devices,
                        train_args=shlex.split(a.train_args))

@@ -27,6 +27,13 @@ def test_epoch_gate_fence_rules():
         g.cancel()                         # cannot cancel after activation
 
 
+def test_protocol_negatives_probe():
+    from shift_b200.ft import protocol_probe
+    rep = protocol_probe.run()
+    assert rep["pass"] and rep["negatives"] == 9, rep
+    assert protocol_probe.main([]) == 0
+
+
 @pytest.mark.parametrize("variant", ["p1f", "p2"])
 def test_planned_handoff_healthy(tmp_path, variant):
     s = PlannedSession(tmp_path, variant, variant=variant)

@@ -26,6 +26,28 @@ from .event_reader import IncrementalReader
 from .supervisor import load_config
 
 
+def joint_boundary(commits, rid, gen, after_step, replicas, ranks):
+    """First joint commit of replica ``rid`` (generation ``gen``) past
+    ``after_step``: the smallest step at which EVERY rank of the replica
+    committed with all ``replicas`` participating and itself contributing
+    (a commit the replica made while healing, without contributing its
+    gradient, does not count).  Returns (step, latest commit time over the
+    ranks) or None.  The rule of the reference's rotation boundary
+    (sf/rotation.py; sf/test_rotation.py:9-43)."""
+    per_step: dict = {}
+    for c in commits:
+        if (c.get("kind", "commit") != "commit" or c.get("rid") != rid or c.get("generation", 0) != gen
+                or c.get("step", 0) <= after_step or c.get("participants") != replicas
+                or c.get("contributed") is False):
+            continue
+        per_step.setdefault(c["step"], {})[c.get("rank", 0)] = c.get("time")
+    for step in sorted(per_step):
+        got = per_step[step]
+        if all(r in got for r in range(ranks)):
+            return step, max(t for t in got.values() if t is not None)
+    return None
+
+
 class Session:
     def __init__(self, root, session: str, config_path, replicas: int = 2, host_ip: str = "127.0.0.1",
                  seconds: float = 900.0):
@@ -82,6 +104,10 @@ class Session:
             m["generation"] = gen
         return self.reader.rows("commit", **m)
 
+    def _joint(self, rid, gen, after_step):
+        rows = [c for r in range(self.ranks()) for c in self.commits(rid, gen, rank=r)]
+        return joint_boundary(rows, rid, gen, after_step, self.replicas, self.ranks())
+
     def last_step(self, rid, rank=0) -> int:
         c = self.commits(rid, rank=rank)
         return c[-1]["step"] if c else 0
@@ -126,10 +152,10 @@ class Session:
         restored = self.reader.rows("restored", rid=rid, generation=gen + 1)
         rstep = max(r["step"] for r in restored)
         t_restored = max(r["time"] for r in restored)
-        # first commit with all replicas participating past the restored step
-        self.await_(lambda: any(c["participants"] == self.replicas and c["step"] > rstep
-                                for c in self.commits(rid, gen + 1)), timeout, "joint commit")
-        joint = [c for c in self.commits(rid, gen + 1) if c["participants"] == self.replicas and c["step"] > rstep][0]
+        # first step every rank of the replica committed jointly past the restored step
+        self.await_(lambda: self._joint(rid, gen + 1, rstep) is not None, timeout, "joint commit")
+        jstep, jtime = self._joint(rid, gen + 1, rstep)
+        joint = {"step": jstep, "time": jtime}
         rec = dict(rid=rid, fault_kind=kind, generation=gen, fault_time=t_fault, solo_time=t_solo,
                    restored_time=t_restored, joint_time=joint["time"], restored_step=rstep, joint_step=joint["step"],
                    fault_to_joint=joint["time"] - t_fault, restored_hashes_match=all(r["hashes_match"] for r in restored))
@@ -159,9 +185,9 @@ class Session:
                     == self.ranks(), timeout, "restored ranks")
         restored = self.reader.rows("restored", rid=rid, generation=gen + 1)
         rstep = max(r["step"] for r in restored)
-        self.await_(lambda: any(c["participants"] == self.replicas and c["step"] > rstep
-                                for c in self.commits(rid, gen + 1)), timeout, "joint commit")
-        joint = [c for c in self.commits(rid, gen + 1) if c["participants"] == self.replicas and c["step"] > rstep][0]
+        self.await_(lambda: self._joint(rid, gen + 1, rstep) is not None, timeout, "joint commit")
+        jstep, jtime = self._joint(rid, gen + 1, rstep)
+        joint = {"step": jstep, "time": jtime}
         placement = {r["rank"]: r.get("placement") for r in self.reader.rows("ready", rid=rid, generation=gen + 1)}
         old_placement = {r["rank"]: r.get("placement") for r in self.reader.rows("ready", rid=rid, generation=gen)}
         rec = dict(rid=rid, fault_kind="sigkill_mid_backward", generation=gen, killed_rank=kill["rank"],

@@ -112,3 +112,21 @@ def test_shipped_configs_validate():
     for f in files:
         cfg = load_config(f)
         assert cfg["train_args"], f
+
+
+def test_joint_boundary_needs_every_contributing_rank():
+    from shift_b200.control.session import joint_boundary
+
+    def c(rank, step, participants=2, contributed=True, t=None):
+        return {"kind": "commit", "rid": 1, "generation": 1, "rank": rank, "step": step,
+                "participants": participants, "contributed": contributed, "time": t if t is not None else step + 0.1 * rank}
+
+    rows = [c(0, 6), c(1, 6, contributed=False),          # rank 1 healed at step 6: did not contribute
+            c(0, 7), c(1, 7, participants=1),              # rank 1 committed step 7 alone
+            c(0, 8), c(1, 8, t=20.0)]
+    assert joint_boundary(rows, 1, 1, 5, 2, 2) == (8, 20.0)
+    assert joint_boundary(rows, 1, 1, 8, 2, 2) is None       # nothing joint past step 8
+    assert joint_boundary(rows, 1, 1, 5, 2, 1) == (6, 6.0)   # one rank: its own joint commit suffices
+    assert joint_boundary(rows, 1, 0, 5, 2, 2) is None       # other generation
+    missing_rank = [r for r in rows if r["rank"] == 0]
+    assert joint_boundary(missing_rank, 1, 1, 5, 2, 2) is None

@@ -244,7 +244,8 @@ class Worker:
             return
         sd = self.engine.state_dict()
         payload = cpu_tree(dict(step=self.progress["updates"], gradients=grad.detach().float(),
-                                model=sd["model"], optimizer=sd["optimizer"], scheduler=sd["scheduler"]))
+                                model=sd["model"], optimizer=sd["optimizer"], scheduler=sd["scheduler"],
+                                offsets={k: [int(o), list(sh)] for k, (o, sh) in self.engine.store.offsets.items()}))
         torch.save(payload, self.out / f"reference_step{self.progress['updates']}_r{self.rank}.pt")
         self.event("reference_dump", step=self.progress["updates"])
 

@@ -71,6 +71,15 @@ def test_flat_vs_shift_reference_dumps(tmp_path):
     bad = summarize(flat_dir, tmp_path / "shift", comparison=res)
     assert not bad["pass"] and not bad["checks"]["same_routing"]["pass"]
     assert bad["checks"]["same_batch_plans"]["pass"]
+    # single-coordinate AdamW trace: both runs follow the recurrence on the coordinate where they differ most
+    from shift_b200.analysis.adam_trace import compare as adam_compare
+    tr = adam_compare(flat_dir, tmp_path / "shift", step=3)
+    for run in ("flat", "shift"):
+        t = tr[run]
+        assert t["adam_step"] == 3
+        assert abs(t["m_residual"]) <= 1e-6 * max(1.0, abs(t["m"])) + 1e-9, t
+        assert abs(t["v_residual"]) <= 1e-5 * abs(t["v"]) + 1e-12, t
+        assert abs(t["master_residual"]) <= 1e-6 * max(1.0, abs(t["master"])), t
     # the oracle is sensitive: a perturbed model fails it
     p = torch.load(flat_dir / "reference_step3_r0.pt", weights_only=False)
     name = next(iter(p["model"]))

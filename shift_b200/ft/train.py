@@ -89,6 +89,10 @@ def parse_args(argv=None):
     p.add_argument("--trace-routing", action="store_true",
                    help="also log a 'routing' event per step, sample and MoE layer with the digest of the router's "
                         "top-k expert indices (read by shift_b200.analysis.trajectory)")
+    p.add_argument("--reference-anchor", default="",
+                   help="start from another run's reference dump: the directory holding reference_step<k>_r<rank>.pt")
+    p.add_argument("--reference-anchor-step", type=int, default=0,
+                   help="k of the anchor dump; training continues at step k with that model, optimizer and scheduler")
     p.add_argument("--seed", type=int, default=2026)
     return p.parse_args(argv)
 
@@ -236,6 +240,23 @@ class Worker:
                 self.event("routing", step=step, sample=sample, layer=layer, topk_hash=h)
         return loss
 
+    def load_anchor(self):
+        """Continue from the committed state of another run's reference dump
+        (model, optimizer, scheduler after step k; the reference's
+        --reference-anchor): two runs anchored at the same dump start from
+        identical bits, so their next steps' routing and gradients can be
+        compared without the drift of earlier steps."""
+        a = self.args
+        path = Path(a.reference_anchor) / f"reference_step{a.reference_anchor_step}_r{self.rank}.pt"
+        dump = torch.load(path, map_location="cpu", weights_only=False)
+        assert int(dump["step"]) == a.reference_anchor_step, (dump["step"], a.reference_anchor_step)
+        self.engine.load_state_dict(_to_device({k: dump[k] for k in ("model", "optimizer", "scheduler")},
+                                               self.device))
+        self.progress["updates"] = int(dump["step"])
+        if self.manager is not None:
+            self.manager.load_state_dict({"step": int(dump["step"])})
+        self.event("reference_anchor_loaded", step=int(dump["step"]), source=str(path))
+
     def reference_dump(self, grad):
         """Per-step numerical reference (shift_full/train.py:584-587 semantics):
         the averaged gradient and the committed state after the step."""
@@ -253,6 +274,8 @@ class Worker:
         """The flat baseline: no quorum, no Manager; one replica trains every
         data rank's microbatches (the same global batch as the shift run)."""
         a = self.args
+        if a.reference_anchor:
+            self.load_anchor()
         self.event("ready", model=a.model, mode="flat", params=self.engine.store.numel,
                    hashes=self.current_hashes() if a.audit_state else {})
         eng = self.engine
@@ -323,6 +346,8 @@ class Worker:
         started = self.phase("manager_init", started)
         if a.resume_checkpoint:
             self.resume()
+        if a.reference_anchor:
+            self.load_anchor()
         self.event("ready", hashes=self.current_hashes() if a.audit_state else {}, model=a.model,
                    params=self.engine.store.numel, device=str(self.device), backend=backend, reduce=a.reduce,
                    full_parameters=self.cfg.param_count())

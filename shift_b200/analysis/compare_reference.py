@@ -53,11 +53,16 @@ def compare_tensors(a, b, atol: float, rtol: float) -> dict:
     return {"pass": bool(ok), "worst_excess": worst, "worst_leaf": worst_key, "leaves": len(la)}
 
 
-def compare_runs(run_a, run_b, steps=None, ranks: int = 1) -> dict:
+def compare_runs(run_a, run_b, steps=None, ranks: int = 1, strict: bool = False) -> dict:
+    """``strict``: zero tolerances (bitwise equality of every leaf) -- the
+    reference's strict-fp32 comparison, which a flat run and a cross-replica
+    average are expected to fail from the first update whose reductions
+    round in a different order."""
     run_a, run_b = Path(run_a), Path(run_b)
+    tol = {f: (0.0, 0.0) for f in TOLERANCES} if strict else TOLERANCES
     if steps is None:
         steps = sorted(int(p.name.split("_step")[1].split("_")[0]) for p in run_a.glob("reference_step*_r0.pt"))
-    out = {"steps": {}, "tolerances": TOLERANCES}
+    out = {"steps": {}, "tolerances": tol, "strict": strict}
     all_ok = bool(steps)
     for k in steps:
         for r in range(ranks):
@@ -68,7 +73,7 @@ def compare_runs(run_a, run_b, steps=None, ranks: int = 1) -> dict:
                 continue
             a = torch.load(pa, weights_only=False)
             b = torch.load(pb, weights_only=False)
-            res = {f: compare_tensors(a[f], b[f], *TOLERANCES[f]) for f in TOLERANCES}
+            res = {f: compare_tensors(a[f], b[f], *tol[f]) for f in TOLERANCES}
             res["scheduler"] = {"pass": a["scheduler"] == b["scheduler"]}
             res["pass"] = all(v["pass"] for v in res.values() if isinstance(v, dict))
             out["steps"][f"{k}/{r}"] = res
@@ -83,10 +88,11 @@ def main(argv=None):
     ap.add_argument("run_b")
     ap.add_argument("--steps", default="")
     ap.add_argument("--ranks", type=int, default=1)
+    ap.add_argument("--strict", action="store_true", help="zero tolerances (bitwise equality)")
     ap.add_argument("--out", default="")
     a = ap.parse_args(argv)
     steps = [int(x) for x in a.steps.split(",") if x] or None
-    res = compare_runs(a.run_a, a.run_b, steps, a.ranks)
+    res = compare_runs(a.run_a, a.run_b, steps, a.ranks, a.strict)
     text = json.dumps(res, indent=1, default=str)
     if a.out:
         Path(a.out).write_text(text)

@@ -51,6 +51,10 @@ def test_flat_vs_shift_reference_dumps(tmp_path):
         s.finish()
     res = compare_runs(flat_dir, tmp_path / "shift", steps=[1, 2, 3])
     assert res["pass"], json.dumps(res, default=str)[:2000]
+    # strict (bitwise) comparison: the runs round their reductions in different orders
+    strict = compare_runs(flat_dir, tmp_path / "shift", steps=[1, 2, 3], strict=True)
+    assert strict["strict"] and strict["tolerances"]["model"] == (0.0, 0.0)
+    assert all(strict["steps"][f"{k}/0"]["scheduler"]["pass"] for k in (1, 2, 3))
     commits = [json.loads(x) for f in sorted((tmp_path / "shift").glob("events_g0_r*.jsonl"))
                for x in f.read_text().splitlines() if '"commit"' in x]
     commits = [c for c in commits if c.get("kind") == "commit"]

@@ -22,15 +22,52 @@ import torch
 TOLERANCES = {"gradients": (1e-5, 1e-3), "model": (1e-6, 1e-4), "optimizer": (1e-5, 1e-3)}
 
 
-def _leaves(tree, prefix=""):
+def _leaves(tree, prefix="", keep_scalars: bool = False):
+    """(path, leaf) pairs in a fixed order.  Tensors always; with
+    ``keep_scalars`` also every non-container leaf (ints, floats, strings)."""
     if isinstance(tree, torch.Tensor):
         yield prefix, tree
     elif isinstance(tree, dict):
         for k in sorted(tree, key=lambda x: (type(x).__name__, str(x))):
-            yield from _leaves(tree[k], f"{prefix}/{k}")
+            yield from _leaves(tree[k], f"{prefix}/{k}", keep_scalars)
     elif isinstance(tree, (list, tuple)):
         for i, v in enumerate(tree):
-            yield from _leaves(v, f"{prefix}/{i}")
+            yield from _leaves(v, f"{prefix}/{i}", keep_scalars)
+    elif keep_scalars:
+        yield prefix, tree
+
+
+def _bitwise_equal(x, y) -> tuple[bool, str]:
+    """Strict equality of two leaves: same type; tensors of the same dtype,
+    shape and layout with identical bytes (so -0.0 differs from 0.0 and NaNs
+    compare by payload); other leaves by ``==``."""
+    if isinstance(x, torch.Tensor) != isinstance(y, torch.Tensor):
+        return False, "tensor vs non-tensor"
+    if not isinstance(x, torch.Tensor):
+        return (type(x) is type(y) and x == y), f"{x!r} != {y!r}"
+    if x.dtype != y.dtype:
+        return False, f"dtype {x.dtype} vs {y.dtype}"
+    if x.shape != y.shape or x.layout != y.layout:
+        return False, f"shape/layout {tuple(x.shape)}/{x.layout} vs {tuple(y.shape)}/{y.layout}"
+    xa, ya = x.detach().cpu().contiguous(), y.detach().cpu().contiguous()
+    if xa.numel() == 0:
+        return True, ""
+    same = torch.equal(xa.flatten().view(torch.uint8), ya.flatten().view(torch.uint8))
+    return same, "" if same else "bytes differ"
+
+
+def compare_strict(a, b) -> dict:
+    """Bitwise comparison of two trees, non-tensor leaves included."""
+    la, lb = dict(_leaves(a, keep_scalars=True)), dict(_leaves(b, keep_scalars=True))
+    if la.keys() != lb.keys():
+        return {"pass": False, "error": "different structure", "only_a": sorted(la.keys() - lb.keys())[:5],
+                "only_b": sorted(lb.keys() - la.keys())[:5]}
+    diffs = []
+    for k in la:
+        ok, why = _bitwise_equal(la[k], lb[k])
+        if not ok:
+            diffs.append({"leaf": k, "why": why})
+    return {"pass": not diffs, "differing_leaves": len(diffs), "first": diffs[:5], "leaves": len(la)}
 
 
 def compare_tensors(a, b, atol: float, rtol: float) -> dict:
@@ -54,10 +91,11 @@ def compare_tensors(a, b, atol: float, rtol: float) -> dict:
 
 
 def compare_runs(run_a, run_b, steps=None, ranks: int = 1, strict: bool = False) -> dict:
-    """``strict``: zero tolerances (bitwise equality of every leaf) -- the
-    reference's strict-fp32 comparison, which a flat run and a cross-replica
-    average are expected to fail from the first update whose reductions
-    round in a different order."""
+    """``strict``: bitwise equality of every leaf -- dtypes, shapes and
+    bytes of tensors, and non-tensor leaves by ``==`` (the reference's strict
+    fp32 comparison, shift_full/compare_reference.py:160-190), which a flat
+    run and a cross-replica average are expected to fail from the first
+    update whose reductions round in a different order."""
     run_a, run_b = Path(run_a), Path(run_b)
     tol = {f: (0.0, 0.0) for f in TOLERANCES} if strict else TOLERANCES
     if steps is None:
@@ -73,7 +111,10 @@ def compare_runs(run_a, run_b, steps=None, ranks: int = 1, strict: bool = False)
                 continue
             a = torch.load(pa, weights_only=False)
             b = torch.load(pb, weights_only=False)
-            res = {f: compare_tensors(a[f], b[f], *tol[f]) for f in TOLERANCES}
+            if strict:
+                res = {f: compare_strict(a[f], b[f]) for f in TOLERANCES}
+            else:
+                res = {f: compare_tensors(a[f], b[f], *tol[f]) for f in TOLERANCES}
             res["scheduler"] = {"pass": a["scheduler"] == b["scheduler"]}
             res["pass"] = all(v["pass"] for v in res.values() if isinstance(v, dict))
             out["steps"][f"{k}/{r}"] = res
@@ -88,7 +129,7 @@ def main(argv=None):
     ap.add_argument("run_b")
     ap.add_argument("--steps", default="")
     ap.add_argument("--ranks", type=int, default=1)
-    ap.add_argument("--strict", action="store_true", help="zero tolerances (bitwise equality)")
+    ap.add_argument("--strict", action="store_true", help="bitwise equality of every leaf (dtype, shape, bytes; non-tensor leaves by ==)")
     ap.add_argument("--out", default="")
     a = ap.parse_args(argv)
     steps = [int(x) for x in a.steps.split(",") if x] or None

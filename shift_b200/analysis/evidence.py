@@ -27,8 +27,11 @@ import argparse
 import hashlib
 import io
 import json
+import os
 import re
+import shutil
 import tarfile
+import tempfile
 from pathlib import Path
 
 HOST_KEYS = {"host_ip", "physical_node", "hostname", "host", "store_addr", "store_address", "manager_addr",
@@ -105,36 +108,53 @@ def pack(sessions, out, with_dumps=False) -> dict:
 
 
 def unpack(archive, dest) -> dict:
+    """Verify the whole bundle, then extract it.  Every member must be a
+    regular file with a safe relative name, be listed in MANIFEST.json with
+    its size and SHA-256, and every listed file must be present.  Nothing is
+    written until all of that holds; the files are then written into a
+    temporary directory beside ``dest`` and moved into place, so a bad
+    bundle leaves ``dest`` untouched."""
     dest = Path(dest).resolve()
-    dest.mkdir(parents=True, exist_ok=True)
+    verified: dict[str, bytes] = {}
     with tarfile.open(archive, "r:gz") as tar:
-        members = tar.getmembers()
         try:
             manifest = json.loads(tar.extractfile("MANIFEST.json").read())["files"]
         except (KeyError, AttributeError, ValueError) as exc:
             raise ValueError(f"archive has no readable MANIFEST.json: {exc}")
-        seen = set()
-        for m in members:
+        for m in tar.getmembers():
             if m.name == "MANIFEST.json":
                 continue
             parts = Path(m.name).parts
-            if not m.isfile() or Path(m.name).is_absolute() or ".." in parts:
+            if not m.isfile() or Path(m.name).is_absolute() or ".." in parts or not parts:
                 raise ValueError(f"unsafe member: {m.name}")
             if m.name not in manifest:
                 raise ValueError(f"member not in manifest: {m.name}")
+            if m.name in verified:
+                raise ValueError(f"member appears twice: {m.name}")
             data = tar.extractfile(m).read()
             if len(data) != manifest[m.name]["size"] or hashlib.sha256(data).hexdigest() != manifest[m.name]["sha256"]:
                 raise ValueError(f"digest mismatch: {m.name}")
-            target = (dest / m.name).resolve()
-            if dest not in target.parents:
-                raise ValueError(f"unsafe member: {m.name}")
-            target.parent.mkdir(parents=True, exist_ok=True)
-            target.write_bytes(data)
-            seen.add(m.name)
-        missing = sorted(set(manifest) - seen)
+            verified[m.name] = data
+        missing = sorted(set(manifest) - set(verified))
         if missing:
             raise ValueError(f"manifest lists missing members: {missing[:3]}")
-    return {"files": len(seen), "dest": str(dest)}
+    dest.parent.mkdir(parents=True, exist_ok=True)
+    stage = Path(tempfile.mkdtemp(prefix=f".{dest.name}.", dir=dest.parent)).resolve()
+    try:
+        for name, data in verified.items():
+            target = (stage / name).resolve()
+            if stage not in target.parents:
+                raise ValueError(f"unsafe member: {name}")
+            target.parent.mkdir(parents=True, exist_ok=True)
+            target.write_bytes(data)
+        dest.mkdir(parents=True, exist_ok=True)
+        for name in verified:
+            final = dest / name
+            final.parent.mkdir(parents=True, exist_ok=True)
+            os.replace(stage / name, final)
+    finally:
+        shutil.rmtree(stage, ignore_errors=True)
+    return {"files": len(verified), "dest": str(dest)}
 
 
 def main(argv=None) -> int:

@@ -2,89 +2,99 @@
 discovery from /proc, tree termination, and orphan reaping that never steals
 the exit status of a child owned by a ``subprocess.Popen``.
 
-Same contract as shift_full/process_tree.py:37-97 and shift_min/supervisor.py:12-33
-(a supervisor adopts orphaned grandchildren, reaps only zombies among its
-direct children, and only those not excluded).
+Same contract as shift_full/process_tree.py:37-97 and shift_min/supervisor.py:12-33:
+a supervisor adopts orphaned grandchildren and collects only zombies among
+its direct children that are not excluded.  Process state comes from
+``/proc/<pid>/status``.
 """
 from __future__ import annotations
 
 import ctypes
+import ctypes.util
 import os
 import signal
 import sys
 import time
-from pathlib import Path
 
-PR_SET_CHILD_SUBREAPER = 36
-PR_GET_CHILD_SUBREAPER = 37
-_prctl = None
+_PR_SET_CHILD_SUBREAPER = 36       # <linux/prctl.h>
+_PR_GET_CHILD_SUBREAPER = 37
 
 
-def _libc_prctl():
-    global _prctl
-    if not sys.platform.startswith("linux"):
-        raise RuntimeError("child subreapers are supported only on Linux")
-    if _prctl is None:
-        fn = ctypes.CDLL(None, use_errno=True).prctl
-        fn.argtypes = [ctypes.c_int, ctypes.c_void_p, ctypes.c_ulong, ctypes.c_ulong, ctypes.c_ulong]
-        fn.restype = ctypes.c_int
-        _prctl = fn
-    return _prctl
+class _Libc:
+    """Lazily bound ``prctl(2)`` from the C library of this process."""
 
+    fn = None
 
-def _prctl_call(option: int, arg) -> int:
-    fn = _libc_prctl()
-    ctypes.set_errno(0)
-    ptr = ctypes.c_void_p(arg) if isinstance(arg, int) else ctypes.cast(arg, ctypes.c_void_p)
-    r = fn(option, ptr, 0, 0, 0)
-    if r == -1:
-        err = ctypes.get_errno()
-        raise OSError(err, os.strerror(err))
-    return r
+    @classmethod
+    def prctl(cls, option: int, value: int) -> int:
+        if sys.platform != "linux":
+            raise RuntimeError(f"prctl is Linux-only (this is {sys.platform})")
+        if cls.fn is None:
+            libc = ctypes.CDLL(ctypes.util.find_library("c") or None, use_errno=True)
+            f = libc.prctl
+            f.restype = ctypes.c_int
+            f.argtypes = [ctypes.c_int] + [ctypes.c_ulong] * 4
+            cls.fn = f
+        rc = cls.fn(option, value, 0, 0, 0)
+        if rc < 0:
+            code = ctypes.get_errno()
+            raise OSError(code, f"prctl({option}): {os.strerror(code)}")
+        return rc
 
 
 def enable_subreaper():
-    _prctl_call(PR_SET_CHILD_SUBREAPER, 1)
+    """Make this process adopt orphaned descendants (instead of init)."""
+    _Libc.prctl(_PR_SET_CHILD_SUBREAPER, 1)
 
 
 def is_subreaper() -> bool:
-    v = ctypes.c_int(0)
-    _prctl_call(PR_GET_CHILD_SUBREAPER, ctypes.byref(v))
-    return v.value == 1
+    flag = ctypes.c_int(-1)
+    _Libc.prctl(_PR_GET_CHILD_SUBREAPER, ctypes.addressof(flag))
+    return flag.value != 0
 
 
-def _proc_stat(pid: int):
-    """(state, ppid) of a process, or None if it vanished."""
+def _status(pid: int):
+    """(state letter, parent pid) from /proc/<pid>/status, or None once the
+    process is gone or unreadable."""
+    fields = {}
     try:
-        s = Path(f"/proc/{pid}/stat").read_text()
-    except (FileNotFoundError, ProcessLookupError, PermissionError):
+        with open(f"/proc/{pid}/status") as f:
+            for line in f:
+                key, _, val = line.partition(":")
+                if key in ("State", "PPid"):
+                    fields[key] = val.strip()
+                    if len(fields) == 2:
+                        break
+    except OSError:
         return None
-    rest = s[s.rfind(")") + 2:].split()
     try:
-        return rest[0], int(rest[1])
-    except (IndexError, ValueError):
+        return fields["State"][:1], int(fields["PPid"])
+    except (KeyError, ValueError):
         return None
+
+
+def _all_pids():
+    with os.scandir("/proc") as it:
+        return [int(e.name) for e in it if e.name.isdigit()]
 
 
 def children_of(parent: int):
+    """[(pid, state letter)] of the live or zombie children of ``parent``."""
     out = []
-    for e in Path("/proc").iterdir():
-        if not e.name.isdecimal():
-            continue
-        st = _proc_stat(int(e.name))
-        if st and st[1] == parent:
-            out.append((int(e.name), st[0]))
+    for pid in _all_pids():
+        st = _status(pid)
+        if st is not None and st[1] == parent:
+            out.append((pid, st[0]))
     return out
 
 
 def descendants(root: int) -> list[int]:
     """All live descendants of ``root`` (breadth first), excluding root."""
     parent_of = {}
-    for e in Path("/proc").iterdir():
-        if e.name.isdecimal():
-            st = _proc_stat(int(e.name))
-            if st:
-                parent_of[int(e.name)] = st[1]
+    for pid in _all_pids():
+        st = _status(pid)
+        if st is not None:
+            parent_of[pid] = st[1]
     kids: dict[int, list[int]] = {}
     for pid, pp in parent_of.items():
         kids.setdefault(pp, []).append(pid)
@@ -116,29 +126,31 @@ def terminate(proc_or_pid, sig=signal.SIGKILL) -> list[int]:
 
 
 def reap_orphans(exclude_pids=(), timeout: float = 2.0) -> list[int]:
-    """Reap zombie direct children (adopted orphans) that are not excluded.
-
-    Only zombies are waited for, by pid, so a status owned by a Popen object is
-    never consumed by a blanket waitpid(-1)."""
+    """Collect adopted orphans: wait, by pid, for each zombie child of this
+    process that is not in ``exclude_pids``, until no such child is left or
+    ``timeout`` seconds have passed.  A child owned by a ``subprocess.Popen``
+    belongs in ``exclude_pids``; waiting by pid (never ``waitpid(-1)``) keeps
+    its exit status for its owner."""
     if not is_subreaper():
-        raise RuntimeError("enable_subreaper() must be called before reaping")
-    excluded = {int(p) for p in exclude_pids}
-    deadline = time.monotonic() + max(0.0, timeout)
-    reaped = []
+        raise RuntimeError("reap_orphans needs enable_subreaper() first: orphans are not re-parented here")
+    keep = {int(p) for p in exclude_pids}
+    me = os.getpid()
+    give_up = time.monotonic() + max(0.0, timeout)
+    nap = 0.001
+    collected: list[int] = []
     while True:
-        pending = False
-        for pid, state in children_of(os.getpid()):
-            if pid in excluded:
-                continue
-            pending = True
-            if state != "Z":
+        left = [(pid, st) for pid, st in children_of(me) if pid not in keep]
+        for pid, st in left:
+            if st != "Z":
                 continue
             try:
-                done, _ = os.waitpid(pid, os.WNOHANG)
-            except ChildProcessError:
-                continue
-            if done:
-                reaped.append(done)
-        if not pending or time.monotonic() >= deadline:
-            return reaped
-        time.sleep(min(0.02, max(0.0, deadline - time.monotonic())))
+                got, _ = os.waitpid(pid, os.WNOHANG)
+            except ChildProcessError:       # somebody else collected it
+                got = 0
+            if got == pid:
+                collected.append(pid)
+        remaining = give_up - time.monotonic()
+        if not left or remaining <= 0:
+            return collected
+        time.sleep(min(nap, remaining))
+        nap = min(nap * 2, 0.05)

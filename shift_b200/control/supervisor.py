@@ -139,7 +139,7 @@ def main(argv=None):
         t0 = time.monotonic()
         while "LISTENING" not in (out / "lighthouse.log").read_text():
             if lighthouse.poll() is not None or time.monotonic() - t0 > 10:
-                raise RuntimeError("Lighthouse failed to start")
+                raise RuntimeError("the lighthouse daemon exited before it accepted connections")
             time.sleep(0.02)
 
     def devices_for_replica():
@@ -236,7 +236,7 @@ def main(argv=None):
                 break
             if time.monotonic() >= deadline:
                 ev("timeout", seconds=args.seconds)
-                raise TimeoutError(f"session exceeded --seconds={args.seconds}")
+                raise TimeoutError(f"training did not finish within the {args.seconds} s allowed by --seconds")
             if training.poll() is None and generation not in faulted:
                 km, wm = out / f"KILL_g{generation}_r{args.replica}", out / f"WORKER_KILL_g{generation}_r{args.replica}"
                 if km.is_file():

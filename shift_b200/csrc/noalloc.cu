@@ -6,6 +6,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <cstdint>
 #include <mutex>
 
 #include "common.cuh"
@@ -128,6 +129,13 @@ extern "C" __attribute__((visibility("default"))) int sb_rmsnorm_bwd_noalloc(
     int hidden, void* stream) {
   using namespace sb::noalloc;
   if (rows < 0 || (hidden != 256 && hidden != 512 && hidden != 1024)) return 1;
+  // The kernels move bf16 rows as 16-byte vectors and fp32 values one at a
+  // time: refuse, before any launch, a pointer the hardware cannot access
+  // that way (a misaligned vector access faults the whole context).
+  auto aligned = [](const void* p, uintptr_t a) { return p != nullptr && (reinterpret_cast<uintptr_t>(p) % a) == 0; };
+  if (!aligned(dy, 16) || !aligned(x, 16) || !aligned(w, 16) || !aligned(dx, 16) ||
+      (dres != nullptr && !aligned(dres, 16)) || !aligned(rstd, 4) || !aligned(dw, 4))
+    return 4;
   int sms = 148;
   int dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);

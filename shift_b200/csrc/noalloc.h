@@ -34,7 +34,10 @@ extern "C" {
 //
 // Returns 0 on success; 1 if the problem needs more scratch than
 // SB_NOALLOC_SCRATCH_FLOATS or hidden is unsupported; 2 if the one-time
-// set-up on this device failed; 3 if the launch failed.  The first call on
+// set-up on this device failed; 3 if the launch failed; 4 if a required
+// pointer is NULL or misaligned (dy, x, w, dx and a non-NULL dres must be
+// 16-byte aligned because rows move as 16-byte vectors; rstd and dw 4-byte
+// aligned), in which case nothing is launched.  The first call on
 // each device performs that set-up (it looks up the scratch array's device
 // address), so make the first call before any stream capture.  Every call
 // shares the same scratch array: calls whose kernels overlap on the GPU

@@ -50,7 +50,7 @@ def pack_state(state: object, step: int, device: torch.device):
             continue
         count += 1
         if v.layout != torch.strided:
-            raise TypeError(f"only strided tensor leaves are supported, got {v.layout}")
+            raise TypeError(f"cannot pack a {v.layout} tensor: the wire format carries dense strided tensors")
         if v.device.type == device.type:
             g = group_of.get(v.dtype)
             if g is None:
@@ -65,17 +65,17 @@ def pack_state(state: object, step: int, device: torch.device):
         elif v.device.type == "cpu":
             cpu_bytes += v.numel() * v.element_size()
             if cpu_bytes > MAX_CPU_TENSOR_BYTES:
-                raise ValueError("CPU tensor leaves exceed the 4 MiB control-data limit")
+                raise ValueError(f"host-resident tensors in the state exceed {MAX_CPU_TENSOR_BYTES} bytes of control data")
             meta.append({"kind": "cpu", "value": v.detach().contiguous().clone()})
         else:
-            raise TypeError(f"unsupported tensor device {v.device}")
+            raise TypeError(f"cannot pack a tensor that lives on {v.device}")
     groups = [torch.cat(p, 0) for p in parts]   # independent contiguous snapshots
     wire = {"version": VERSION, "step": step, "treespec": spec,
             "groups": [{"dtype": parts[i][0].dtype, "numel": numels[i]} for i in range(len(parts))],
             "leaves": meta, "tensor_count": count, "cpu_tensor_bytes": cpu_bytes}
     blob = pickle.dumps(wire, protocol=pickle.HIGHEST_PROTOCOL)
     if len(blob) > MAX_METADATA_BYTES:
-        raise ValueError(f"checkpoint metadata is {len(blob)} bytes; limit is {MAX_METADATA_BYTES}")
+        raise ValueError(f"pickled state description needs {len(blob)} bytes, more than the {MAX_METADATA_BYTES} allowed")
     return blob, groups, count, cpu_bytes
 
 
@@ -83,7 +83,7 @@ def unpack_state(wire: dict, groups: list[torch.Tensor]):
     leaves = []
     for leaf in wire["leaves"]:
         if not isinstance(leaf, dict):
-            raise ValueError("invalid checkpoint leaf metadata")
+            raise ValueError("state description: a leaf entry is not a well-formed record")
         kind = leaf.get("kind")
         if kind in ("value", "cpu"):
             leaves.append(leaf.get("value"))
@@ -91,38 +91,38 @@ def unpack_state(wire: dict, groups: list[torch.Tensor]):
             g, off, shape = leaf.get("group"), leaf.get("offset"), leaf.get("shape")
             if (not isinstance(g, int) or g < 0 or g >= len(groups) or not isinstance(off, int) or off < 0
                     or not isinstance(shape, (tuple, list)) or any(not isinstance(d, int) or d < 0 for d in shape)):
-                raise ValueError("invalid packed tensor leaf metadata")
+                raise ValueError("state description: a device leaf has a bad group, offset or shape")
             n = math.prod(shape)
             if off + n > groups[g].numel():
-                raise ValueError("tensor leaf exceeds its packed group")
+                raise ValueError("state description: a device leaf runs past the end of its flat buffer")
             leaves.append(groups[g].narrow(0, off, n).view(tuple(shape)))
         else:
-            raise ValueError(f"unknown checkpoint leaf kind: {kind!r}")
+            raise ValueError(f"state description: leaf kind {kind!r} is not value, cpu or cuda")
     return tree_unflatten(leaves, wire["treespec"])
 
 
 def validate_wire(wire, step: int):
     if not isinstance(wire, dict) or wire.get("version") != VERSION:
-        raise ValueError("unsupported packed transport metadata")
+        raise ValueError("state description has an unknown wire version")
     if wire.get("step") != step:
-        raise ValueError(f"checkpoint step mismatch: {wire.get('step')} != {step}")
+        raise ValueError(f"received the state of step {wire.get('step')} while expecting step {step}")
     if not isinstance(wire.get("groups"), list) or not isinstance(wire.get("leaves"), list):
-        raise ValueError("malformed packed transport metadata")
+        raise ValueError("state description is missing required fields")
     cpu = 0
     for leaf in wire["leaves"]:
         if isinstance(leaf, dict) and leaf.get("kind") == "cpu":
             v = leaf.get("value")
             if not isinstance(v, torch.Tensor) or v.device.type != "cpu" or v.layout != torch.strided:
-                raise ValueError("invalid CPU tensor in checkpoint metadata")
+                raise ValueError("state description: a host tensor entry is malformed")
             cpu += v.numel() * v.element_size()
             if cpu > MAX_CPU_TENSOR_BYTES:
-                raise ValueError("CPU tensor leaves exceed the 4 MiB control-data limit")
+                raise ValueError(f"host-resident tensors in the state exceed {MAX_CPU_TENSOR_BYTES} bytes of control data")
     if cpu != wire.get("cpu_tensor_bytes"):
-        raise ValueError("CPU tensor byte count does not match metadata")
+        raise ValueError("host tensor bytes differ from the declared total")
     for i, g in enumerate(wire["groups"]):
         if (not isinstance(g, dict) or not isinstance(g.get("dtype"), torch.dtype) or not isinstance(g.get("numel"), int)
                 or g["numel"] < 0):
-            raise ValueError(f"invalid tensor group {i}")
+            raise ValueError(f"flat buffer #{i} has a bad dtype or length")
 
 
 class PackedTransport:
@@ -177,7 +177,7 @@ class PackedTransport:
         self._pg.recv([length], src_rank, tag=1).wait()
         n = int(length.item())
         if n <= 0 or n > MAX_METADATA_BYTES:
-            raise ValueError(f"invalid checkpoint metadata length {n}; limit is {MAX_METADATA_BYTES}")
+            raise ValueError(f"peer announced a {n}-byte state description (allowed: 1..{MAX_METADATA_BYTES})")
         meta = torch.empty(n, dtype=torch.uint8, device=self._device)
         self._pg.recv([meta], src_rank, tag=2).wait()
         wire = pickle.loads(meta.cpu().numpy().tobytes())
@@ -213,7 +213,7 @@ class FrozenTransport(PackedTransport):
 
     def send_checkpoint(self, dst_ranks, step, state_dict, timeout=None, packed=None):
         if step != self.frozen_step:
-            raise ValueError("frozen version mismatch")
+            raise ValueError("a frozen tensor was modified while its snapshot was being sent")
         if self.ready is not None:
             self.ready.wait()
         return super().send_checkpoint(dst_ranks, step, None, timeout, packed=self.frozen)

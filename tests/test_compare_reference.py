@@ -55,6 +55,9 @@ def test_flat_vs_shift_reference_dumps(tmp_path):
     strict = compare_runs(flat_dir, tmp_path / "shift", steps=[1, 2, 3], strict=True)
     assert strict["strict"] and strict["tolerances"]["model"] == (0.0, 0.0)
     assert all(strict["steps"][f"{k}/0"]["scheduler"]["pass"] for k in (1, 2, 3))
+    assert not strict["pass"]          # different reduction orders differ in the last bits
+    # a run compared with itself passes strict mode
+    assert compare_runs(flat_dir, flat_dir, steps=[1, 2, 3], strict=True)["pass"]
     commits = [json.loads(x) for f in sorted((tmp_path / "shift").glob("events_g0_r*.jsonl"))
                for x in f.read_text().splitlines() if '"commit"' in x]
     commits = [c for c in commits if c.get("kind") == "commit"]
@@ -90,3 +93,32 @@ def test_flat_vs_shift_reference_dumps(tmp_path):
     p["model"][name] = p["model"][name] + 1e-3
     torch.save(p, flat_dir / "reference_step3_r0.pt")
     assert not compare_runs(flat_dir, tmp_path / "shift", steps=[3])["pass"]
+
+
+def test_strict_mode_sees_what_tolerances_forgive(tmp_path):
+    """Dumps differing by one ulp, by dtype, by the sign of zero, or in an int
+    leaf pass the tolerant comparison and fail the strict one."""
+    base = {"gradients": {"w": torch.tensor([1.0, 0.0, 2.0])},
+            "model": {"w": torch.tensor([1.0, 0.0, 2.0])},
+            "optimizer": {"state": {0: {"step": 3, "exp_avg": torch.tensor([0.5, 0.25])}}},
+            "scheduler": {"last_epoch": 3}}
+    import copy
+    variants = {
+        "ulp": lambda d: d["model"].__setitem__("w", torch.nextafter(d["model"]["w"], torch.tensor(9.0))),
+        "dtype": lambda d: d["gradients"].__setitem__("w", d["gradients"]["w"].double()),
+        "negzero": lambda d: d["model"].__setitem__("w", torch.tensor([1.0, -0.0, 2.0])),
+        "int_leaf": lambda d: d["optimizer"]["state"][0].__setitem__("step", 4),
+    }
+    a = tmp_path / "a"
+    a.mkdir()
+    torch.save(base, a / "reference_step1_r0.pt")
+    for name, change in variants.items():
+        b = tmp_path / name
+        b.mkdir()
+        d = copy.deepcopy(base)
+        change(d)
+        torch.save(d, b / "reference_step1_r0.pt")
+        assert not compare_runs(a, b, steps=[1], strict=True)["pass"], name
+        if name != "int_leaf":       # the tolerant mode compares tensors only
+            assert compare_runs(a, b, steps=[1])["pass"], name
+    assert compare_runs(a, a, steps=[1], strict=True)["pass"]

@@ -68,3 +68,12 @@ def test_unpack_refuses_bad_archives(tmp_path):
     with pytest.raises(ValueError):
         evidence.unpack(tmp_path / "miss.tar.gz", tmp_path / "d4")
     assert not (tmp_path / "evil.json").exists()
+    # a good member followed by a bad one: nothing at all is written
+    good = b"[2]\n"
+    okg = {"size": len(good), "sha256": hashlib.sha256(good).hexdigest()}
+    _tar(tmp_path / "late.tar.gz", [("S/good.json", good), ("S/bad.json", data)],
+         {"S/good.json": okg, "S/bad.json": {"size": 99, "sha256": "0" * 64}})
+    with pytest.raises(ValueError):
+        evidence.unpack(tmp_path / "late.tar.gz", tmp_path / "d5")
+    assert not (tmp_path / "d5").exists()
+    assert not [p for p in tmp_path.iterdir() if p.name.startswith(".d5.")]

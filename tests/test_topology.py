@@ -12,8 +12,8 @@ def test_table_layouts_replica_counts_and_sources(name, expected):
     assert plan["valid"], plan["rejections"]
     assert plan["candidate_replica_count"] == expected == plan["min_dp_reference"]
     assert {r["size"] for r in plan["replicas"]} == {16 // expected}
-    for key in ("role_coverage_matches", "execution_groups_unbroken", "recovery_sources_complete",
-                "generated_min_dp_reference_matches"):
+    for key in ("roles_one_each", "groups_inside_replicas", "single_recovery_source",
+                "replicas_equal_min_dp_degree"):
         assert plan["checks"][key]["pass"], key
     for rank, sources in plan["recovery_sources"].items():
         assert len(sources) == expected - 1
@@ -35,7 +35,7 @@ def test_vendor_layouts_node_failure_survival():
 def test_overlapping_group_rejected():
     g = make_power2_layout(16, tp=2, pp=2, ep=4, etp=1)["groups"]
     bad = [[0, 1], [1, 2]] + [[r] for r in range(3, 16)]
-    with pytest.raises(TopologyError, match="execution TP groups overlap at rank 1"):
+    with pytest.raises(TopologyError, match="rank 1 is in both group #0 and group #1"):
         analyze_topology(16, g["dense_dp"], g["expert_dp"], {**g["execution"], "TP": bad})
 
 
@@ -43,15 +43,15 @@ def test_missing_dense_expert_source_reported():
     g = make_power2_layout(16, tp=2, pp=2, ep=4, etp=1)["groups"]
     res = analyze_topology(16, g["dense_dp"], [[r] for r in range(16)], g["execution"])
     assert res["candidate_replica_count"] == 2 and not res["valid"]
-    assert not res["checks"]["recovery_sources_complete"]["pass"]
-    assert "missing or ambiguous dense∩expert" in " ".join(res["rejections"])
+    assert not res["checks"]["single_recovery_source"]["pass"]
+    assert "missing or ambiguous source" in " ".join(res["rejections"])
 
 
 def test_non_power_of_two():
     res = analyze_topology(6, [[0, 1, 2], [3, 4, 5]], [[0, 1, 2], [3, 4, 5]], {"TP": [list(range(6))]})
     assert res["candidate_replica_count"] == 1 and not res["valid"]
     assert res["metrics"]["dense_dp_group_sizes"] == [3, 3]
-    with pytest.raises(TopologyError, match="world_size=12.*power of two"):
+    with pytest.raises(TopologyError, match="world_size=12.*powers of two"):
         make_power2_layout(12, tp=2, pp=2, ep=2, etp=1)
 
 
@@ -59,15 +59,15 @@ def test_fused_execution_dependency_merges_replicas():
     g = make_power2_layout(16, tp=2, pp=2, ep=4, etp=1)["groups"]
     res = analyze_topology(16, g["dense_dp"], g["expert_dp"], {**g["execution"], "FUSED": [list(range(16))]})
     assert res["candidate_replica_count"] == 1
-    assert res["checks"]["execution_groups_unbroken"]["pass"]
-    assert not res["checks"]["recovery_sources_complete"]["pass"]
+    assert res["checks"]["groups_inside_replicas"]["pass"]
+    assert not res["checks"]["single_recovery_source"]["pass"]
 
 
 def test_dp_family_names_rejected_and_infeasible_layout():
-    with pytest.raises(TopologyError, match="DP family"):
+    with pytest.raises(TopologyError, match="replicates state"):
         analyze_topology(2, [[0, 1]], [[0, 1]], {"DP": [[0], [1]]})
     # EP2 x ETP2 x PP2 needs 8 ranks per replica: a 4-GPU replica cannot hold it
-    with pytest.raises(TopologyError, match="ETP×EP×PP"):
+    with pytest.raises(TopologyError, match="ETP×EP×PP blocks"):
         make_power2_layout(4, tp=2, pp=2, ep=2, etp=2)
 
 
@@ -81,3 +81,30 @@ def test_box_layouts(n, tp, pp):
     for rank, src in plan["recovery_sources"].items():
         for other, s in src.items():
             assert s % (tp * pp) == rank % (tp * pp)
+
+
+@pytest.mark.parametrize("groups,msg", [
+    (None, "no groups given"),
+    (5, "expected a list of rank lists"),
+    ([], "the list of groups is empty"),
+    ([[0, 1], []], "group #1 has no ranks"),
+    ([[0, 1], [2, 9]], "names 9, which is not a rank"),
+    ([[0, 0], [1, 2, 3]], "rank 0 is listed twice"),
+    ([[0, 1], [2]], r"ranks \[3\] belong to no group"),
+    ([[0, True], [2, 3]], "names True"),
+])
+def test_malformed_groups_rejected(groups, msg):
+    with pytest.raises(TopologyError, match=msg):
+        analyze_topology(4, groups, [[0, 1], [2, 3]], {"TP": [[0], [1], [2], [3]]})
+
+
+def test_rank_to_node_validation_and_label_propagation_order():
+    ex = {"TP": [[0, 3], [1], [2]], "PP": [[3, 2], [0], [1]]}   # 0-3-2 chained through two families
+    res = analyze_topology(4, [[0, 1], [2], [3]], [[0, 1], [2], [3]], ex, rank_to_node=[0, 0, 1, 1])
+    assert [r["ranks"] for r in res["replicas"]] == [[0, 2, 3], [1]]
+    assert res["survivable_replicas_by_node_failure"] == {0: [], 1: [1]}
+    with pytest.raises(TopologyError, match="lists 3 nodes for 4 ranks"):
+        analyze_topology(4, [[0, 1, 2, 3]], [[0, 1, 2, 3]], {"TP": [[0], [1], [2], [3]]}, rank_to_node=[0, 0, 1])
+    with pytest.raises(TopologyError, match=r"without a node \[3\]"):
+        analyze_topology(4, [[0, 1, 2, 3]], [[0, 1, 2, 3]], {"TP": [[0], [1], [2], [3]]},
+                         rank_to_node={0: 0, 1: 0, 2: 1})

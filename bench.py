@@ -40,6 +40,7 @@ REFERENCE_PUBLISHED_TOKENS_PER_S = 5591.0   # reference SHIFT 2x8 H800, 8 x 512 
 GLOBAL_BATCH = 8
 SEQ = 2048
 METRIC = "tokens/s (device-timed, max over ranks)"
+LOSS_RTOL = 2e-3
 
 
 def parse():
@@ -52,6 +53,10 @@ def parse():
     p.add_argument("--batch", type=int, default=GLOBAL_BATCH)
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-launch-count", action="store_true")
+    p.add_argument("--no-check", action="store_true",
+                   help="skip the N>1 correctness evidence (replica fingerprints, 1-GPU loss recomputation)")
+    p.add_argument("--no-k1-compare", action="store_true",
+                   help="skip the NCCL all_reduce + AdamW arm of the cross-replica step (replicas x 1 GPU layout)")
     p.add_argument("--trace", default=None,
                    help="write a kernel timeline (chrome trace) of one untimed step per rank into this folder")
     return p.parse_args()
@@ -105,6 +110,77 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def correctness_checks(args, runner, world, rank, local, warm_losses, init_full) -> dict:
+    """After the timed loops, untimed.  (1) Every replica's committed state
+    (bf16 params, fp32 master and Adam moments) must be bit-identical at each
+    model position: 64-bit fingerprints gathered over the process group.
+    (2) The global mean loss of the W warm-up steps must match a one-GPU
+    recomputation from the same initial weights on the same global batches
+    (rank 0; relative tolerance LOSS_RTOL)."""
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.synchronize()
+    fps = [None] * world
+    dist.all_gather_object(fps, runner.state_fingerprints())
+    by_pos: dict = {}
+    for f in fps:
+        by_pos.setdefault(f["position"], []).append(f)
+    identical = all(len({(g["param"], g["master"], g["exp_avg"], g["exp_avg_sq"], g["step"]) for g in grp}) == 1
+                    for grp in by_pos.values())
+    losses = [None] * world
+    dist.all_gather_object(losses, warm_losses)
+    out = {"replicas_bit_identical": identical, "fingerprinted_positions": len(by_pos)}
+    if rank == 0:
+        from shift_b200.runner import SingleRunner
+        replicas = len({f["replica"] for f in fps})
+        glob = [sum(l[i] for l in losses) / replicas for i in range(len(warm_losses))]
+        one = SingleRunner(runner.cfg, torch.device("cuda", local), args.batch, args.seq,
+                           n_prefetch=len(runner.dev_batches), graphs=False)
+        st = one.engine.store
+        st.load_model_state_dict(init_full)
+        st.master[st.cur].copy_(st.param[st.cur].float())
+        ref = [float(one.step(i)) for i in range(len(glob))]
+        one.close()
+        del one, init_full
+        torch.cuda.empty_cache()
+        rel = max(abs(a - b) / abs(b) for a, b in zip(glob, ref)) if ref else None
+        out.update({"loss_matches_n1": bool(rel is not None and rel <= LOSS_RTOL), "loss_max_rel_diff": rel,
+                    "loss_rtol": LOSS_RTOL, "losses_n": [round(x, 5) for x in glob],
+                    "losses_n1": [round(x, 5) for x in ref]})
+    dist.barrier()
+    return out
+
+
+def k1_comparison(args, runner, world, fused_ms) -> dict:
+    """The same step with the cross-replica reduction on NCCL (all_reduce of
+    each bf16 gradient bucket on the side stream, then the local AdamW):
+    W warm-up + K device-timed steps, max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    runner.set_k1_mode("nccl")
+    base = 10_000
+    for i in range(args.warmup):
+        runner.step(base + i)
+    torch.cuda.synchronize()
+    dist.barrier()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for i in range(args.steps):
+        runner.step(base + args.warmup + i)
+    t1.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    ms = torch.tensor([t0.elapsed_time(t1) / args.steps], device="cuda")
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    runner.set_k1_mode("auto")
+    nccl_ms = float(ms)
+    return {"fused_ms_per_step": round(fused_ms, 3), "nccl_ms_per_step": round(nccl_ms, 3),
+            "fused_speedup": round(nccl_ms / fused_ms, 3),
+            "nccl_arm": "NCCL all_reduce of each bf16 gradient bucket + local fused AdamW, same step graphs"}
+
+
 def reference_arm(args):
     line = {"impl": "reference",
             "unavailable": ("reference is not installable: no setup.py/pyproject in Zwhao0/SHIFT, and its model, "
@@ -140,8 +216,14 @@ def main():
         if world > 1:
             dist.barrier()
 
+    # ---------------- correctness evidence for N > 1 (untimed) ----------------
+    check = world > 1 and not args.no_check
+    init_full = runner.initial_full_state() if (check and rank == 0) else None
+    warm_losses = []
     for i in range(args.warmup):
-        runner.step(i)
+        loss = runner.step(i)
+        if check:
+            warm_losses.append(float(loss))      # this rank's share of the step's global mean loss
     torch.cuda.synchronize()
 
     # ---------------- launch count (one untimed profiled step) ----------------
@@ -174,6 +256,12 @@ def main():
         prof.export_chrome_trace(os.path.join(args.trace, f"trace_n{world}_r{rank}.json"))
         barrier()
 
+    # a few untimed steps after the profiled ones, so the timed loop starts in steady state
+    for i in range(2):
+        runner.step(args.warmup + 1 + i)
+    torch.cuda.synchronize()
+    step0 = args.warmup + 3
+
     # ---------------- device-timed loop ----------------
     clocks = ClockSampler(local)
     barrier()
@@ -184,7 +272,7 @@ def main():
     t0.record()
     for i in range(args.steps):
         torch.cuda.nvtx.range_push("step")      # lets a profiler select whole timed steps
-        runner.step(args.warmup + 1 + i)
+        runner.step(step0 + i)
         torch.cuda.nvtx.range_pop()
     t1.record()
     torch.cuda.synchronize()
@@ -206,7 +294,7 @@ def main():
         w0 = time.perf_counter()
         h2d = d2h = 0
         for i in range(args.steps):
-            loss, nb_in, nb_out = runner.step_e2e(args.warmup + 1 + args.steps + i)
+            loss, nb_in, nb_out = runner.step_e2e(step0 + args.steps + i)
             h2d, d2h = nb_in, nb_out
         torch.cuda.synchronize()
         barrier()
@@ -217,6 +305,12 @@ def main():
         e2e = {"value": tokens / (float(el_t) / args.steps), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h, "ms_per_step": float(el_t) / args.steps * 1e3, "timer": "host wall clock"}
 
+    checks = None
+    if check:
+        checks = correctness_checks(args, runner, world, rank, local, warm_losses, init_full)
+    k1 = None
+    if world > 1 and hasattr(runner, "set_k1_mode") and not args.no_k1_compare:
+        k1 = k1_comparison(args, runner, world, ms)
     runner.close()
     if rank == 0:
         line = {
@@ -230,6 +324,8 @@ def main():
             "higher_is_better": True,
             "scaling": "strong",
             "vs_baseline": round(value / REFERENCE_PUBLISHED_TOKENS_PER_S, 2),
+            "vs_baseline_note": ("cross-config context only: the published 5,591 tokens/s is the reference's "
+                                 "2x8 H800 SHIFT step at seq 512 and vocab 151,936 (8 x 512 tokens / 0.7326 s)"),
             "dtype": "bf16",
             "data": "synthetic (uniform random token ids, random N(0,0.02) init)",
             "config": {"model": "qwen-moe-0.494b (12L, h1024, 16q/4kv x64, 16 experts top-4 ffn672, vocab 32768)",
@@ -243,6 +339,10 @@ def main():
             "library_launches_per_step": library_launches,
             "impl": "ours",
         }
+        if checks is not None:
+            line.update(checks)
+        if k1 is not None:
+            line["k1"] = k1
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

@@ -236,6 +236,8 @@ def main(argv=None):
     ap.add_argument("--replicas", type=int, default=2)
     ap.add_argument("--faults", type=int, default=1)
     ap.add_argument("--fault-step", type=int, default=5)
+    ap.add_argument("--interval", type=float, default=0.0,
+                    help="seconds to keep training between a recovery and the next fault (on top of --fault-step)")
     ap.add_argument("--victim", type=int, default=1)
     ap.add_argument("--worker-kill", type=int, default=None, help="kill one rank instead of the launcher tree")
     ap.add_argument("--joint-commits", type=int, default=3)
@@ -264,6 +266,8 @@ def main(argv=None):
         for i in range(a.faults):
             target = a.fault_step * (i + 1)
             s.await_(lambda: s.last_step(a.victim) >= target, 300, f"step {target}")
+            if a.interval > 0:
+                time.sleep(a.interval)
             rec = s.fault(a.victim, "worker" if a.worker_kill is not None else "launcher",
                           a.worker_kill or 0)
             results.append(rec)

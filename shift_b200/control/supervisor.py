@@ -10,7 +10,14 @@ shift_full/supervisor.py:375-439:
 * ``WORKER_KILL_g<G>``     SIGKILL one rank (file holds the local rank)
 * ``RESTART_g<G+1>``       relaunch as generation G+1 after a fault
 * ``EXPECT_PEER_FAILURE_g<G>``  a non-zero exit of generation G is expected
+* ``PREPARE_g<N>``         pre-launch generation N as a standby (file holds
+                           ``cpu`` or ``gpu``: the trainer's ``--standby`` mode);
+                           a later ``RESTART_g<N>`` activates it instead of
+                           cold-launching (shift_full/rotation.py:141-157)
 * ``STOP``                 stop; the supervisor tears down only its own tree
+
+A ``RESTART_g<N>`` file holding ``resume_checkpoint`` relaunches with
+``--resume-checkpoint`` (the disk-checkpoint restart scenario).
 
 Replica 0 also owns the lighthouse (the C++ daemon) unless the config says
 ``external_lighthouse``.  Events go to ``supervisor_r<R>.jsonl`` and
@@ -30,7 +37,7 @@ import sys
 import time
 from pathlib import Path
 
-from ..utils.events import EventLog, read_jsonl
+from ..utils.events import EventLog, atomic_write, read_jsonl
 from . import process_tree as pt
 
 DEFAULTS = {
@@ -78,6 +85,10 @@ def load_config(path) -> dict:
     return cfg
 
 
+def atomic_touch(path: Path):
+    atomic_write(path, "")
+
+
 def provenance(root: Path) -> dict:
     out = {}
     pkg = Path(__file__).resolve().parents[1]
@@ -117,9 +128,11 @@ def main(argv=None):
     env["PYTHONPATH"] = str(Path(__file__).resolve().parents[2]) + os.pathsep + env.get("PYTHONPATH", "")
     deadline = time.monotonic() + args.seconds
     generation = 0
+    prepared: set[int] = set()
     faulted: set[int] = set()
     lighthouse = None
     training = None
+    standby = None            # (generation, launcher, activate marker) of a prepared standby
     completed = False
     logs = []
 
@@ -142,30 +155,43 @@ def main(argv=None):
                 raise RuntimeError("the lighthouse daemon exited before it accepted connections")
             time.sleep(0.02)
 
-    def devices_for_replica():
-        d = cfg["restart_devices"] if (generation > 0 and cfg["restart_devices"]) else cfg["devices"]
+    def devices_for_replica(gen):
+        d = cfg["restart_devices"] if (gen > 0 and cfg["restart_devices"]) else cfg["devices"]
         if not d:
             return ""
         return ",".join(str(x) for x in d[args.replica % len(d)])
 
-    def launch():
-        port = cfg["master_port"] + 10 * args.replica + generation
-        log = (out / f"launcher_r{args.replica}_g{generation}.log").open("w")
+    def launch(gen=None, extra=()):
+        gen = generation if gen is None else gen
+        port = cfg["master_port"] + 10 * args.replica + gen
+        log = (out / f"launcher_r{args.replica}_g{gen}.log").open("w")
         logs.append(log)
         cmd = [cfg["python"], "-m", "shift_b200.control.launch", "--nproc", str(cfg["nproc_per_node"]),
                "--master-port", str(port), "--module", cfg["entry_module"]]
-        dev = devices_for_replica()
+        dev = devices_for_replica(gen)
         if dev:
             cmd += ["--devices", dev]
-        cmd += ["--", "--session", args.session, "--replica", str(args.replica), "--generation", str(generation),
+        cmd += ["--", "--session", args.session, "--replica", str(args.replica), "--generation", str(gen),
                 "--host-ip", args.host_ip, "--root", str(args.root), "--target-steps", str(cfg["target_steps"]),
                 "--lighthouse", f"{cfg['lighthouse_ip']}:{cfg['lighthouse_port']}", "--min-replicas",
-                str(cfg["min_replicas"]), *cfg["train_args"]]
+                str(cfg["min_replicas"]), *cfg["train_args"], *extra]
         e = dict(env)
-        e["SHIFT_STORE_PORT"] = str(cfg["store_port_base"] + 10 * args.replica + generation)
+        e["SHIFT_STORE_PORT"] = str(cfg["store_port_base"] + 10 * args.replica + gen)
         proc = sp.Popen(cmd, env=e, stdout=log, stderr=sp.STDOUT, start_new_session=True)
-        ev("launched", generation=generation, launcher_pid=proc.pid, master_port=port, command=cmd)
+        ev("launched", generation=gen, launcher_pid=proc.pid, master_port=port, command=cmd,
+           standby=extra[1] if extra and extra[0] == "--standby" else None)
         return proc
+
+    def prepare_standby(gen, mode):
+        """Generation ``gen`` started ahead of need: a cpu standby waits before
+        CUDA initialisation, a gpu standby with its model built and warmed;
+        both wait for their own ACTIVATE marker."""
+        nonlocal standby
+        if mode not in ("cpu", "gpu"):
+            raise ValueError(f"PREPARE_g{gen}: standby mode must be cpu or gpu, got {mode!r}")
+        marker = f"ACTIVATE_g{gen}_r{args.replica}"
+        standby = (gen, launch(gen, ("--standby", mode, "--activate-marker", marker)), marker)
+        cev("standby_launched", generation=gen, mode=mode, launcher_pid=standby[1].pid)
 
     def ready_pid(rank, gen):
         for row in read_jsonl(out / f"events_g{gen}_r{rank}.jsonl"):
@@ -243,6 +269,10 @@ def main(argv=None):
                     inject_launcher_kill()
                 elif wm.is_file():
                     inject_worker_kill(int(wm.read_text().strip()))
+            pm = out / f"PREPARE_g{generation + 1}_r{args.replica}"
+            if standby is None and pm.is_file() and (generation + 1) not in prepared:
+                prepared.add(generation + 1)
+                prepare_standby(generation + 1, pm.read_text().strip() or "gpu")
             if training.poll() is not None:
                 rc = training.returncode
                 if all_stopped(generation):
@@ -256,11 +286,21 @@ def main(argv=None):
                     break
                 if generation in faulted:
                     nxt = generation + 1
-                    if (out / f"RESTART_g{nxt}_r{args.replica}").is_file():
+                    rm = out / f"RESTART_g{nxt}_r{args.replica}"
+                    if rm.is_file():
                         generation = nxt
-                        cev("restart_requested", generation=generation, previous_generation=generation - 1)
+                        how = rm.read_text().strip()
+                        cev("restart_requested", generation=generation, previous_generation=generation - 1,
+                            standby=standby is not None and standby[0] == nxt, policy=how or "cold")
                         ev("restart_requested", generation=generation, previous_generation=generation - 1)
-                        training = launch()
+                        if standby is not None and standby[0] == nxt:
+                            # the prepared standby becomes the replica: release it
+                            atomic_touch(out / standby[2])
+                            training = standby[1]
+                            standby = None
+                            cev("standby_activated", generation=generation)
+                        else:
+                            training = launch(extra=("--resume-checkpoint",) if how == "resume_checkpoint" else ())
                     elif (out / "STOP").exists():
                         ev("stopping", requested=True, faulted=True)
                         break
@@ -291,6 +331,8 @@ def main(argv=None):
             except sp.TimeoutExpired:
                 pass
         trc = stop_and_wait(training)
+        if standby is not None:
+            stop_and_wait(standby[1])
         lrc = stop_and_wait(lighthouse)
         reaped = pt.reap_orphans()
         ev("cleanup", completed=completed, trainer_returncode=trc, lighthouse_returncode=lrc, reaped=reaped,

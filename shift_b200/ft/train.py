@@ -74,6 +74,8 @@ def parse_args(argv=None):
     p.add_argument("--checkpoint-cold", action="store_true")
     p.add_argument("--resume-checkpoint", action="store_true")
     p.add_argument("--standby", choices=("cpu", "gpu"))
+    p.add_argument("--activate-marker", default="ACTIVATE",
+                   help="marker file (in the session directory) that releases a standby process")
     p.add_argument("--bucket-size", type=int, default=64 * 1024 * 1024)
     p.add_argument("--inject", default="", help="test fault: nonfinite@STEP | exit@STEP | slow@MS")
     p.add_argument("--mode", choices=["shift", "flat"], default="shift",
@@ -131,7 +133,7 @@ class Worker:
         self.event("standby_ready", mode=mode, cpu_maxrss_kib=resource.getrusage(resource.RUSAGE_SELF).ru_maxrss,
                    cuda_allocated_bytes=torch.cuda.memory_allocated() if self.device.type == "cuda" else 0)
         until = time.monotonic() + self.args.max_seconds
-        while not self.marker("ACTIVATE").exists():
+        while not self.marker(self.args.activate_marker).exists():
             if self.marker("STOP").exists() or time.monotonic() > until:
                 raise RuntimeError("standby stopped or timed out before activation")
             time.sleep(0.02)

@@ -145,10 +145,34 @@ def run_attn(iters, B=8, S=2048, Hq=16, Hkv=4, D=64):
     causal_flops = 4.0 * B * Hq * S * S * D / 2
     tf = timeit(lambda: Fn.attention_fwd(qkv, B, S, Hq, Hkv, D, scale), iters, warmup=_WARMUP)
     tb = timeit(lambda: Fn.attention_bwd(qkv, o, lse, do, B, S, Hq, Hkv, D, scale), iters, warmup=_WARMUP)
-    return [{"case": f"attn.fwd B{B} S{S} {Hq}q/{Hkv}kv d{D}", "ms": round(tf, 4),
+    rows = [{"case": f"attn.fwd B{B} S{S} {Hq}q/{Hkv}kv d{D}", "ms": round(tf, 4),
              "tflops": round(causal_flops / tf / 1e9, 1), "frac_of_peak": round(causal_flops / tf / 1e9 / pk["bf16_tflops"], 3)},
             {"case": "attn.bwd", "ms": round(tb, 4), "tflops": round(2.5 * causal_flops / tb / 1e9, 1),
              "frac_of_peak": round(2.5 * causal_flops / tb / 1e9 / pk["bf16_tflops"], 3)}]
+    # library yardstick on the same shapes: torch SDPA with each backend it has here
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+    q = qkv[:, :Hq * D].reshape(B, S, Hq, D).transpose(1, 2).contiguous().requires_grad_(True)
+    k = qkv[:, Hq * D:(Hq + Hkv) * D].reshape(B, S, Hkv, D).transpose(1, 2).contiguous().requires_grad_(True)
+    v = qkv[:, (Hq + Hkv) * D:].reshape(B, S, Hkv, D).transpose(1, 2).contiguous().requires_grad_(True)
+    g = do.reshape(B, S, Hq, D).transpose(1, 2).contiguous()
+    for name, be in (("cudnn", SDPBackend.CUDNN_ATTENTION), ("flash", SDPBackend.FLASH_ATTENTION),
+                     ("efficient", SDPBackend.EFFICIENT_ATTENTION)):
+        try:
+            with sdpa_kernel([be]):
+                f = lambda: torch.nn.functional.scaled_dot_product_attention(q, k, v, is_causal=True, scale=scale,
+                                                                             enable_gqa=True)
+                out = f()
+                lf = timeit(lambda: f().detach(), iters, warmup=_WARMUP)
+                lb = timeit(lambda: torch.autograd.grad(out, (q, k, v), g, retain_graph=True), iters,
+                            warmup=_WARMUP)
+        except Exception as e:  # a backend may not support these shapes / this GPU
+            rows.append({"case": f"sdpa.{name}", "unavailable": type(e).__name__ + ": " + str(e)[:120]})
+            continue
+        rows.append({"case": f"sdpa.{name}.fwd", "ms": round(lf, 4), "tflops": round(causal_flops / lf / 1e9, 1),
+                     "ours_vs_lib": round(lf / tf, 3)})
+        rows.append({"case": f"sdpa.{name}.bwd", "ms": round(lb, 4),
+                     "tflops": round(2.5 * causal_flops / lb / 1e9, 1), "ours_vs_lib": round(lb / tb, 3)})
+    return rows
 
 
 def run_mem(iters, T=16384, H=1024):

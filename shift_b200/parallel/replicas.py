@@ -16,7 +16,7 @@ import torch.distributed as dist
 from ..engine import Engine, synthetic_batch
 from ..graphs import StepGraphs, graphs_enabled
 from ..models.qwen_moe import MoEConfig
-from ..ops._ext import check_status
+from ..ops._ext import check_status, ext
 from .symmetric import CrossReplicaFused, SymmetricHeap, _tag
 
 
@@ -44,6 +44,7 @@ class ReplicaDPRunner:
         store = dist.distributed_c10d._get_default_store()
         self.heap = SymmetricHeap(store, f"r{rank}", self.device)
         self.fused = CrossReplicaFused(self.engine, self.heap)
+        self.fused.nccl_group = dist.group.WORLD       # the K1 baseline arm (SHIFT_K1=nccl) reduces over it
         dist.barrier()
         self.fused.configure([f"r{i}" for i in range(n_gpus)])
         layers = cfg.layers
@@ -55,6 +56,7 @@ class ReplicaDPRunner:
         self.graphs = StepGraphs(self.device, graphs_enabled())
         self.manager = None
         self.step_no = 0
+        self.eager_until = 2
         if with_manager:
             self._init_manager(store)
         dist.barrier()
@@ -85,7 +87,7 @@ class ReplicaDPRunner:
             self.manager.start_quorum()
         step = self.step_no
         self.engine.prepare_step(_tag(step))
-        if step < 2:      # eager warm-up steps; buffer-reuse waits start at step 2
+        if step < self.eager_until:      # eager warm-up steps; buffer-reuse waits start at step 2
             loss = self._device_step()
         else:
             loss = self.graphs.run((self.engine.store.cur, step % 2), self._device_step)
@@ -101,6 +103,24 @@ class ReplicaDPRunner:
         self.tokens.copy_(self.dev_batches[i % len(self.dev_batches)])
         return self._train()
 
+    def set_k1_mode(self, mode: str):
+        """Switch the cross-replica reduction between the fused peer-memory
+        kernels ("auto") and the NCCL baseline ("nccl"); the step graphs are
+        captured again after two eager steps."""
+        torch.cuda.synchronize()
+        self.graphs.reset()
+        self.fused.mode = mode
+        self.eager_until = self.step_no + 2
+
+    # ------------------------------------------------------------------ correctness checks
+    def initial_full_state(self) -> dict:
+        """Whole-model weights of this replica (call before training): every
+        replica starts from the same seeded initialisation."""
+        return {n: t.clone() for n, t in self.engine.store.model_state_dict().items()}
+
+    def state_fingerprints(self) -> dict:
+        return state_fingerprints(self.engine.store, replica=self.rank, position="dp")
+
     def step_e2e(self, i: int):
         self.tokens.copy_(self.host, non_blocking=True)
         loss = self._train()
@@ -115,6 +135,16 @@ class ReplicaDPRunner:
             self.manager.shutdown()
         dist.barrier()
         self.heap.close_peers()
+
+
+def state_fingerprints(store, replica: int, position: str) -> dict:
+    """64-bit fingerprints of this rank's committed flat state (bf16 params,
+    fp32 master, Adam moments): replicas of one position must agree bit for
+    bit after every committed step."""
+    fp = ext().fingerprint
+    c = store.cur
+    return {"replica": replica, "position": position, "param": fp(store.param[c]), "master": fp(store.master[c]),
+            "exp_avg": fp(store.exp_avg[c]), "exp_avg_sq": fp(store.exp_avg_sq[c]), "step": store.step}
 
 
 def make_parallel_runner(n_gpus: int, rank: int, local_rank: int, batch: int, seq: int, cfg: MoEConfig):

@@ -20,6 +20,8 @@ through the kernel status word.
 """
 from __future__ import annotations
 
+import os
+
 import torch
 
 from ..ops._ext import ext, status_word
@@ -74,7 +76,8 @@ def _tag(step: int) -> int:
 class CrossReplicaFused:
     """K1 for one rank: fused cross-replica gradient reduction + AdamW."""
 
-    def __init__(self, engine, heap: SymmetricHeap, timeout_s: float = 30.0, two_phase: bool = True):
+    def __init__(self, engine, heap: SymmetricHeap, timeout_s: float = 30.0, two_phase: bool = True,
+                 mode: str | None = None):
         self.engine = engine
         self.heap = heap
         self.timeout = timeout_s
@@ -85,8 +88,18 @@ class CrossReplicaFused:
         self.nb = len(st.buckets)
         # flags: ready[nb] | done[2] | slice[nb]
         self.flags = heap.alloc("flags", 4 * (2 * self.nb + 2) + 64).view(torch.int32)
+        # K1 form per segment: "auto" reads every source directly and sums in
+        # fp32 when a segment has at most two sources (one peer: the same NVLink
+        # bytes per direction as reduce-scatter + all-gather, and no bf16
+        # rounding of the sum), and uses the two-phase slice form above that;
+        # "one" / "two" force a form; "nccl" is the baseline: NCCL all_reduce
+        # of each bucket on the side stream, then the local fused AdamW.
+        self.mode = mode or os.environ.get("SHIFT_K1", "auto")
+        if self.mode not in ("auto", "one", "two", "nccl"):
+            raise ValueError(f"SHIFT_K1={self.mode!r}: expected auto, one, two or nccl")
+        self.nccl_group = None
         # reduced gradient written by every member's slice (two-phase K1)
-        self.two_phase = two_phase
+        self.two_phase = two_phase and self.mode != "one"
         if two_phase:
             self.red = heap.alloc("red", nbytes).view(torch.bfloat16)[: self.numel]
         st.set_grad_buffers(self.gbuf)
@@ -191,14 +204,16 @@ class CrossReplicaFused:
             self.side.wait_event(ev)
             c, n = st.cur, st.nxt
             o = self.engine.optim
-            if self.two_phase:
-                self._two_phase(b, bk, par, tag, c, n, o)
+            if self.mode == "nccl":
+                self._nccl(b, bk, c, n, o)
                 self.launched.add(b)
                 return
+            if self.two_phase:
+                self._two_phase(b, bk, par, tag, c, n, o)
             for seg in self.segments:
                 lo, hi, srcs, scale = seg[:4]
                 s0, s1 = max(bk.start, lo), min(bk.end, hi)
-                if s0 >= s1:
+                if s0 >= s1 or self._sliced(srcs):
                     continue
                 sl = slice(s0, s1)
                 grad_ptrs = [self.grad_maps[w][par][sl].data_ptr() for w in srcs]
@@ -208,6 +223,25 @@ class CrossReplicaFused:
                                          st.exp_avg_sq[n][sl], st.param[n][sl], o.beta1, o.beta2, o.eps,
                                          o.weight_decay, scale, self.engine.nonfinite, self.status, self.timeout)
         self.launched.add(b)
+
+    def _sliced(self, srcs) -> bool:
+        """Whether a segment with these sources takes the two-phase form."""
+        return self.two_phase and (self.mode == "two" or len(srcs) > 2)
+
+    def _nccl(self, b, bk, c, n, o):
+        """Baseline K1: NCCL all_reduce (sum) of the bucket's bf16 gradient over
+        the replicas, then AdamW with the 1/R scale from the local buffer."""
+        import torch.distributed as dist
+        st = self.engine.store
+        if self.nccl_group is None:
+            raise RuntimeError("SHIFT_K1=nccl needs nccl_group (the replicas' process group)")
+        sl = slice(bk.start, bk.end)
+        g = st.grad[sl]
+        dist.all_reduce(g, group=self.nccl_group)
+        ext().fused_reduce_adamw([g.data_ptr()], [], self.sdev, st.master[c][sl], st.exp_avg[c][sl],
+                                 st.exp_avg_sq[c][sl], st.master[n][sl], st.exp_avg[n][sl], st.exp_avg_sq[n][sl],
+                                 st.param[n][sl], o.beta1, o.beta2, o.eps, o.weight_decay, self.scale,
+                                 self.engine.nonfinite, self.status, self.timeout)
 
     def _two_phase(self, b, bk, par, tag, c, n, o):
         """Phase A: reduce this rank's slice of every segment and store it into
@@ -223,7 +257,7 @@ class CrossReplicaFused:
             # quorum, members that do not contribute (healing / spare)
             members = seg[4] if len(seg) > 4 else list(srcs)
             s0, s1 = max(bk.start, lo), min(bk.end, hi)
-            if s0 >= s1:
+            if s0 >= s1 or not self._sliced(srcs):
                 continue
             parts.append((s0, s1, srcs))
             if me not in srcs:
@@ -234,6 +268,8 @@ class CrossReplicaFused:
                                        [self.red_maps[w].data_ptr() for w in members], cuts[k], cuts[k + 1],
                                        [self.flag_maps[w][b].data_ptr() for w in srcs if w != me], self.sdev,
                                        scale, self.status, self.timeout)
+        if not parts:
+            return
         ext().flag_set(self.flags[slice_flag].data_ptr(), self.sdev, 0)
         for s0, s1, srcs in parts:
             sl = slice(s0, s1)

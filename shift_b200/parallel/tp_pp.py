@@ -13,7 +13,6 @@ over replicas inside the same kernel.
 from __future__ import annotations
 
 import os
-import zlib
 
 import torch
 import torch.distributed as dist
@@ -22,8 +21,10 @@ from ..engine import Engine, synthetic_batch
 from ..models.qwen_moe import TP_SHARDED, MoEConfig, Partition, param_specs
 from ..ops._ext import check_status
 from ..graphs import StepGraphs, graphs_enabled
-from .replicas import _order
+from .replicas import _order, state_fingerprints
 from .symmetric import CrossReplicaFused, SymmetricHeap, _tag
+from .assemble import initial_model_parallel_weights, shard_seed
+from .pipe import ACT, GRAD, PipeNccl, PipePeer
 from .tp import TPComm, TPPeer
 
 
@@ -33,11 +34,12 @@ def _is_sharded(name: str) -> bool:
 
 class ModelParallelRunner:
     def __init__(self, cfg: MoEConfig, n_gpus: int, rank: int, local_rank: int, batch: int, seq: int,
-                 replicas: int, tp: int, pp: int, microbatch: int | None = None, tp_backend: str | None = None):
+                 replicas: int, tp: int, pp: int, microbatch: int | None = None, tp_backend: str | None = None,
+                 pp_backend: str | None = None, with_manager: bool | None = None):
         if microbatch is None:
-            # one microbatch per replica without pipelining; with it, two sequences per
-            # microbatch (measured on 4 B200, TP2 x PP2: 38.3 ms per step vs 57.4 ms with one)
-            microbatch = batch // replicas if pp == 1 else max(1, min(2, batch // replicas // pp))
+            # one microbatch per replica without pipelining; with it, one sequence per
+            # microbatch (four microbatches per replica: a 1F1B bubble of 1/5 instead of 1/3)
+            microbatch = batch // replicas if pp == 1 else 1
         if replicas * tp * pp != n_gpus:
             raise ValueError(f"{replicas} x tp{tp} x pp{pp} != {n_gpus} GPUs")
         if batch % (replicas * microbatch):
@@ -80,8 +82,7 @@ class ModelParallelRunner:
         t_rank = self.t
 
         def seed_of(spec):
-            salt = f"/tp{t_rank}" if _is_sharded(spec.name) else ""
-            return 2026 + zlib.crc32((spec.name + salt).encode())
+            return shard_seed(spec.name, t_rank)
 
         store = dist.distributed_c10d._get_default_store()
         self.heap = SymmetricHeap(store, f"r{self.r}s{self.s}t{self.t}", self.device)
@@ -100,6 +101,8 @@ class ModelParallelRunner:
         self.rep_end = st.offsets[shard[0].name][0] if shard else st.numel
         # ---- fused cross-replica (and cross-TP for replicated params) reduction ----
         self.fused = CrossReplicaFused(self.engine, self.heap)
+        if self.fused.mode == "nccl":
+            raise ValueError("the NCCL K1 baseline (SHIFT_K1=nccl) is wired for the replicas x 1 GPU layout only")
         dist.barrier()
         if isinstance(self.comm, TPPeer):
             self.comm.connect(self.engine.step_block.dev)
@@ -116,29 +119,50 @@ class ModelParallelRunner:
         self.dev_batches = [synthetic_batch(cfg, i, batch, seq)[sl].to(self.device) for i in range(2)]
         self.host = synthetic_batch(cfg, 10_000, batch, seq)[sl].contiguous().pin_memory()
         self.tokens = torch.empty_like(self.dev_batches[0])      # static step input (graph replay)
-        use_graphs = graphs_enabled() and (pp == 1 or os.environ.get("SHIFT_PP_GRAPHS") == "1")
+        use_graphs = graphs_enabled()
         if self.tp_backend == "nccl" and tp > 1:
             use_graphs = use_graphs and os.environ.get("SHIFT_PP_GRAPHS") == "1"
+        self.tok_loc = self.mb * seq // tp
+        # ---- pipeline send/recv: peer memory (default) or the NCCL baseline ----
+        self.pipe = None
+        if pp > 1:
+            self.pp_backend = pp_backend or os.environ.get("SHIFT_PP_BACKEND", "peer")
+            act_shape, grad_shape = (2, self.tok_loc, cfg.hidden), (self.tok_loc, cfg.hidden)
+            if self.pp_backend == "peer":
+                self.pipe = PipePeer(self.heap, [f"r{self.r}s{q}t{self.t}" for q in range(pp)], self.s, act_shape,
+                                     grad_shape, self.M, self.device, self.engine.step_block.dev)
+            else:
+                self.pp_backend = "nccl"
+                self.pipe = PipeNccl(self.pp_group, self.pp_ranks, self.s, act_shape, grad_shape, self.M,
+                                     self.device)
+            self.layout += f", PP send/recv over {'peer memory' if self.pp_backend == 'peer' else 'NCCL'}"
+            use_graphs = graphs_enabled() and (self.pipe.graphable or os.environ.get("SHIFT_PP_GRAPHS") == "1")
+            if self.tp_backend == "nccl" and tp > 1:
+                use_graphs = use_graphs and os.environ.get("SHIFT_PP_GRAPHS") == "1"
         self.graphs = StepGraphs(self.device, use_graphs)
         self.step_no = 0
-        self.tok_loc = self.mb * seq // tp
+        dist.barrier()
+        if isinstance(self.pipe, PipePeer):
+            self.pipe.connect()
+        # ---- fault tolerance: quorum + commit vote of every replica every step ----
+        self.manager = None
+        if with_manager is None:
+            with_manager = os.environ.get("SHIFT_BENCH_FT", "1") == "1"
+        if with_manager and replicas > 1:
+            self._init_manager(store, per)
         dist.barrier()
 
-    # ------------------------------------------------------------------ pipeline p2p
-    def _p2p(self, send=None, send_to=None, recv_from=None):
-        ops, buf = [], None
-        if send is not None:
-            ops.append(dist.P2POp(dist.isend, send.contiguous(), self.pp_ranks[send_to], group=self.pp_group))
-        if recv_from is not None:
-            buf = torch.empty(self._act_shape(), dtype=torch.bfloat16, device=self.device)
-            ops.append(dist.P2POp(dist.irecv, buf, self.pp_ranks[recv_from], group=self.pp_group))
-        if ops:
-            for w in dist.batch_isend_irecv(ops):
-                w.wait()
-        return buf
-
-    def _act_shape(self):
-        return (2, self.tok_loc, self.cfg.hidden)
+    def _init_manager(self, store, per):
+        from ..ft.manager import Manager
+        from ..ft.native import LighthouseServer
+        if self.rank == 0:
+            self._lh = LighthouseServer("127.0.0.1:0", min_replicas=self.R, join_timeout_ms=500,
+                                        heartbeat_timeout_ms=2000, quorum_tick_ms=20)
+            store.set("bench/lighthouse", self._lh.address)
+        addr = store.get("bench/lighthouse").decode()
+        # one manager per rank; the replica's rank 0 serves its ranks' quorum and commit votes
+        self.manager = Manager(None, None, None, self.R, f"shift{self.r}", addr, rank=self.s * self.TP + self.t,
+                               world_size=per, store=store, local_prefix=f"/bench{self.r}")
 
     # ------------------------------------------------------------------ one step (1F1B)
     def _slot(self, i):
@@ -162,15 +186,17 @@ class ModelParallelRunner:
         model = self.engine.model
         model._accumulate = i > 0
         model.layer_done_hook = self._hook if i == self.M - 1 else None
-        d = model.backward(None if dout is None else dout[0])
+        d = model.backward(dout)        # the same gradient reaches both halves of the stage input pair
         model.layer_done_hook = None
-        return None if d is None else torch.stack([d, d])
+        return d
 
     def _train(self, data):
         """One step.  Without pipelining (no NCCL on the step's path when the
         TP pair runs over peer memory) the step is captured as a CUDA graph per
         (state generation, step parity) after two eager steps; with pipelining
         it runs eagerly unless SHIFT_PP_GRAPHS=1 (NCCL p2p inside the graph)."""
+        if self.manager is not None:
+            self.manager.start_quorum()
         step = self.step_no
         self.engine.prepare_step(_tag(step))
         if data is not self.tokens:
@@ -179,7 +205,11 @@ class ModelParallelRunner:
             loss = self._device_step()
         else:
             loss = self.graphs.run((self.engine.store.cur, step % 2), self._device_step)
-        self.engine.commit()
+        commit = True
+        if self.manager is not None:
+            commit = self.manager.should_commit()
+        if commit:
+            self.engine.commit()
         self.step_no += 1
         return loss
 
@@ -192,34 +222,46 @@ class ModelParallelRunner:
         self._loss = None
         M, s, pp = self.M, self.s, self.PP
         first, last = s == 0, s == pp - 1
+        pipe = self.pipe
+        if pipe is not None:
+            pipe.set_parity(self.step_no % 2)
         n_warm = min(pp - s - 1, M)
         n_rem = M - n_warm
         for i in range(n_warm):
-            x = None if first else self._p2p(recv_from=s - 1)
+            x = None if first else pipe.exchange(recv=(ACT, i))
             y = self._fwd(i, data, x)
-            self._p2p(send=y, send_to=s + 1)
-        x = None if (first or n_rem == 0) else self._p2p(recv_from=s - 1)
+            pipe.exchange(send=(ACT, i, y))
+        x = None if (first or n_rem == 0) else pipe.exchange(recv=(ACT, n_warm))
         for j in range(n_rem):
             i = n_warm + j
             y = self._fwd(i, data, x)
-            dy = None if last else self._p2p(send=y, send_to=s + 1, recv_from=s + 1)
+            dy = None if last else pipe.exchange(send=(ACT, i, y), recv=(GRAD, j))
             dx = self._bwd(j, dy)
             if j == n_rem - 1:
                 if not first:
-                    self._p2p(send=dx, send_to=s - 1)
+                    pipe.exchange(send=(GRAD, j, dx))
             else:
-                x = None if first else self._p2p(send=dx, send_to=s - 1, recv_from=s - 1)
+                x = None if first else pipe.exchange(send=(GRAD, j, dx), recv=(ACT, i + 1))
         for j in range(n_rem, M):
-            dy = None if last else self._p2p(recv_from=s + 1)
+            dy = None if last else pipe.exchange(recv=(GRAD, j))
             dx = self._bwd(j, dy)
             if not first:
-                self._p2p(send=dx, send_to=s - 1)
+                pipe.exchange(send=(GRAD, j, dx))
         eng.model._accumulate = False
         self.fused.finish_step()
         return self._loss if self._loss is not None else torch.zeros((), device=self.device)
 
     def step(self, i: int):
         return self._train(self.dev_batches[i % len(self.dev_batches)])
+
+    # ------------------------------------------------------------------ correctness checks
+    def initial_full_state(self) -> dict:
+        """Whole-model initial weights of a replica, rebuilt on the host from
+        the per-shard seeds (no shard moves)."""
+        return initial_model_parallel_weights(self.cfg, self.TP, self.PP)
+
+    def state_fingerprints(self) -> dict:
+        return state_fingerprints(self.engine.store, replica=self.r, position=f"s{self.s}t{self.t}")
 
     def step_e2e(self, i: int):
         loss = self._train(self.host)
@@ -230,16 +272,19 @@ class ModelParallelRunner:
         torch.cuda.synchronize()
         self.graphs.reset()
         check_status(self.device)
+        if self.manager is not None:
+            self.manager.shutdown()
         dist.barrier()
         self.heap.close_peers()
 
 
 def make_model_parallel_runner(layout: str, cfg, n_gpus, rank, local_rank, batch, seq):
-    """layout: 'tp' (replicas x TP2) or 'tppp' (replicas x TP2 x PP2) or 'auto'."""
+    """layout: 'tp' (replicas x TP2), 'tppp' (replicas x TP2 x PP2), 'pp'
+    (replicas x PP2, no tensor parallelism) or 'auto'."""
     if layout == "auto":
         layout = {4: "tp", 8: "tppp"}.get(n_gpus, "tp")
-    tp = 2
-    pp = 2 if layout == "tppp" else 1
+    tp = 1 if layout == "pp" else 2
+    pp = 2 if layout in ("tppp", "pp") else 1
     replicas = n_gpus // (tp * pp)
     mb = os.environ.get("SHIFT_MICROBATCH")      # sequences per pipeline microbatch
     return ModelParallelRunner(cfg, n_gpus, rank, local_rank, batch, seq, replicas, tp, pp,

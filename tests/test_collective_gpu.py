@@ -95,7 +95,7 @@ def _free_port():
     return p
 
 
-def _k1_worker(rank, world, port, q):
+def _k1_worker(rank, world, port, q, mode):
     import torch.distributed as dist
     from datetime import timedelta
 
@@ -113,7 +113,7 @@ def _k1_worker(rank, world, port, q):
         B, S = 2, 128
         eng = Engine(cfg, dev, bucket_numel=1 << 18)
         heap = SymmetricHeap(dist.distributed_c10d._get_default_store(), f"r{rank}", dev)
-        fused = CrossReplicaFused(eng, heap, timeout_s=20)
+        fused = CrossReplicaFused(eng, heap, timeout_s=20, mode=mode)
         dist.barrier()
         fused.configure([f"r{i}" for i in range(world)])
         eng.model.layer_done_hook = lambda layer: fused.on_layer_done(_order(layer, cfg.layers))
@@ -137,9 +137,13 @@ def _k1_worker(rank, world, port, q):
                     data = synthetic_batch(cfg, 100 * step + src, B, S).to(dev)
                     r.forward_backward([(data[:, :-1], data[:, 1:])], B, S)
                     gl.append(r.store.grad.clone())
-                # the two-phase reduction averages in fp32 and rounds to bf16 before AdamW
-                avg = ((gl[0].float() + gl[1].float()) * (1.0 / world)).to(torch.bfloat16)
-                r.optimizer_step([avg], 1.0)
+                if mode == "two":
+                    # the two-phase reduction averages in fp32 and rounds to bf16 before AdamW
+                    avg = ((gl[0].float() + gl[1].float()) * (1.0 / world)).to(torch.bfloat16)
+                    r.optimizer_step([avg], 1.0)
+                else:
+                    # one-phase: both bf16 gradients summed in fp32 inside the AdamW kernel, no rounding
+                    r.optimizer_step([gl[0], gl[1]], 1.0 / world)
                 r.commit()
                 grads.append(gl)
             q.put(("ref", r.store.state_tensors()["master"].cpu()))
@@ -151,12 +155,13 @@ def _k1_worker(rank, world, port, q):
 
 
 @pytest.mark.multigpu
-def test_fused_cross_replica_two_gpus_bit_identical_and_matches_reference():
+@pytest.mark.parametrize("mode", ["auto", "two"])
+def test_fused_cross_replica_two_gpus_bit_identical_and_matches_reference(mode):
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_k1_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_k1_worker, args=(r, world, port, q, mode)) for r in range(world)]
     for p in procs:
         p.start()
     got = {}

@@ -67,7 +67,7 @@ def free_block(size: int = 64) -> int:
 
 class PlannedSession:
     def __init__(self, root, name, variant="p1f", scenario="healthy", model="tiny", device="cpu", nproc=1,
-                 audit=True, train_args=None, devices=None, seconds=600):
+                 audit=True, train_args=None, devices=None, seconds=600, module="shift_b200.ft.planned_train"):
         self.dir = Path(root) / name
         self.dir.mkdir(parents=True, exist_ok=True)
         self.root, self.name = Path(root), name
@@ -75,6 +75,7 @@ class PlannedSession:
         self.model, self.device, self.nproc = model, device, nproc
         self.devices = devices or {}
         self.seconds = seconds
+        self.module = module
         self.log = EventLog(self.dir / "controller.jsonl", role="controller")
         self.reader = IncrementalReader(self.dir)
         base = free_block(200)
@@ -138,7 +139,7 @@ class PlannedSession:
         env["SHIFT_STORE_PORT"] = str(self.store_base + 20 * {"A": 0, "B": 1, "C": 2}[name])
         env.setdefault("NCCL_NVLS_ENABLE", "0")
         cmd = [sys.executable, "-m", "shift_b200.control.launch", "--nproc", str(self.nproc), "--master-port",
-               str(self.master_base + 10 * {"A": 0, "B": 1, "C": 2}[name]), "--module", "shift_b200.ft.planned_train"]
+               str(self.master_base + 10 * {"A": 0, "B": 1, "C": 2}[name]), "--module", self.module]
         if name in self.devices:
             cmd += ["--devices", ",".join(str(d) for d in self.devices[name])]
         cmd += ["--", "--session", self.name, "--replica", str(rid), "--generation", str(gen), "--root",

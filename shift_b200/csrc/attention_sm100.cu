@@ -85,11 +85,22 @@ SB_DEVICE uint64_t mndesc(uint32_t addr) { return make_sw128_desc(addr, 8192, 10
 SB_DEVICE void named_bar(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
 
 // ============================ forward ============================
+// The forward's softmax is issue-bound (exp2, FMA, conversion and stores per
+// score), so it runs four warps per TMEM lane quarter: warp 2 + 4k + q' reads
+// lanes of quarter (warp % 4) and columns [32k, 32k + 32) of each S tile and
+// folds columns [16k, 16k + 16) of O -- 16 softmax warps and half the
+// registers per thread of a two-warp split, so more warps hide the latency of
+// each other's TMEM loads, exponentials and barriers.
 constexpr int kFwdStages = 2;
+constexpr int kFwdSplit = 4;                          // softmax warps per lane quarter
+constexpr int kFwdSoft = 128 * kFwdSplit;             // softmax threads
+constexpr int kFwdThreads = 64 + kFwdSoft;
+constexpr int kFwdCols = BN / kFwdSplit;              // S columns per softmax warp
+constexpr int kFwdOCols = D / kFwdSplit;              // O columns per softmax warp
 constexpr int kFwdSmem = 1024 + kTile /*Q*/ + 2 * kFwdStages * kTile /*K,V*/ + 2 * 2 * kTile /*P x2*/ + 256 +
-                         (2 * 2 * 128 + 2 * 128) * 4 /*row max / sum exchange*/;
+                         (2 * kFwdSplit * 128 + kFwdSplit * 128) * 4 /*row max / sum exchange*/;
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kFwdThreads, 1)
 fwd_kernel(const __grid_constant__ CUtensorMap tm, Params p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -107,12 +118,13 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm, Params p) {
   uint64_t* o_full = p_full + 2;
   uint64_t* drain = o_full + 2;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(drain + 1);
-  // row-max exchange between the two softmax warps of a lane quarter,
-  // double-buffered by block parity: [parity][half][row]; then the row sums
+  // row-max exchange between the softmax warps of a lane quarter,
+  // double-buffered by block parity: [parity][part][row]; then the row sums
   float* s_max = reinterpret_cast<float*>(tslot + 4);
-  float* s_sum = s_max + 2 * 2 * BM;
+  float* s_sum = s_max + 2 * kFwdSplit * BM;
 
-  const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  // longest rows of the causal triangle first (they bound the tail of the grid)
+  const int qb = static_cast<int>(gridDim.x) - 1 - static_cast<int>(blockIdx.x), h = blockIdx.y, b = blockIdx.z;
   const int kvh = h / (p.Hq / p.Hkv);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int q0 = qb * BM;
@@ -127,7 +139,7 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm, Params p) {
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], kSoftThreads);
+      mbar_init(&p_full[i], kFwdSoft);
       mbar_init(&o_full[i], 1);
     }
     mbar_init(drain, 1);
@@ -192,65 +204,66 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm, Params p) {
     }
   } else {
     // ----------------------------- softmax -----------------------------
-    const int quarter = warp % 4;
-    const int half = (warp - 2) / 4;          // columns [64*half, 64*half+64) of S, [32*half, +32) of O
+    const int quarter = warp % 4;             // TMEM lane quarter this warp may access
+    const int part = (warp - 2) / 4;          // columns [32*part, +32) of S, [16*part, +16) of O
     const int row = quarter * 32 + lane;
     const int q = q0 + row;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    const int pair_bar = 1 + quarter;         // named barrier of the two warps of this quarter
+    const int quad_bar = 1 + quarter;         // named barrier of the four warps of this quarter
     float m_run = -INFINITY, l_run = 0.f, m_fold = -INFINITY;
-    float o_acc[D / 2];
+    float o_acc[kFwdOCols];
 #pragma unroll
-    for (int i = 0; i < D / 2; ++i) o_acc[i] = 0.f;
+    for (int i = 0; i < kFwdOCols; ++i) o_acc[i] = 0.f;
     bool ok = true;
     auto fold = [&](int i, float m_i) -> bool {
       if (!mbar_wait(&o_full[i & 1], (i >> 1) & 1, p.status)) return false;
       tc_fence_after();
       const float a = (m_fold == -INFINITY) ? 0.f : ex2(m_fold - m_i);
-      uint32_t v[32];
-      tmem_ld_32x32b_x32(tbase + 256 + (i & 1) * D + half * 32 + lane_off, v);
+      uint32_t v[kFwdOCols];
+      tmem_ld_32x32b_x16(tbase + 256 + (i & 1) * D + part * kFwdOCols + lane_off, v);
       tmem_wait_ld();
 #pragma unroll
-      for (int t = 0; t < 32; ++t) o_acc[t] = o_acc[t] * a + __uint_as_float(v[t]);
+      for (int t = 0; t < kFwdOCols; ++t) o_acc[t] = o_acc[t] * a + __uint_as_float(v[t]);
       m_fold = m_i;
       return true;
     };
-    // Both warps of a pair run every iteration's named barrier even after a
+    // All warps of a quarter run every iteration's named barrier even after a
     // bounded wait failed (they then skip the work), so a failure in one warp
-    // can never leave its partner blocked on the barrier.
+    // can never leave its partners blocked on the barrier.
     for (int j = 0; j < n_kv; ++j) {
       if (ok && !mbar_wait(&s_full[j & 1], (j >> 1) & 1, p.status)) ok = false;
       if (ok) tc_fence_after();
       const uint32_t ts = tbase + (j & 1) * BN + lane_off;
       const bool diag = (j == qb);
-      // pass 1: this warp's 64 columns of S come out of TMEM once (two loads,
-      // one wait) and stay in registers for pass 2.  Row max over them (the
-      // causal mask only exists on the diagonal tile) in four independent
-      // chains, scaled once, then combined with the partner warp's.
-      uint32_t v[64];
+      // pass 1: this warp's 32 columns of S come out of TMEM once and stay in
+      // registers for pass 2; row max over them (the causal mask only exists
+      // on the diagonal tile) in four independent chains, then combined with
+      // the other three warps' through shared memory.
+      uint32_t v[kFwdCols];
       float mraw = -INFINITY;
-      const int c_lo = half * 64;
+      const int c_lo = part * kFwdCols;
       if (ok) {
         tmem_ld_32x32b_x32(ts + c_lo, v);
-        tmem_ld_32x32b_x32(ts + c_lo + 32, v + 32);
         tmem_wait_ld();
         float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
         if (diag) {
           const int lim = q - j * BN - c_lo;       // columns t <= lim are visible
 #pragma unroll
-          for (int t = 0; t < 64; ++t)
+          for (int t = 0; t < kFwdCols; ++t)
             if (t <= lim) m4[t & 3] = fmaxf(m4[t & 3], __uint_as_float(v[t]));
         } else {
 #pragma unroll
-          for (int t = 0; t < 64; ++t) m4[t & 3] = fmaxf(m4[t & 3], __uint_as_float(v[t]));
+          for (int t = 0; t < kFwdCols; ++t) m4[t & 3] = fmaxf(m4[t & 3], __uint_as_float(v[t]));
         }
         mraw = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
       }
       float mx = fmaxf(m_run, mraw * p.scale_log2);
-      s_max[((j & 1) * 2 + half) * BM + row] = mx;
-      named_bar(pair_bar, 64);
+      float* xm = s_max + (j & 1) * kFwdSplit * BM;
+      xm[part * BM + row] = mx;
+      named_bar(quad_bar, 128);
       if (!ok) continue;
-      mx = fmaxf(mx, s_max[((j & 1) * 2 + (half ^ 1)) * BM + row]);
+#pragma unroll
+      for (int o = 1; o < kFwdSplit; ++o) mx = fmaxf(mx, xm[((part + o) % kFwdSplit) * BM + row]);
       const float m_prev = m_run;
       m_run = mx;
       // pass 2: probabilities -> shared memory (bf16, swizzled); the row sum
@@ -258,29 +271,25 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm, Params p) {
       uint8_t* pbuf = sP + (j & 1) * 2 * kTile;
       const float nmx = -mx;
       float l4[4] = {0.f, 0.f, 0.f, 0.f};
+      float pr[kFwdCols];
+      if (diag) {
+        const int lim = q - j * BN - c_lo;
 #pragma unroll
-      for (int cc = 0; cc < 2; ++cc) {
-        float pr[32];
-        if (diag) {
-          const int lim = q - j * BN - c_lo - cc * 32;
-#pragma unroll
-          for (int t = 0; t < 32; ++t) {
-            pr[t] = (t > lim) ? 0.f : ex2(fmaf(__uint_as_float(v[cc * 32 + t]), p.scale_log2, nmx));
-            l4[t & 3] += pr[t];
-          }
-        } else {
-#pragma unroll
-          for (int t = 0; t < 32; ++t) {
-            pr[t] = ex2(fmaf(__uint_as_float(v[cc * 32 + t]), p.scale_log2, nmx));
-            l4[t & 3] += pr[t];
-          }
+        for (int t = 0; t < kFwdCols; ++t) {
+          pr[t] = (t > lim) ? 0.f : ex2(fmaf(__uint_as_float(v[t]), p.scale_log2, nmx));
+          l4[t & 3] += pr[t];
         }
+      } else {
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          bf16x8 pk = float_to_bf16x8(pr + 8 * u);
-          *reinterpret_cast<uint4*>(swz_chunk(pbuf, row, ((c_lo + cc * 32) >> 3) + u)) =
-              make_uint4(pk.w[0], pk.w[1], pk.w[2], pk.w[3]);
+        for (int t = 0; t < kFwdCols; ++t) {
+          pr[t] = ex2(fmaf(__uint_as_float(v[t]), p.scale_log2, nmx));
+          l4[t & 3] += pr[t];
         }
+      }
+#pragma unroll
+      for (int u = 0; u < kFwdCols / 8; ++u) {
+        bf16x8 pk = float_to_bf16x8(pr + 8 * u);
+        *reinterpret_cast<uint4*>(swz_chunk(pbuf, row, (c_lo >> 3) + u)) = make_uint4(pk.w[0], pk.w[1], pk.w[2], pk.w[3]);
       }
       l_run = ((m_prev == -INFINITY) ? 0.f : l_run * ex2(m_prev - mx)) + ((l4[0] + l4[1]) + (l4[2] + l4[3]));
       fence_proxy_async_smem();
@@ -289,21 +298,22 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm, Params p) {
       if (j >= 1 && !fold(j - 1, m_prev)) ok = false;
     }
     if (ok) ok = fold(n_kv - 1, m_run);
-    // row sum = both halves' partial sums (same running max)
-    s_sum[half * BM + row] = l_run;
-    named_bar(pair_bar, 64);
-    l_run += s_sum[(half ^ 1) * BM + row];
+    // row sum = the four parts' partial sums (same running max)
+    s_sum[part * BM + row] = l_run;
+    named_bar(quad_bar, 128);
+#pragma unroll
+    for (int o = 1; o < kFwdSplit; ++o) l_run += s_sum[((part + o) % kFwdSplit) * BM + row];
     if (ok) {
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-      __nv_bfloat16* orow = p.o + static_cast<long>(tok0 + q) * p.o_stride + h * D + half * 32;
+      __nv_bfloat16* orow = p.o + static_cast<long>(tok0 + q) * p.o_stride + h * D + part * kFwdOCols;
 #pragma unroll
-      for (int c = 0; c < D / 2; c += 8) {
+      for (int c = 0; c < kFwdOCols; c += 8) {
         float t8[8];
 #pragma unroll
         for (int t = 0; t < 8; ++t) t8[t] = o_acc[c + t] * inv;
         *reinterpret_cast<bf16x8*>(orow + c) = float_to_bf16x8(t8);
       }
-      if (half == 0) p.lse[(static_cast<long>(b) * p.Hq + h) * p.S + q] = m_run + log2f(l_run);
+      if (part == 0) p.lse[(static_cast<long>(b) * p.Hq + h) * p.S + q] = m_run + log2f(l_run);
     }
   }
   tc_fence_before();
@@ -898,7 +908,7 @@ std::vector<at::Tensor> fwd(const at::Tensor& qkv, int64_t B, int64_t S, int64_t
     cfg = true;
   }
   dim3 grid(static_cast<unsigned>(S / BM), static_cast<unsigned>(Hq), static_cast<unsigned>(B));
-  fwd_kernel<<<grid, kThreads, kFwdSmem, at::cuda::getCurrentCUDAStream()>>>(tm, p);
+  fwd_kernel<<<grid, kFwdThreads, kFwdSmem, at::cuda::getCurrentCUDAStream()>>>(tm, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return {o, lse};
 }

@@ -64,11 +64,11 @@ void fused_reduce_adamw(const std::vector<int64_t>& grad_ptrs, const std::vector
                         const at::Tensor& step_dev, const at::Tensor& master, const at::Tensor& m, const at::Tensor& v,
                         at::Tensor& master_out, at::Tensor& m_out, at::Tensor& v_out, at::Tensor& param_out,
                         double beta1, double beta2, double eps, double wd, double grad_scale,
-                        const at::Tensor& nonfinite, const at::Tensor& status, double timeout_s);
+                        const at::Tensor& nonfinite, const at::Tensor& status, double timeout_s, int64_t blocks_per_sm);
 void flag_set(int64_t flag_ptr, const at::Tensor& step_dev, int64_t delta);
 void reduce_slice_scatter(const std::vector<int64_t>& src_ptrs, const std::vector<int64_t>& dst_ptrs, int64_t lo,
                           int64_t hi, const std::vector<int64_t>& flag_ptrs, const at::Tensor& step_dev,
-                          double scale, const at::Tensor& status, double timeout_s);
+                          double scale, const at::Tensor& status, double timeout_s, int64_t blocks_per_sm);
 void flag_wait(const std::vector<int64_t>& flag_ptrs, const at::Tensor& step_dev, int64_t delta,
                const at::Tensor& status, double timeout_s);
 void peer_copy(int64_t src_ptr, int64_t dst_ptr, int64_t nbytes);

@@ -347,7 +347,8 @@ void fused_reduce_adamw(const std::vector<int64_t>& grad_ptrs, const std::vector
                         const at::Tensor& step_dev, const at::Tensor& master, const at::Tensor& m, const at::Tensor& v,
                         at::Tensor& master_out, at::Tensor& m_out, at::Tensor& v_out, at::Tensor& param_out,
                         double beta1, double beta2, double eps, double wd, double grad_scale,
-                        const at::Tensor& nonfinite, const at::Tensor& status, double timeout_s) {
+                        const at::Tensor& nonfinite, const at::Tensor& status, double timeout_s,
+                        int64_t blocks_per_sm) {
   check_step_dev(step_dev, master);
   TORCH_CHECK(!grad_ptrs.empty() && grad_ptrs.size() <= static_cast<size_t>(kMaxSrc), "1..8 gradient sources");
   const at::cuda::CUDAGuard guard(master.device());
@@ -365,7 +366,12 @@ void fused_reduce_adamw(const std::vector<int64_t>& grad_ptrs, const std::vector
   a.grad_scale = static_cast<float>(grad_scale);
   const long n = master.numel();
   if (n == 0) return;
-  const long blocks = std::min<long>((n / 8 + 255) / 256 + 1, static_cast<long>(sm_count()) * 8);
+  // blocks_per_sm <= 0: the whole GPU (8 per SM, grid-stride).  A small value
+  // (1) leaves room on every SM for the compute kernels the reduction runs
+  // beside during backward: its blocks co-reside with them instead of
+  // holding every SM until the bucket is done.
+  const long per_sm = blocks_per_sm > 0 ? blocks_per_sm : 8;
+  const long blocks = std::min<long>((n / 8 + 255) / 256 + 1, static_cast<long>(sm_count()) * per_sm);
   const int ns = static_cast<int>(grad_ptrs.size());
 #define SB_K1(NS)                                                                                              \
   fused_reduce_adamw_kernel<NS><<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(                          \
@@ -385,7 +391,7 @@ void fused_reduce_adamw(const std::vector<int64_t>& grad_ptrs, const std::vector
 // element offsets relative to the given base pointers.
 void reduce_slice_scatter(const std::vector<int64_t>& src_ptrs, const std::vector<int64_t>& dst_ptrs, int64_t lo,
                           int64_t hi, const std::vector<int64_t>& flag_ptrs, const at::Tensor& step_dev,
-                          double scale, const at::Tensor& status, double timeout_s) {
+                          double scale, const at::Tensor& status, double timeout_s, int64_t blocks_per_sm) {
   TORCH_CHECK(!src_ptrs.empty() && src_ptrs.size() <= static_cast<size_t>(kMaxSrc), "1..8 sources");
   TORCH_CHECK(!dst_ptrs.empty() && dst_ptrs.size() <= static_cast<size_t>(kMaxSrc), "1..8 destinations");
   if (hi <= lo) return;
@@ -394,7 +400,8 @@ void reduce_slice_scatter(const std::vector<int64_t>& src_ptrs, const std::vecto
   DstPtrs d{};
   for (size_t i = 0; i < dst_ptrs.size(); ++i) d.p[i] = reinterpret_cast<__nv_bfloat16*>(dst_ptrs[i]);
   const long n = hi - lo;
-  const long blocks = std::max<long>(1, std::min<long>((n / 8 + 255) / 256 + 1, static_cast<long>(sm_count()) * 4));
+  const long per_sm = blocks_per_sm > 0 ? blocks_per_sm : 4;
+  const long blocks = std::max<long>(1, std::min<long>((n / 8 + 255) / 256 + 1, static_cast<long>(sm_count()) * per_sm));
   const int ns = static_cast<int>(src_ptrs.size());
 #define SB_RS(NS)                                                                                           \
   reduce_slice_scatter_kernel<NS><<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(                     \

@@ -116,7 +116,12 @@ class MPWorker(Worker):
                 self.pp_group = g
         self.pp_ranks = [s * a.tp + self.t for s in range(a.pp)]
 
-    def build_engine(self):
+    def data_replica(self) -> int:
+        """Data rank of this replica in the sample index (the replica id; a
+        planned spare uses the logical id of the replica it replaces)."""
+        return self.args.replica
+
+    def build_engine(self, ipc_state: bool = False):
         a = self.args
         cfg = self.cfg
         lps = cfg.layers // a.pp
@@ -136,7 +141,7 @@ class MPWorker(Worker):
 
         self.comm = GroupTP(self.tp_group, self.t, a.tp) if a.tp > 1 else None
         self.engine = Engine(cfg, self.device, part=part, specs=rep + shard, seed_of=seed_of, tp=self.comm,
-                             bucket_numel=a.bucket_size)
+                             bucket_numel=a.bucket_size, ipc_state=ipc_state)
         st = self.engine.store
         self.rep_end = st.offsets[shard[0].name][0] if shard else st.numel
 
@@ -159,7 +164,7 @@ class MPWorker(Worker):
         pp, s = a.pp, self.s
         first, last = s == 0, s == pp - 1
         M, S, mb = a.microbatches, a.seq_len, a.batch
-        data = [synthetic_batch(self.cfg, step * (M * 4) + m * 4 + a.replica, mb, S, a.data,
+        data = [synthetic_batch(self.cfg, step * (M * 4) + m * 4 + self.data_replica(), mb, S, a.data,
                                 seed_base=100_000 + a.data_seed * 1_000_000).to(self.device) for m in range(M)]
         scale = 1.0 / (M * mb * S)
         losses = []
@@ -214,6 +219,13 @@ class MPWorker(Worker):
         kind, _, arg = self.args.inject.partition("@")
         return (kind == kind_wanted and step == int(arg) and self.rank == self.args.inject_rank
                 and self.args.replica == self.args.inject_replica and self.args.generation == 0)
+
+    def _replica_leaves(self, step) -> bool:
+        """The planned between-steps SIGKILL of one rank of this replica
+        happens after committing ``step``."""
+        kind, _, arg = self.args.inject.partition("@")
+        return (kind == "sigkill_step" and step == int(arg) and self.args.replica == self.args.inject_replica
+                and self.args.generation == 0)
 
     def _die(self, layer):
         self.event("injected_sigkill", step=self.progress["updates"], layer=layer, stage=self.s, tp_rank=self.t,
@@ -290,12 +302,19 @@ class MPWorker(Worker):
                            tokens=tokens_per_replica * mgr.num_participants(), seconds=time.monotonic() - it0)
             else:
                 self.event("skipped", step=step, error=str(mgr.errored()))
-            if commit and self._kill_now(step, "sigkill_step"):
+            if commit and self._replica_leaves(step):
                 # GPU form of the fault: the rank leaves between steps, with
-                # none of its kernels or collectives in flight
+                # none of its kernels or collectives in flight.  Every rank of
+                # the replica knows the plan, so the others stop at the same
+                # boundary on the host instead of launching a step that would
+                # wait for the dead rank inside a collective.
                 if self.device.type == "cuda":
                     torch.cuda.synchronize(self.device)
-                self._die(-1)
+                if self._kill_now(step, "sigkill_step"):
+                    self._die(-1)
+                self.event("replica_peer_leaving", step=self.progress["updates"], leaving_rank=a.inject_rank)
+                self.event.close()
+                os._exit(0)
         self.event("stopped", step=self.progress["updates"])
         mgr.shutdown()
         self.event.close()

@@ -52,6 +52,10 @@ def parse_args(argv=None):
 
 
 class PlannedWorker(Worker):
+    # model-parallel subclasses reduce over the Manager's process group (NCCL)
+    # instead of the fused peer-memory reducer of 1-GPU replicas
+    group_reduce = False
+
     def __init__(self, args):
         super().__init__(args)
         self.role = args.planned_role
@@ -137,7 +141,7 @@ class PlannedWorker(Worker):
     def make_manager(self, epoch: int, members: str = "AB", activate: bool = True):
         a = self.args
         port = a.lighthouse_port + 10 * epoch + (1 if members == "AB" and epoch > self.round else 0)
-        if self.device.type == "cuda":
+        if self.device.type == "cuda" and not self.group_reduce:
             # fused peer-memory reduction + IPC healing: a new epoch only re-maps handles
             from .fused import PeerStateTransport
             self.ensure_reducer()
@@ -145,11 +149,12 @@ class PlannedWorker(Worker):
             transport = PeerStateTransport(self.engine, self.device, self.reducer.owner, self.event,
                                            lambda: self.manager)
         else:
-            backend = a.backend or "gloo"
-            pg = ReconfigurableGroup(backend, a.communication_timeout, None, prefix=f"x{self.rank}e{epoch}",
-                                     event=self.event)
-            transport = PackedTransport(pg, torch.device("cpu"), timedelta(seconds=a.communication_timeout),
-                                        self.event)
+            cuda = self.device.type == "cuda"
+            backend = a.backend or ("nccl" if cuda else "gloo")
+            pg = ReconfigurableGroup(backend, a.communication_timeout, self.device if backend == "nccl" else None,
+                                     prefix=f"x{self.rank}e{epoch}", event=self.event)
+            transport = PackedTransport(pg, self.device if backend == "nccl" else torch.device("cpu"),
+                                        timedelta(seconds=a.communication_timeout), self.event)
         rid = self.logical_rid
         store_port = int(os.environ.get("SHIFT_STORE_PORT", "0"))
         store_port = (store_port + 100 * (epoch + 1) + 7 * (members == "AB")) if store_port else _free_port()
@@ -197,19 +202,30 @@ class PlannedWorker(Worker):
         return out, ids
 
     # ------------------------------------------------------------------ run
-    def run(self):
+    def setup_engine(self):
+        """The replica's model state (IPC-exportable on GPUs, so a spare can
+        pull it straight from the donor's HBM)."""
         from ..engine import Engine
+        a = self.args
+        cuda = self.device.type == "cuda"
+        self.engine = Engine(self.cfg, self.device, seed=a.seed, bucket_numel=a.bucket_size, ipc_state=cuda)
+        if cuda:
+            self.ensure_reducer()
+
+    def compute(self, step, batches):
+        """Forward + backward of this replica's share of step ``step``; the
+        gradient is left in the engine's flat buffer."""
+        return self.engine.forward_backward(batches, self.args.batch, self.args.seq_len)
+
+    def run(self):
         from ..models.qwen_moe import MoEConfig
         a = self.args
         torch.set_num_threads(1)
         self.cfg = MoEConfig.tiny() if a.model == "tiny" else MoEConfig.bench()
-        cuda = self.device.type == "cuda"
-        self.engine = Engine(self.cfg, self.device, seed=a.seed, bucket_numel=a.bucket_size, ipc_state=cuda)
+        self.setup_engine()
         self.engine.optim.lr = a.lr
         self.engine.scheduler.base_lrs = [a.lr]
         self.engine.scheduler._last_lr = [a.lr]
-        if cuda:
-            self.ensure_reducer()
         self.handoff = self.new_handoff(self.round)
         self.transport_on_cpu = False
         base_epoch = a.planned_round
@@ -243,7 +259,8 @@ class PlannedWorker(Worker):
         self.coord = Coordinator(a.coord, f"round/{round_}" if round_ else "")
         mover = a.mover if a.mover != "auto" else ("ipc" if cuda else "packed")
         cls = OverlapHandoff if a.planned_variant == "p2" else PlannedHandoff
-        hooks = [self.premap_k1, self.warmup_spare, self.precreate_manager] if cuda else [self.precreate_manager]
+        hooks = ([self.premap_k1, self.warmup_spare, self.precreate_manager] if cuda and not self.group_reduce
+                 else [self.precreate_manager])
         emit = lambda kind, **kw: self.event(kind, round=round_, **kw)   # noqa: E731
         h = cls(self.role, a.planned_variant, self.rank, self.local_world, self.coord, emit,
                 self.export_state, self.load_state, self.progress, self.manifest, self.device, mover,
@@ -309,7 +326,7 @@ class PlannedWorker(Worker):
                 eng.store.zero_grad()
                 loss = torch.zeros(())
             else:
-                loss = eng.forward_backward(batches, a.batch, a.seq_len)
+                loss = self.compute(step, batches)
                 self.forward_calls += 1
                 if a.planned_inject == "slow-compute":
                     time.sleep(a.planned_slow_ms / 1000.0)

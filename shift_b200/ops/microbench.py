@@ -242,12 +242,12 @@ def run_fused(iters):
     pb = torch.empty(n, device=dev, dtype=torch.bfloat16)
     nf = torch.zeros(1, dtype=torch.int32, device=dev)
     t = timeit(lambda: ext().reduce_slice_scatter([g0.data_ptr(), g1.data_ptr()], [red0.data_ptr(), red1.data_ptr()],
-                                                  0, n // 2, [], blk.dev, 0.5, st, 5.0), iters, warmup=_WARMUP)
+                                                  0, n // 2, [], blk.dev, 0.5, st, 5.0, 0), iters, warmup=_WARMUP)
     nbytes = (n // 2) * 2 * (2 + 2)                     # read 2 sources, write 2 destinations (bf16)
     rows.append({"case": f"K1.reduce_slice_scatter half of {n}", "ms": round(t, 4), "gbs": round(nbytes / t / 1e6, 1),
                  "frac_of_peak": round(nbytes / t / 1e6 / pk["hbm_gbs"], 3)})
     t = timeit(lambda: ext().fused_reduce_adamw([red0.data_ptr()], [], blk.dev, master, m, v, *outs, pb, 0.9, 0.999,
-                                                1e-8, 0.01, 1.0, nf, st, 5.0), iters, warmup=_WARMUP)
+                                                1e-8, 0.01, 1.0, nf, st, 5.0, 0), iters, warmup=_WARMUP)
     nbytes = n * (2 + 12 + 12 + 2)
     rows.append({"case": f"K1.fused_reduce_adamw {n}", "ms": round(t, 4), "gbs": round(nbytes / t / 1e6, 1),
                  "frac_of_peak": round(nbytes / t / 1e6 / pk["hbm_gbs"], 3)})

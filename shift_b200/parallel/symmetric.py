@@ -121,6 +121,7 @@ class CrossReplicaFused:
         self.step = 0
         self.launched: set[int] = set()
         self.active = False
+        self.overlap_blocks_per_sm = int(os.environ.get("SHIFT_K1_OVERLAP_BLOCKS", "1"))
 
     # ------------------------------------------------------------------ membership
     def configure(self, owners_in_replica_order: list[str], participating: list[bool] | None = None,
@@ -221,8 +222,16 @@ class CrossReplicaFused:
                 ext().fused_reduce_adamw(grad_ptrs, flag_ptrs, self.sdev, st.master[c][sl], st.exp_avg[c][sl],
                                          st.exp_avg_sq[c][sl], st.master[n][sl], st.exp_avg[n][sl],
                                          st.exp_avg_sq[n][sl], st.param[n][sl], o.beta1, o.beta2, o.eps,
-                                         o.weight_decay, scale, self.engine.nonfinite, self.status, self.timeout)
+                                         o.weight_decay, scale, self.engine.nonfinite, self.status, self.timeout,
+                                         self._grid())
         self.launched.add(b)
+
+    def _grid(self) -> int:
+        """Blocks per SM of a reduction launch: one while backward is still
+        running (the memory-bound reduction then shares every SM with the
+        compute kernels instead of holding the GPU until the bucket is done),
+        the whole GPU for buckets launched after backward."""
+        return self.overlap_blocks_per_sm if self.active else 0
 
     def _sliced(self, srcs) -> bool:
         """Whether a segment with these sources takes the two-phase form."""
@@ -241,7 +250,7 @@ class CrossReplicaFused:
         ext().fused_reduce_adamw([g.data_ptr()], [], self.sdev, st.master[c][sl], st.exp_avg[c][sl],
                                  st.exp_avg_sq[c][sl], st.master[n][sl], st.exp_avg[n][sl], st.exp_avg_sq[n][sl],
                                  st.param[n][sl], o.beta1, o.beta2, o.eps, o.weight_decay, self.scale,
-                                 self.engine.nonfinite, self.status, self.timeout)
+                                 self.engine.nonfinite, self.status, self.timeout, self._grid())
 
     def _two_phase(self, b, bk, par, tag, c, n, o):
         """Phase A: reduce this rank's slice of every segment and store it into
@@ -267,7 +276,7 @@ class CrossReplicaFused:
             ext().reduce_slice_scatter([self.grad_maps[w][par].data_ptr() for w in srcs],
                                        [self.red_maps[w].data_ptr() for w in members], cuts[k], cuts[k + 1],
                                        [self.flag_maps[w][b].data_ptr() for w in srcs if w != me], self.sdev,
-                                       scale, self.status, self.timeout)
+                                       scale, self.status, self.timeout, self._grid())
         if not parts:
             return
         ext().flag_set(self.flags[slice_flag].data_ptr(), self.sdev, 0)
@@ -277,10 +286,12 @@ class CrossReplicaFused:
                                      [self.flag_maps[w][slice_flag].data_ptr() for w in srcs if w != me], self.sdev,
                                      st.master[c][sl], st.exp_avg[c][sl], st.exp_avg_sq[c][sl], st.master[n][sl],
                                      st.exp_avg[n][sl], st.exp_avg_sq[n][sl], st.param[n][sl], o.beta1, o.beta2,
-                                     o.eps, o.weight_decay, 1.0, self.engine.nonfinite, self.status, self.timeout)
+                                     o.eps, o.weight_decay, 1.0, self.engine.nonfinite, self.status, self.timeout,
+                                     self._grid())
 
     def finish_step(self):
         """After backward: launch what is left, publish done, join streams."""
+        self.active = False          # nothing left to overlap with: full-GPU launches
         for b in range(self.nb):
             if b not in self.launched:
                 self._launch(b)

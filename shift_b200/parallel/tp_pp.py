@@ -249,7 +249,10 @@ class ModelParallelRunner:
                 pipe.exchange(send=(GRAD, j, dx))
         eng.model._accumulate = False
         self.fused.finish_step()
-        return self._loss if self._loss is not None else torch.zeros((), device=self.device)
+        if self._loss is None:
+            return torch.zeros((), device=self.device)
+        # the model returns token sums; this rank's share of the replica's mean loss
+        return self._loss / float(self.M * self.mb * self.S)
 
     def step(self, i: int):
         return self._train(self.dev_batches[i % len(self.dev_batches)])

@@ -12,22 +12,40 @@ host inputs copied in, loss read back) and ``layout``.
 """
 from __future__ import annotations
 
+import os
+
 import torch
 
 from .engine import Engine, synthetic_batch
 from .graphs import StepGraphs, graphs_enabled
 from .models.qwen_moe import MoEConfig
+from .parallel.symmetric import _tag
 
 
 class SingleRunner:
     layout = "dp1"
 
     def __init__(self, cfg: MoEConfig, device, batch: int, seq: int, n_prefetch: int = 4,
-                 graphs: bool | None = None):
+                 graphs: bool | None = None, overlap_optimizer: bool | None = None):
         self.cfg = cfg
         self.engine = Engine(cfg, device)
         self.B, self.S = batch, seq
         self.device = torch.device(device)
+        # AdamW per gradient bucket on a side stream as soon as backward has
+        # written the bucket (the cross-replica step's machinery with this
+        # GPU as the only member), instead of one full-model pass afterwards
+        if overlap_optimizer is None:
+            overlap_optimizer = os.environ.get("SHIFT_N1_OVERLAP", "1") == "1"
+        self.fused = None
+        if overlap_optimizer and self.device.type == "cuda":
+            from .parallel.replicas import _order
+            from .parallel.symmetric import CrossReplicaFused, SymmetricHeap
+            self.heap = SymmetricHeap(None, "solo", self.device)
+            self.fused = CrossReplicaFused(self.engine, self.heap, mode="one")
+            self.fused.configure(["solo"])
+            layers = cfg.layers
+            self.engine.model.layer_done_hook = lambda layer: self.fused.on_layer_done(_order(layer, layers))
+            self.layout = "dp1 (AdamW per bucket overlapped with backward)"
         # device-resident inputs for the kernel-timed loop
         self.dev_batches = [synthetic_batch(cfg, i, batch, seq).to(self.device) for i in range(n_prefetch)]
         self.host = synthetic_batch(cfg, 10_000, batch, seq).pin_memory()
@@ -38,12 +56,18 @@ class SingleRunner:
 
     def _device_step(self):
         tok, lab = self.tokens[:, :-1], self.tokens[:, 1:]
+        if self.fused is not None:
+            self.engine.nonfinite.zero_()
+            self.fused.begin_step(self.step_no, prepare=False)
+            loss = self.engine.forward_backward([(tok, lab)], self.B, self.S)
+            self.fused.finish_step()
+            return loss
         loss = self.engine.forward_backward([(tok, lab)], self.B, self.S)
         self.engine.optimizer_step(prepared=True)
         return loss
 
     def _train(self):
-        self.engine.prepare_step(self.step_no + 1)
+        self.engine.prepare_step(_tag(self.step_no))
         if self.step_no < 2:      # eager warm-up steps (lazy initialisation)
             loss = self._device_step()
         else:

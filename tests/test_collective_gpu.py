@@ -35,7 +35,7 @@ def test_fused_reduce_adamw_local_sources_matches_reference():
     st.zero_()
     sdev = _step_block(dev, 1, 1e-3, 0.9, 0.999, 5)
     ext().fused_reduce_adamw([g.data_ptr() for g in gs], [], sdev, master, m, v, *outs, pb, 0.9, 0.999, 1e-8,
-                             0.01, 1 / 3, flag, st, 5.0)
+                             0.01, 1 / 3, flag, st, 5.0, 0)
     torch.cuda.synchronize()
     g = (gs[0].float() + gs[1].float() + gs[2].float()) / 3
     em, emm, ev = ref.adamw(master, m, v, g, 1e-3, 0.9, 0.999, 1e-8, 0.01, 5)
@@ -72,7 +72,7 @@ def test_flag_wait_times_out_with_status_and_context_survives():
     s5 = _step_block(dev, 5, 1e-3, 0.9, 0.999, 1)
     ext().fused_reduce_adamw([g.data_ptr()], [flags[1].data_ptr()], s5, master, master, master, out, out.clone(),
                              out.clone(), torch.empty(n, device=dev, dtype=torch.bfloat16), 0.9, 0.999, 1e-8,
-                             0.0, 1.0, nf, st, 0.2)
+                             0.0, 1.0, nf, st, 0.2, 0)
     torch.cuda.synchronize()
     assert int(st[0]) == 2
     assert torch.all(out == 123.0)

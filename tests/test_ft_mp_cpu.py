@@ -8,6 +8,8 @@ equal state hashes again."""
 import json
 import socket
 
+import pytest
+
 from shift_b200.control.session import Session
 
 
@@ -23,14 +25,18 @@ def _ports(n):
     return out
 
 
-def test_tp_rank_sigkill_mid_backward_recovers_with_migration(tmp_path):
+@pytest.mark.parametrize("inject", ["sigkill_bwd@5", "sigkill_step@5"])
+def test_tp_rank_sigkill_recovers_with_migration(tmp_path, inject):
+    """sigkill_bwd: the rank dies mid-backward (CPU only); sigkill_step: the
+    form used on GPUs -- the rank dies between steps and the rest of its
+    replica stops at the same boundary on the host."""
     lh, mp, sp_ = _ports(3)
     cfg = {
         "entry_module": "shift_b200.ft.mp_train",
         "nproc_per_node": 4,
         "train_args": ["--model", "tiny", "--device", "cpu", "--seq-len", "128", "--batch", "1", "--microbatches",
                        "2", "--tp", "2", "--pp", "2", "--audit-state", "--hash-every", "1", "--data", "random",
-                       "--communication-timeout", "20", "--inject", "sigkill_bwd@5", "--inject-rank", "1",
+                       "--communication-timeout", "20", "--inject", inject, "--inject-rank", "1",
                        "--inject-replica", "0"],
         "lighthouse_port": lh, "master_port": mp, "store_port_base": sp_ + 1000 if sp_ < 60000 else 20000,
         "min_replicas": 1, "heartbeat_timeout_ms": 400, "join_timeout_ms": 300, "quorum_tick_ms": 20,

@@ -71,3 +71,17 @@ def test_three_rotation_cycles_with_audits(tmp_path, variant):
     from shift_b200.analysis.verify_rotation import verify
     ver = verify(s.dir, variant=variant)
     assert ver["pass"], {k: v for k, v in ver["checks"].items() if not v["pass"]}
+
+
+@pytest.mark.parametrize("variant", ["p1f", "p2"])
+def test_planned_handoff_of_a_tp2_pp2_replica(tmp_path, variant):
+    """The whole 4-rank TP2 x PP2 replica B is handed to a 4-rank spare C:
+    every rank of C restores the same-coordinate rank of B (state hashes
+    audited), and the post-handoff A+C commits agree with A bit for bit."""
+    s = PlannedSession(tmp_path, f"mp_{variant}", variant=variant, nproc=4, module="shift_b200.ft.mp_planned_train",
+                       train_args=["--tp", "2", "--pp", "2", "--microbatches", "2", "--batch", "1"])
+    res = s.run(post_steps=3)
+    assert res["returncodes"] == {"A": 0, "B": 0, "C": 0}, res["returncodes"]
+    failed = {k: v for k, v in res["checks"].items() if not v["pass"]}
+    assert res["pass"], failed
+    assert res["handoff_interval_s"] > 0

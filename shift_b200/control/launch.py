@@ -10,6 +10,13 @@ after terminating the other ranks, like torchrun's behaviour under
 ``--max_restarts=0`` that the reference relies on (shift_full/supervisor.py:203-248).
 It is a light native replacement for torchrun (no rendezvous agent), which is
 what keeps the relaunch of a killed replica short.
+
+``--fork``: the ranks are forked from this process and run the trainer
+module in-process (``runpy``) instead of exec'ing a new interpreter.  A
+supervisor that has already imported torch and the trainer (without touching
+CUDA) forks the launcher the same way, so a relaunched replica starts with
+every module loaded -- the reference's fork preload
+(shift_full/fast_launch.py:27-97, shift_full/launch_server.py).
 """
 from __future__ import annotations
 
@@ -21,6 +28,83 @@ import sys
 import time
 
 
+class ForkedProcess:
+    """The part of ``subprocess.Popen`` the launchers use, for a forked child."""
+
+    def __init__(self, pid: int):
+        self.pid = pid
+        self.returncode = None
+
+    @classmethod
+    def start(cls, body, log_path=None, new_session=False) -> "ForkedProcess":
+        sys.stdout.flush()
+        sys.stderr.flush()
+        pid = os.fork()
+        if pid == 0:                                  # child
+            code = 1
+            try:
+                if new_session:
+                    os.setsid()
+                if log_path is not None:
+                    fd = os.open(log_path, os.O_WRONLY | os.O_CREAT | os.O_APPEND, 0o644)
+                    os.dup2(fd, 1)
+                    os.dup2(fd, 2)
+                    os.close(fd)
+                code = body() or 0
+            except SystemExit as e:
+                code = e.code if isinstance(e.code, int) else (0 if e.code is None else 1)
+            except BaseException:
+                import traceback
+                traceback.print_exc()
+                code = 1
+            finally:
+                try:
+                    sys.stdout.flush()
+                    sys.stderr.flush()
+                finally:
+                    os._exit(code)
+        return cls(pid)
+
+    def poll(self):
+        if self.returncode is None:
+            try:
+                got, status = os.waitpid(self.pid, os.WNOHANG)
+            except ChildProcessError:                 # collected elsewhere (e.g. an orphan reaper)
+                self.returncode = -signal.SIGKILL
+                return self.returncode
+            if got == self.pid:
+                self.returncode = os.waitstatus_to_exitcode(status)
+        return self.returncode
+
+    def wait(self, timeout=None):
+        end = None if timeout is None else time.monotonic() + timeout
+        while self.poll() is None:
+            if end is not None and time.monotonic() > end:
+                raise subprocess.TimeoutExpired(f"pid {self.pid}", timeout)
+            time.sleep(0.01)
+        return self.returncode
+
+    def send_signal(self, sig):
+        if self.poll() is None:
+            os.kill(self.pid, sig)
+
+    def terminate(self):
+        self.send_signal(signal.SIGTERM)
+
+    def kill(self):
+        self.send_signal(signal.SIGKILL)
+
+
+def run_module_in_child(module: str, args: list, env: dict):
+    """Body of a forked rank: its environment, then the module as __main__."""
+    import runpy
+    os.environ.clear()
+    os.environ.update(env)
+    sys.argv = [module, *args]
+    runpy.run_module(module, run_name="__main__", alter_sys=True)
+    return 0
+
+
 def main(argv=None):
     p = argparse.ArgumentParser()
     p.add_argument("--nproc", type=int, default=1)
@@ -28,6 +112,7 @@ def main(argv=None):
     p.add_argument("--master-port", type=int, default=29600)
     p.add_argument("--devices", default="")
     p.add_argument("--module", required=True)
+    p.add_argument("--fork", action="store_true", help="fork the ranks from this (preloaded) process")
     p.add_argument("rest", nargs=argparse.REMAINDER)
     a = p.parse_args(argv)
     rest = a.rest[1:] if a.rest and a.rest[0] == "--" else a.rest
@@ -38,7 +123,10 @@ def main(argv=None):
                    LOCAL_WORLD_SIZE=str(a.nproc), MASTER_ADDR=a.master_addr, MASTER_PORT=str(a.master_port))
         if devices:
             env["SHIFT_CUDA_DEVICE"] = devices[r % len(devices)]
-        procs.append(subprocess.Popen([sys.executable, "-m", a.module, *rest], env=env))
+        if a.fork:
+            procs.append(ForkedProcess.start(lambda env=env: run_module_in_child(a.module, rest, env)))
+        else:
+            procs.append(subprocess.Popen([sys.executable, "-m", a.module, *rest], env=env))
 
     def forward(sig, _frame):
         for q in procs:

@@ -361,6 +361,10 @@ def main(argv=None):
     ap.add_argument("--nproc", type=int, default=1)
     ap.add_argument("--gpus", default="", help="A,B,C device lists, e.g. '0;1;2'")
     ap.add_argument("--train-args", default="", help="extra trainer flags, e.g. '--seq-len 2048 --batch 4'")
+    ap.add_argument("--module", default="shift_b200.ft.planned_train",
+                    help="worker module; shift_b200.ft.mp_planned_train hands over TP x PP replicas "
+                         "(--nproc tp*pp, --train-args '--tp 2 --pp 2 ...')")
+    ap.add_argument("--runs", type=int, default=1, help="independent handoff sessions (name_1, name_2, ...)")
     ap.add_argument("--no-preflight", action="store_true",
                     help="skip the check that no other compute process holds the session's GPUs")
     a = ap.parse_args(argv)
@@ -376,12 +380,23 @@ def main(argv=None):
             print(json.dumps({"pass": False, "preflight": pre}, default=str))
             return 2
     import shlex
-    s = PlannedSession(a.root, a.name, a.variant, a.scenario, a.model, a.device, a.nproc, devices=devices,
-                       train_args=shlex.split(a.train_args))
-    res = s.run_cycles(a.cycles, a.post_steps) if a.cycles > 1 else s.run(a.post_steps, a.cancel)
-    print(json.dumps({k: v for k, v in res.items() if k != "checks"}, indent=1, default=str))
-    print(json.dumps({k: v["pass"] for k, v in res.get("checks", {}).items()}, indent=1))
-    return 0 if res.get("pass") else 1
+    results = []
+    for i in range(a.runs):
+        name = a.name if a.runs == 1 else f"{a.name}_{i + 1}"
+        s = PlannedSession(a.root, name, a.variant, a.scenario, a.model, a.device, a.nproc, devices=devices,
+                           train_args=shlex.split(a.train_args), module=a.module)
+        res = s.run_cycles(a.cycles, a.post_steps) if a.cycles > 1 else s.run(a.post_steps, a.cancel)
+        print(json.dumps({k: v for k, v in res.items() if k != "checks"}, indent=1, default=str))
+        print(json.dumps({k: v["pass"] for k, v in res.get("checks", {}).items()}, indent=1))
+        results.append(res)
+    if a.runs > 1:
+        ivs = sorted(r["handoff_interval_s"] for r in results if r.get("handoff_interval_s") is not None)
+        agg = {"runs": a.runs, "variant": a.variant, "module": a.module, "intervals_s": ivs,
+               "median_interval_s": ivs[len(ivs) // 2] if ivs else None,
+               "all_pass": all(r.get("pass") for r in results)}
+        (Path(a.root) / f"{a.name}_runs.json").write_text(json.dumps(agg, indent=1) + "\n")
+        print(json.dumps(agg, indent=1))
+    return 0 if all(r.get("pass") for r in results) else 1
 
 
 if __name__ == "__main__":

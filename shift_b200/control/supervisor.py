@@ -61,6 +61,13 @@ DEFAULTS = {
     "devices": [],                 # per replica: list of GPU index lists, or [] for CPU
     "restart_devices": [],         # per replica: GPUs of a relaunched generation (stage migration to spares)
     "store_port_base": 29700,
+    # fork every generation from this supervisor after importing torch and the
+    # trainer once (no CUDA in the supervisor): a relaunch skips interpreter
+    # and import start-up
+    "fast_launch": False,
+    # relaunched generations skip the seeded initialisation (their state comes
+    # from a live peer); they refuse to train if no heal happens
+    "lazy_restart_init": False,
 }
 REQUIRED = ("train_args",)
 
@@ -177,7 +184,22 @@ def main(argv=None):
                 str(cfg["min_replicas"]), *cfg["train_args"], *extra]
         e = dict(env)
         e["SHIFT_STORE_PORT"] = str(cfg["store_port_base"] + 10 * args.replica + gen)
-        proc = sp.Popen(cmd, env=e, stdout=log, stderr=sp.STDOUT, start_new_session=True)
+        if gen > 0 and cfg["lazy_restart_init"] and "--standby" not in extra:
+            cmd += ["--lazy-init"]
+        if cfg["fast_launch"]:
+            from .launch import ForkedProcess, main as launch_main
+            largs = cmd[3:]                            # after "<python> -m shift_b200.control.launch"
+            largs.insert(largs.index("--module"), "--fork")
+
+            def body(largs=largs, e=e):
+                os.environ.clear()
+                os.environ.update(e)
+                launch_main(largs)
+
+            proc = ForkedProcess.start(body, log_path=str(out / f"launcher_r{args.replica}_g{gen}.log"),
+                                       new_session=True)
+        else:
+            proc = sp.Popen(cmd, env=e, stdout=log, stderr=sp.STDOUT, start_new_session=True)
         ev("launched", generation=gen, launcher_pid=proc.pid, master_port=port, command=cmd,
            standby=extra[1] if extra and extra[0] == "--standby" else None)
         return proc
@@ -251,6 +273,12 @@ def main(argv=None):
                 proc.wait(timeout=10)
         return proc.poll()
 
+    if cfg["fast_launch"]:
+        # preload: torch and the trainer module, CPU only, before any fork
+        import importlib
+        t0 = time.monotonic()
+        importlib.import_module(cfg["entry_module"])
+        ev("preloaded", module=cfg["entry_module"], seconds=time.monotonic() - t0)
     try:
         if cfg["mode"] == "shift" and args.replica == 0 and not cfg["external_lighthouse"]:
             start_lighthouse()

@@ -115,7 +115,7 @@ class StepBlock:
 class Engine:
     def __init__(self, cfg: MoEConfig, device, part: Partition | None = None, optim: OptimConfig | None = None,
                  seed: int = 2026, bucket_numel: int = 64 * 1024 * 1024, compute_dtype=None,
-                 ipc_state: bool = False, tp=None, specs=None, seed_of=None):
+                 ipc_state: bool = False, tp=None, specs=None, seed_of=None, init: bool = True):
         self.cfg = cfg
         self.device = torch.device(device)
         self.part = part or Partition()
@@ -124,7 +124,10 @@ class Engine:
             compute_dtype = torch.bfloat16 if self.device.type == "cuda" else torch.float32
         self.store = FlatParams(specs if specs is not None else param_specs(cfg, self.part), self.device,
                                 compute_dtype, bucket_numel, ipc_state=ipc_state)
-        self.store.init_(cfg.init_std, torch.Generator().manual_seed(seed), seed_of=seed_of)
+        if init:
+            self.store.init_(cfg.init_std, torch.Generator().manual_seed(seed), seed_of=seed_of)
+        # init=False: the flat buffers stay zero until a state is loaded into them
+        # (a relaunched replica that heals from a live peer)
         self.model = QwenMoE(cfg, self.store, self.part, tp=tp)
         self.scheduler = StepLR(self.optim.lr, self.optim.step_size, self.optim.gamma)
         self.nonfinite = torch.zeros(1, dtype=torch.int32, device=self.device)

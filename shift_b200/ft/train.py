@@ -74,6 +74,9 @@ def parse_args(argv=None):
     p.add_argument("--checkpoint-cold", action="store_true")
     p.add_argument("--resume-checkpoint", action="store_true")
     p.add_argument("--standby", choices=("cpu", "gpu"))
+    p.add_argument("--lazy-init", action="store_true",
+                   help="skip the seeded initialisation: the state must come from a live peer at the first quorum "
+                        "(a relaunched replica); the worker refuses to train otherwise")
     p.add_argument("--activate-marker", default="ACTIVATE",
                    help="marker file (in the session directory) that releases a standby process")
     p.add_argument("--bucket-size", type=int, default=64 * 1024 * 1024)
@@ -193,6 +196,7 @@ class Worker:
             self.engine.load_state_dict(payload)
         self.progress.update(payload["progress"])
         set_rng_state(payload, self.device)
+        self.healed = True
         if self.device.type == "cuda":
             torch.cuda.current_stream().synchronize()
         loaded = time.monotonic()
@@ -305,7 +309,7 @@ class Worker:
         started = self.phase("python_imports", _MODULE_STARTED)
         torch.set_num_threads(1)
         self.cfg = MoEConfig.tiny() if a.model == "tiny" else MoEConfig.bench()
-        self.engine = Engine(self.cfg, self.device, seed=a.seed, bucket_numel=a.bucket_size)
+        self.engine = Engine(self.cfg, self.device, seed=a.seed, bucket_numel=a.bucket_size, init=not a.lazy_init)
         self.engine.optim.lr = a.lr
         self.engine.scheduler.base_lrs = [a.lr]
         self.engine.scheduler._last_lr = [a.lr]
@@ -393,6 +397,8 @@ class Worker:
                 recovery_requested = True
             q0 = time.monotonic()
             mgr.start_quorum()
+            if a.lazy_init and not getattr(self, "healed", False):
+                raise RuntimeError("--lazy-init: the first quorum did not load a live peer's state into this replica")
             step = self.progress["updates"]
             participants = mgr.num_participants()
             self.event("begin", step=step, participants=participants, quorum_seconds=time.monotonic() - q0)

@@ -22,7 +22,7 @@ def _ports(n):
     return out
 
 
-def _config(tmp_path, extra=()):
+def _config(tmp_path, extra=(), **keys):
     lh, mp, sp_ = _ports(3)
     cfg = {
         "train_args": ["--model", "tiny", "--device", "cpu", "--seq-len", "64", "--batch", "2", "--audit-state",
@@ -30,6 +30,7 @@ def _config(tmp_path, extra=()):
         "lighthouse_port": lh, "master_port": mp, "store_port_base": sp_ + 1000 if sp_ < 60000 else 20000,
         "min_replicas": 1, "heartbeat_timeout_ms": 400, "join_timeout_ms": 300, "quorum_tick_ms": 20,
         "target_steps": 100000,
+        **keys,
     }
     p = tmp_path / "cfg.json"
     p.write_text(json.dumps(cfg))
@@ -74,3 +75,20 @@ def test_checkpoint_restart_resumes_both_replicas(tmp_path):
     assert res["pass"], res
     assert res["checkpoint_step"] == 3 and res["resumed_steps"] == [3]
     assert res["first_joint_step"] > 3
+
+
+def test_fast_launch_and_lazy_restart_heal(tmp_path):
+    """Generations forked from the preloaded supervisor; the relaunched one
+    skips the seeded initialisation and must still restore the live state."""
+    s = Session(tmp_path, "fast", _config(tmp_path, fast_launch=True, lazy_restart_init=True), replicas=2,
+                seconds=900)
+    s.start(timeout=180)
+    try:
+        res = Rotation(s, "cold", seed=1).fault(0)
+    finally:
+        s.finish()
+    assert res["pass"] and res["rpo_zero"] and res["restore_hashes_match"], res
+    sup = [json.loads(x) for r in (0, 1) for x in (tmp_path / "fast" / f"supervisor_r{r}.jsonl").read_text().splitlines()]
+    assert sum(1 for r in sup if r.get("kind") == "preloaded") == 2
+    launched = [r for r in sup if r.get("kind") == "launched" and r.get("generation") == 1]
+    assert launched and "--lazy-init" in launched[0]["command"]

@@ -12,7 +12,8 @@
 //   warp 1   TMEM allocation + single-thread tcgen05.mma issue:
 //              S_j = Q K_j^T   (128x128x64, TMEM, double-buffered)
 //              O_j = P_j V_j   (128x64x128, TMEM, double-buffered, fresh per block)
-//   warps 2-5 softmax, one thread per query row (= TMEM lane): reads S_j with
+//   warps 2-9 softmax, two warps per query row group (= TMEM lane quarter),
+//              each on half of the columns: reads S_j with
 //              tcgen05.ld, online max / sum, writes P_j (bf16) into 128B-swizzled
 //              shared memory for the next MMA, and folds O_{j-1} into a register
 //              accumulator with the running rescale (no TMEM read-modify-write).
@@ -44,10 +45,14 @@ namespace fa {
 constexpr int D = 64;
 constexpr int BM = 128;
 constexpr int BN = 128;
-// warp 0: TMA producer, warp 1: TMEM owner + MMA issuer, warps 2..9: softmax /
-// epilogue.  Two softmax warps share each TMEM lane quarter (warp % 4) and
-// split the 128 columns of a tile (half = (warp - 2) / 4), which halves the
-// per-thread exponent/convert/store stream that bounds these kernels.
+// warp 0: TMA producer, warp 1: TMEM owner + MMA issuer, then the softmax /
+// epilogue warps.  Forward: two softmax warps share each TMEM lane quarter
+// (warp % 4) and split the 128 columns of a tile (half = (warp - 2) / 4).
+// Backward: four warps per quarter, each taking 16 of a 64-column sub-block
+// (no cross-warp reductions there: lse and delta are given), which gives the
+// SM four times the warps to hide TMEM-load and exponent latencies.  (Four
+// warps per quarter in the forward measured slower -- 0.312 vs 0.257 ms at
+// B 8, S 2048 -- its row max / sum exchange spans twice the warps.)
 constexpr int kThreads = 320;
 constexpr int kSoftThreads = 256;
 constexpr int kTile = 128 * 128;   // bytes of one 128 x 64 bf16 tile
@@ -85,22 +90,11 @@ SB_DEVICE uint64_t mndesc(uint32_t addr) { return make_sw128_desc(addr, 8192, 10
 SB_DEVICE void named_bar(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
 
 // ============================ forward ============================
-// The forward's softmax is issue-bound (exp2, FMA, conversion and stores per
-// score), so it runs four warps per TMEM lane quarter: warp 2 + 4k + q' reads
-// lanes of quarter (warp % 4) and columns [32k, 32k + 32) of each S tile and
-// folds columns [16k, 16k + 16) of O -- 16 softmax warps and half the
-// registers per thread of a two-warp split, so more warps hide the latency of
-// each other's TMEM loads, exponentials and barriers.
 constexpr int kFwdStages = 2;
-constexpr int kFwdSplit = 4;                          // softmax warps per lane quarter
-constexpr int kFwdSoft = 128 * kFwdSplit;             // softmax threads
-constexpr int kFwdThreads = 64 + kFwdSoft;
-constexpr int kFwdCols = BN / kFwdSplit;              // S columns per softmax warp
-constexpr int kFwdOCols = D / kFwdSplit;              // O columns per softmax warp
 constexpr int kFwdSmem = 1024 + kTile /*Q*/ + 2 * kFwdStages * kTile /*K,V*/ + 2 * 2 * kTile /*P x2*/ + 256 +
-                         (2 * kFwdSplit * 128 + kFwdSplit * 128) * 4 /*row max / sum exchange*/;
+                         (2 * 2 * 128 + 2 * 128) * 4 /*row max / sum exchange*/;
 
-__global__ void __launch_bounds__(kFwdThreads, 1)
+__global__ void __launch_bounds__(kThreads, 1)
 fwd_kernel(const __grid_constant__ CUtensorMap tm, Params p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -118,13 +112,12 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm, Params p) {
   uint64_t* o_full = p_full + 2;
   uint64_t* drain = o_full + 2;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(drain + 1);
-  // row-max exchange between the softmax warps of a lane quarter,
-  // double-buffered by block parity: [parity][part][row]; then the row sums
+  // row-max exchange between the two softmax warps of a lane quarter,
+  // double-buffered by block parity: [parity][half][row]; then the row sums
   float* s_max = reinterpret_cast<float*>(tslot + 4);
-  float* s_sum = s_max + 2 * kFwdSplit * BM;
+  float* s_sum = s_max + 2 * 2 * BM;
 
-  // longest rows of the causal triangle first (they bound the tail of the grid)
-  const int qb = static_cast<int>(gridDim.x) - 1 - static_cast<int>(blockIdx.x), h = blockIdx.y, b = blockIdx.z;
+  const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int kvh = h / (p.Hq / p.Hkv);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int q0 = qb * BM;
@@ -139,7 +132,7 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm, Params p) {
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], kFwdSoft);
+      mbar_init(&p_full[i], kSoftThreads);
       mbar_init(&o_full[i], 1);
     }
     mbar_init(drain, 1);
@@ -204,66 +197,65 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm, Params p) {
     }
   } else {
     // ----------------------------- softmax -----------------------------
-    const int quarter = warp % 4;             // TMEM lane quarter this warp may access
-    const int part = (warp - 2) / 4;          // columns [32*part, +32) of S, [16*part, +16) of O
+    const int quarter = warp % 4;
+    const int half = (warp - 2) / 4;          // columns [64*half, 64*half+64) of S, [32*half, +32) of O
     const int row = quarter * 32 + lane;
     const int q = q0 + row;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    const int quad_bar = 1 + quarter;         // named barrier of the four warps of this quarter
+    const int pair_bar = 1 + quarter;         // named barrier of the two warps of this quarter
     float m_run = -INFINITY, l_run = 0.f, m_fold = -INFINITY;
-    float o_acc[kFwdOCols];
+    float o_acc[D / 2];
 #pragma unroll
-    for (int i = 0; i < kFwdOCols; ++i) o_acc[i] = 0.f;
+    for (int i = 0; i < D / 2; ++i) o_acc[i] = 0.f;
     bool ok = true;
     auto fold = [&](int i, float m_i) -> bool {
       if (!mbar_wait(&o_full[i & 1], (i >> 1) & 1, p.status)) return false;
       tc_fence_after();
       const float a = (m_fold == -INFINITY) ? 0.f : ex2(m_fold - m_i);
-      uint32_t v[kFwdOCols];
-      tmem_ld_32x32b_x16(tbase + 256 + (i & 1) * D + part * kFwdOCols + lane_off, v);
+      uint32_t v[32];
+      tmem_ld_32x32b_x32(tbase + 256 + (i & 1) * D + half * 32 + lane_off, v);
       tmem_wait_ld();
 #pragma unroll
-      for (int t = 0; t < kFwdOCols; ++t) o_acc[t] = o_acc[t] * a + __uint_as_float(v[t]);
+      for (int t = 0; t < 32; ++t) o_acc[t] = o_acc[t] * a + __uint_as_float(v[t]);
       m_fold = m_i;
       return true;
     };
-    // All warps of a quarter run every iteration's named barrier even after a
+    // Both warps of a pair run every iteration's named barrier even after a
     // bounded wait failed (they then skip the work), so a failure in one warp
-    // can never leave its partners blocked on the barrier.
+    // can never leave its partner blocked on the barrier.
     for (int j = 0; j < n_kv; ++j) {
       if (ok && !mbar_wait(&s_full[j & 1], (j >> 1) & 1, p.status)) ok = false;
       if (ok) tc_fence_after();
       const uint32_t ts = tbase + (j & 1) * BN + lane_off;
       const bool diag = (j == qb);
-      // pass 1: this warp's 32 columns of S come out of TMEM once and stay in
-      // registers for pass 2; row max over them (the causal mask only exists
-      // on the diagonal tile) in four independent chains, then combined with
-      // the other three warps' through shared memory.
-      uint32_t v[kFwdCols];
+      // pass 1: this warp's 64 columns of S come out of TMEM once (two loads,
+      // one wait) and stay in registers for pass 2.  Row max over them (the
+      // causal mask only exists on the diagonal tile) in four independent
+      // chains, scaled once, then combined with the partner warp's.
+      uint32_t v[64];
       float mraw = -INFINITY;
-      const int c_lo = part * kFwdCols;
+      const int c_lo = half * 64;
       if (ok) {
         tmem_ld_32x32b_x32(ts + c_lo, v);
+        tmem_ld_32x32b_x32(ts + c_lo + 32, v + 32);
         tmem_wait_ld();
         float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
         if (diag) {
           const int lim = q - j * BN - c_lo;       // columns t <= lim are visible
 #pragma unroll
-          for (int t = 0; t < kFwdCols; ++t)
+          for (int t = 0; t < 64; ++t)
             if (t <= lim) m4[t & 3] = fmaxf(m4[t & 3], __uint_as_float(v[t]));
         } else {
 #pragma unroll
-          for (int t = 0; t < kFwdCols; ++t) m4[t & 3] = fmaxf(m4[t & 3], __uint_as_float(v[t]));
+          for (int t = 0; t < 64; ++t) m4[t & 3] = fmaxf(m4[t & 3], __uint_as_float(v[t]));
         }
         mraw = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
       }
       float mx = fmaxf(m_run, mraw * p.scale_log2);
-      float* xm = s_max + (j & 1) * kFwdSplit * BM;
-      xm[part * BM + row] = mx;
-      named_bar(quad_bar, 128);
+      s_max[((j & 1) * 2 + half) * BM + row] = mx;
+      named_bar(pair_bar, 64);
       if (!ok) continue;
-#pragma unroll
-      for (int o = 1; o < kFwdSplit; ++o) mx = fmaxf(mx, xm[((part + o) % kFwdSplit) * BM + row]);
+      mx = fmaxf(mx, s_max[((j & 1) * 2 + (half ^ 1)) * BM + row]);
       const float m_prev = m_run;
       m_run = mx;
       // pass 2: probabilities -> shared memory (bf16, swizzled); the row sum
@@ -271,25 +263,29 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm, Params p) {
       uint8_t* pbuf = sP + (j & 1) * 2 * kTile;
       const float nmx = -mx;
       float l4[4] = {0.f, 0.f, 0.f, 0.f};
-      float pr[kFwdCols];
-      if (diag) {
-        const int lim = q - j * BN - c_lo;
 #pragma unroll
-        for (int t = 0; t < kFwdCols; ++t) {
-          pr[t] = (t > lim) ? 0.f : ex2(fmaf(__uint_as_float(v[t]), p.scale_log2, nmx));
-          l4[t & 3] += pr[t];
+      for (int cc = 0; cc < 2; ++cc) {
+        float pr[32];
+        if (diag) {
+          const int lim = q - j * BN - c_lo - cc * 32;
+#pragma unroll
+          for (int t = 0; t < 32; ++t) {
+            pr[t] = (t > lim) ? 0.f : ex2(fmaf(__uint_as_float(v[cc * 32 + t]), p.scale_log2, nmx));
+            l4[t & 3] += pr[t];
+          }
+        } else {
+#pragma unroll
+          for (int t = 0; t < 32; ++t) {
+            pr[t] = ex2(fmaf(__uint_as_float(v[cc * 32 + t]), p.scale_log2, nmx));
+            l4[t & 3] += pr[t];
+          }
         }
-      } else {
 #pragma unroll
-        for (int t = 0; t < kFwdCols; ++t) {
-          pr[t] = ex2(fmaf(__uint_as_float(v[t]), p.scale_log2, nmx));
-          l4[t & 3] += pr[t];
+        for (int u = 0; u < 4; ++u) {
+          bf16x8 pk = float_to_bf16x8(pr + 8 * u);
+          *reinterpret_cast<uint4*>(swz_chunk(pbuf, row, ((c_lo + cc * 32) >> 3) + u)) =
+              make_uint4(pk.w[0], pk.w[1], pk.w[2], pk.w[3]);
         }
-      }
-#pragma unroll
-      for (int u = 0; u < kFwdCols / 8; ++u) {
-        bf16x8 pk = float_to_bf16x8(pr + 8 * u);
-        *reinterpret_cast<uint4*>(swz_chunk(pbuf, row, (c_lo >> 3) + u)) = make_uint4(pk.w[0], pk.w[1], pk.w[2], pk.w[3]);
       }
       l_run = ((m_prev == -INFINITY) ? 0.f : l_run * ex2(m_prev - mx)) + ((l4[0] + l4[1]) + (l4[2] + l4[3]));
       fence_proxy_async_smem();
@@ -298,22 +294,21 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm, Params p) {
       if (j >= 1 && !fold(j - 1, m_prev)) ok = false;
     }
     if (ok) ok = fold(n_kv - 1, m_run);
-    // row sum = the four parts' partial sums (same running max)
-    s_sum[part * BM + row] = l_run;
-    named_bar(quad_bar, 128);
-#pragma unroll
-    for (int o = 1; o < kFwdSplit; ++o) l_run += s_sum[((part + o) % kFwdSplit) * BM + row];
+    // row sum = both halves' partial sums (same running max)
+    s_sum[half * BM + row] = l_run;
+    named_bar(pair_bar, 64);
+    l_run += s_sum[(half ^ 1) * BM + row];
     if (ok) {
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-      __nv_bfloat16* orow = p.o + static_cast<long>(tok0 + q) * p.o_stride + h * D + part * kFwdOCols;
+      __nv_bfloat16* orow = p.o + static_cast<long>(tok0 + q) * p.o_stride + h * D + half * 32;
 #pragma unroll
-      for (int c = 0; c < kFwdOCols; c += 8) {
+      for (int c = 0; c < D / 2; c += 8) {
         float t8[8];
 #pragma unroll
         for (int t = 0; t < 8; ++t) t8[t] = o_acc[c + t] * inv;
         *reinterpret_cast<bf16x8*>(orow + c) = float_to_bf16x8(t8);
       }
-      if (part == 0) p.lse[(static_cast<long>(b) * p.Hq + h) * p.S + q] = m_run + log2f(l_run);
+      if (half == 0) p.lse[(static_cast<long>(b) * p.Hq + h) * p.S + q] = m_run + log2f(l_run);
     }
   }
   tc_fence_before();
@@ -332,10 +327,17 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm, Params p) {
 // With two S/dP buffers the tensor core computes S_{k+1} while the softmax
 // warps work on k, and the dV/dK update of k-1 overlaps the softmax of k.
 constexpr int kBwdStages = 2;
+// as in the forward: four softmax warps per TMEM lane quarter, each taking 16
+// of a 64-column sub-block, 16 softmax warps in all
+constexpr int kBwdSplit = 4;
+constexpr int kBwdSoft = 128 * kBwdSplit;
+constexpr int kBwdThreads = 64 + kBwdSoft;
+constexpr int kBwdCols = 64 / kBwdSplit;              // columns of a sub-block per softmax warp
+constexpr int kBwdOut = D / kBwdSplit;                // dK / dV / dQ columns per softmax warp in the epilogue
 constexpr int kDkdvSmem = 1024 + 2 * kTile /*K,V*/ + 2 * kBwdStages * kTile /*Q,dO*/ + 4 * kTile /*P^T,dS^T x2*/ +
                           2 * BM * 4 * 2 /*lse,delta*/ + 256;
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kBwdThreads, 1)
 dkdv_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtensorMap tmo, Params p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -364,9 +366,9 @@ dkdv_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUte
   // critical path (it meets every later query block of every head of its
   // group); with hsplit > 1 the group's query heads are spread over hsplit
   // CTAs whose fp32 partials are summed in a fixed order afterwards.
-  const int kb = blockIdx.x, kvh = blockIdx.y / p.hsplit, part = blockIdx.y % p.hsplit, b = blockIdx.z;
+  const int kb = blockIdx.x, kvh = blockIdx.y / p.hsplit, part_h = blockIdx.y % p.hsplit, b = blockIdx.z;
   const int group = p.Hq / p.Hkv / p.hsplit;     // query heads handled by this CTA
-  const int h_first = kvh * (p.Hq / p.Hkv) + part * group;
+  const int h_first = kvh * (p.Hq / p.Hkv) + part_h * group;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int k0 = kb * BN;
   const int tok0 = b * p.S;
@@ -383,8 +385,8 @@ dkdv_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUte
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sdp_full[i], 1);
-      mbar_init(&sdp_empty[i], kSoftThreads);
-      mbar_init(&ds_full[i], kSoftThreads);
+      mbar_init(&sdp_empty[i], kBwdSoft);
+      mbar_init(&ds_full[i], kBwdSoft);
       mbar_init(&pds_empty[i], 1);
     }
     mbar_init(acc_done, 1);
@@ -463,11 +465,11 @@ dkdv_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUte
     }
   } else {
     const int quarter = warp % 4;
-    const int half = (warp - 2) / 4;         // columns [32*half, +32) of a 64-query sub-block; of dK/dV
+    const int part = (warp - 2) / 4;         // columns [16*part, +16) of a 64-query sub-block; of dK/dV
     const int row = quarter * 32 + lane;     // key row within the block
     const int key = k0 + row;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    const int sm_tid = threadIdx.x - 64;     // 0..255
+    const int sm_tid = threadIdx.x - 64;     // 0..kBwdSoft-1
     bool ok = true;
     // lse / delta of the 128-query block of iteration it live in buffer it & 1;
     // the next iteration's values are loaded into registers during the
@@ -483,7 +485,7 @@ dkdv_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUte
       s_lse[sm_tid] = p.lse[li_of(0)];
       s_del[sm_tid] = p.delta[li_of(0)];
     }
-    named_bar(1, kSoftThreads);
+    named_bar(1, kBwdSoft);
     for (int it = 0; it < n_it; ++it) {
       const int qb = kb + it % per_head;
       const int buf = it & 1;
@@ -501,20 +503,20 @@ dkdv_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUte
         if (ok && !mbar_wait(&sdp_full[k & 1], (k >> 1) & 1, p.status)) ok = false;
         if (!ok) continue;
         tc_fence_after();
-        uint32_t vs[32], vd[32];
-        tmem_ld_32x32b_x32(tS0 + (k & 1) * 64 + half * 32 + lane_off, vs);
-        tmem_ld_32x32b_x32(tdP0 + (k & 1) * 64 + half * 32 + lane_off, vd);
+        uint32_t vs[kBwdCols], vd[kBwdCols];
+        tmem_ld_32x32b_x16(tS0 + (k & 1) * 64 + part * kBwdCols + lane_off, vs);
+        tmem_ld_32x32b_x16(tdP0 + (k & 1) * 64 + part * kBwdCols + lane_off, vd);
         tmem_wait_ld();
         tc_fence_before();
         mbar_arrive(&sdp_empty[k & 1]);                 // S/dP buffer may be overwritten by S_{k+2}
-        const int c0 = hh * 64 + half * 32;             // column of the 128-query block
-        float pt[32], dst[32];
-        // lse / delta of the 32 queries: eight 16-byte broadcast loads each
-        // (c0 is a multiple of 32 floats; the arrays start 1024-byte aligned)
+        const int c0 = hh * 64 + part * kBwdCols;       // column of the 128-query block
+        float pt[kBwdCols], dst[kBwdCols];
+        // lse / delta of the 16 queries: four 16-byte broadcast loads each
+        // (c0 is a multiple of 16 floats; the arrays start 1024-byte aligned)
         const float4* cl4 = reinterpret_cast<const float4*>(cl + c0);
         const float4* cd4 = reinterpret_cast<const float4*>(cd + c0);
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
+        for (int u = 0; u < kBwdCols / 4; ++u) {
           const float4 l = cl4[u], d = cd4[u];
           const float la[4] = {l.x, l.y, l.z, l.w}, da[4] = {d.x, d.y, d.z, d.w};
 #pragma unroll
@@ -527,8 +529,8 @@ dkdv_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUte
         }
         if (qb == kb) {             // causal mask only on the diagonal block
 #pragma unroll
-          for (int t = 0; t < 32; ++t)
-            if (key > q0 + half * 32 + t) pt[t] = dst[t] = 0.f;
+          for (int t = 0; t < kBwdCols; ++t)
+            if (key > q0 + part * kBwdCols + t) pt[t] = dst[t] = 0.f;
         }
         if (k >= 2 && !mbar_wait(&pds_empty[k & 1], ((k - 2) >> 1) & 1, p.status)) {
           ok = false;
@@ -537,11 +539,12 @@ dkdv_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUte
         uint8_t* pb = sP + (k & 1) * kTile;
         uint8_t* db = sS + (k & 1) * kTile;
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < kBwdCols / 8; ++u) {
           bf16x8 a = float_to_bf16x8(pt + 8 * u);
           bf16x8 d = float_to_bf16x8(dst + 8 * u);
-          *reinterpret_cast<uint4*>(swz_chunk(pb, row, half * 4 + u)) = make_uint4(a.w[0], a.w[1], a.w[2], a.w[3]);
-          *reinterpret_cast<uint4*>(swz_chunk(db, row, half * 4 + u)) = make_uint4(d.w[0], d.w[1], d.w[2], d.w[3]);
+          const int ch = part * (kBwdCols / 8) + u;
+          *reinterpret_cast<uint4*>(swz_chunk(pb, row, ch)) = make_uint4(a.w[0], a.w[1], a.w[2], a.w[3]);
+          *reinterpret_cast<uint4*>(swz_chunk(db, row, ch)) = make_uint4(d.w[0], d.w[1], d.w[2], d.w[3]);
         }
         fence_proxy_async_smem();
         tc_fence_before();
@@ -551,48 +554,48 @@ dkdv_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUte
         s_lse[(buf ^ 1) * BM + sm_tid] = nl;
         s_del[(buf ^ 1) * BM + sm_tid] = nd;
       }
-      named_bar(1, kSoftThreads);   // next buffer written; everyone done with this one
+      named_bar(1, kBwdSoft);   // next buffer written; everyone done with this one
     }
     if (ok && p.hsplit > 1 && mbar_wait(acc_done, 0, p.status)) {
       tc_fence_after();
-      uint32_t v[32];
-      float* wrow = p.ws + ((((static_cast<long>(b) * p.Hkv + kvh) * p.hsplit + part) * p.S) + key) * (2 * D);
+      uint32_t v[kBwdOut];
+      float* wrow = p.ws + ((((static_cast<long>(b) * p.Hkv + kvh) * p.hsplit + part_h) * p.S) + key) * (2 * D);
       {
-        const int c = half * 32;
-        tmem_ld_32x32b_x32(tdK + c + lane_off, v);
+        const int c = part * kBwdOut;
+        tmem_ld_32x32b_x16(tdK + c + lane_off, v);
         tmem_wait_ld();
 #pragma unroll
-        for (int t = 0; t < 32; t += 4)
+        for (int t = 0; t < kBwdOut; t += 4)
           *reinterpret_cast<float4*>(wrow + c + t) =
               make_float4(__uint_as_float(v[t]) * p.scale, __uint_as_float(v[t + 1]) * p.scale,
                           __uint_as_float(v[t + 2]) * p.scale, __uint_as_float(v[t + 3]) * p.scale);
-        tmem_ld_32x32b_x32(tdV + c + lane_off, v);
+        tmem_ld_32x32b_x16(tdV + c + lane_off, v);
         tmem_wait_ld();
 #pragma unroll
-        for (int t = 0; t < 32; t += 4)
+        for (int t = 0; t < kBwdOut; t += 4)
           *reinterpret_cast<float4*>(wrow + D + c + t) = make_float4(
               __uint_as_float(v[t]), __uint_as_float(v[t + 1]), __uint_as_float(v[t + 2]), __uint_as_float(v[t + 3]));
       }
     } else if (ok && mbar_wait(acc_done, 0, p.status)) {
       tc_fence_after();
-      uint32_t v[32];
+      uint32_t v[kBwdOut];
       __nv_bfloat16* krow = p.dqkv + static_cast<long>(tok0 + key) * p.dqkv_stride + (p.Hq + kvh) * D;
       __nv_bfloat16* vrow = p.dqkv + static_cast<long>(tok0 + key) * p.dqkv_stride + (p.Hq + p.Hkv + kvh) * D;
       {
-        const int c = half * 32;
-        float f[32];
-        tmem_ld_32x32b_x32(tdK + c + lane_off, v);
+        const int c = part * kBwdOut;
+        float f[kBwdOut];
+        tmem_ld_32x32b_x16(tdK + c + lane_off, v);
         tmem_wait_ld();
 #pragma unroll
-        for (int t = 0; t < 32; ++t) f[t] = __uint_as_float(v[t]) * p.scale;
+        for (int t = 0; t < kBwdOut; ++t) f[t] = __uint_as_float(v[t]) * p.scale;
 #pragma unroll
-        for (int u = 0; u < 4; ++u) reinterpret_cast<bf16x8*>(krow + c)[u] = float_to_bf16x8(f + 8 * u);
-        tmem_ld_32x32b_x32(tdV + c + lane_off, v);
+        for (int u = 0; u < kBwdOut / 8; ++u) reinterpret_cast<bf16x8*>(krow + c)[u] = float_to_bf16x8(f + 8 * u);
+        tmem_ld_32x32b_x16(tdV + c + lane_off, v);
         tmem_wait_ld();
 #pragma unroll
-        for (int t = 0; t < 32; ++t) f[t] = __uint_as_float(v[t]);
+        for (int t = 0; t < kBwdOut; ++t) f[t] = __uint_as_float(v[t]);
 #pragma unroll
-        for (int u = 0; u < 4; ++u) reinterpret_cast<bf16x8*>(vrow + c)[u] = float_to_bf16x8(f + 8 * u);
+        for (int u = 0; u < kBwdOut / 8; ++u) reinterpret_cast<bf16x8*>(vrow + c)[u] = float_to_bf16x8(f + 8 * u);
       }
     }
   }
@@ -609,7 +612,7 @@ dkdv_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUte
 //   dQ += dS_k K_k (TMEM accumulator)
 constexpr int kDqSmem = 1024 + 2 * kTile /*Q,dO*/ + 2 * kBwdStages * kTile /*K,V*/ + 2 * kTile /*dS x2*/ + 256;
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kBwdThreads, 1)
 dq_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtensorMap tmo, Params p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -647,8 +650,8 @@ dq_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtens
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sdp_full[i], 1);
-      mbar_init(&sdp_empty[i], kSoftThreads);
-      mbar_init(&ds_full[i], kSoftThreads);
+      mbar_init(&sdp_empty[i], kBwdSoft);
+      mbar_init(&ds_full[i], kBwdSoft);
       mbar_init(&ds_empty[i], 1);
     }
     mbar_init(acc_done, 1);
@@ -719,7 +722,7 @@ dq_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtens
     }
   } else {
     const int quarter = warp % 4;
-    const int half = (warp - 2) / 4;          // columns [32*half, +32) of a 64-key sub-block; of dQ
+    const int part = (warp - 2) / 4;          // columns [16*part, +16) of a 64-key sub-block; of dQ
     const int row = quarter * 32 + lane;
     const int q = q0 + row;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
@@ -734,20 +737,20 @@ dq_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtens
         break;
       }
       tc_fence_after();
-      uint32_t vs[32], vd[32];
-      tmem_ld_32x32b_x32(tS0 + (k & 1) * 64 + half * 32 + lane_off, vs);
-      tmem_ld_32x32b_x32(tdP0 + (k & 1) * 64 + half * 32 + lane_off, vd);
+      uint32_t vs[kBwdCols], vd[kBwdCols];
+      tmem_ld_32x32b_x16(tS0 + (k & 1) * 64 + part * kBwdCols + lane_off, vs);
+      tmem_ld_32x32b_x16(tdP0 + (k & 1) * 64 + part * kBwdCols + lane_off, vd);
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(&sdp_empty[k & 1]);
-      float ds[32];
+      float ds[kBwdCols];
 #pragma unroll
-      for (int t = 0; t < 32; ++t)
+      for (int t = 0; t < kBwdCols; ++t)
         ds[t] = ex2(fmaf(__uint_as_float(vs[t]), p.scale_log2, nlse)) * (__uint_as_float(vd[t]) - del);
       if (j == qb) {             // causal mask only on the diagonal block
-        const int key0 = j * BN + hh * 64 + half * 32;
+        const int key0 = j * BN + hh * 64 + part * kBwdCols;
 #pragma unroll
-        for (int t = 0; t < 32; ++t)
+        for (int t = 0; t < kBwdCols; ++t)
           if (key0 + t > q) ds[t] = 0.f;
       }
       if (k >= 2 && !mbar_wait(&ds_empty[k & 1], ((k - 2) >> 1) & 1, p.status)) {
@@ -756,9 +759,10 @@ dq_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtens
       }
       uint8_t* db = sS + (k & 1) * kTile;
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < kBwdCols / 8; ++u) {
         bf16x8 d = float_to_bf16x8(ds + 8 * u);
-        *reinterpret_cast<uint4*>(swz_chunk(db, row, half * 4 + u)) = make_uint4(d.w[0], d.w[1], d.w[2], d.w[3]);
+        *reinterpret_cast<uint4*>(swz_chunk(db, row, part * (kBwdCols / 8) + u)) =
+            make_uint4(d.w[0], d.w[1], d.w[2], d.w[3]);
       }
       fence_proxy_async_smem();
       tc_fence_before();
@@ -766,17 +770,17 @@ dq_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtens
     }
     if (ok && mbar_wait(acc_done, 0, p.status)) {
       tc_fence_after();
-      uint32_t v[32];
+      uint32_t v[kBwdOut];
       __nv_bfloat16* qrow = p.dqkv + static_cast<long>(tok0 + q) * p.dqkv_stride + h * D;
       {
-        const int c = half * 32;
-        float f[32];
-        tmem_ld_32x32b_x32(tdQ + c + lane_off, v);
+        const int c = part * kBwdOut;
+        float f[kBwdOut];
+        tmem_ld_32x32b_x16(tdQ + c + lane_off, v);
         tmem_wait_ld();
 #pragma unroll
-        for (int t = 0; t < 32; ++t) f[t] = __uint_as_float(v[t]) * p.scale;
+        for (int t = 0; t < kBwdOut; ++t) f[t] = __uint_as_float(v[t]) * p.scale;
 #pragma unroll
-        for (int u = 0; u < 4; ++u) reinterpret_cast<bf16x8*>(qrow + c)[u] = float_to_bf16x8(f + 8 * u);
+        for (int u = 0; u < kBwdOut / 8; ++u) reinterpret_cast<bf16x8*>(qrow + c)[u] = float_to_bf16x8(f + 8 * u);
       }
     }
   }
@@ -908,7 +912,7 @@ std::vector<at::Tensor> fwd(const at::Tensor& qkv, int64_t B, int64_t S, int64_t
     cfg = true;
   }
   dim3 grid(static_cast<unsigned>(S / BM), static_cast<unsigned>(Hq), static_cast<unsigned>(B));
-  fwd_kernel<<<grid, kFwdThreads, kFwdSmem, at::cuda::getCurrentCUDAStream()>>>(tm, p);
+  fwd_kernel<<<grid, kThreads, kFwdSmem, at::cuda::getCurrentCUDAStream()>>>(tm, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return {o, lse};
 }
@@ -952,14 +956,14 @@ at::Tensor bwd(const at::Tensor& qkv, const at::Tensor& o, const at::Tensor& lse
     p.ws = ws.data_ptr<float>();
   }
   dim3 g1(static_cast<unsigned>(S / BN), static_cast<unsigned>(Hkv * hs), static_cast<unsigned>(B));
-  dkdv_kernel<<<g1, kThreads, kDkdvSmem, stream>>>(tm, tmo, p);
+  dkdv_kernel<<<g1, kBwdThreads, kDkdvSmem, stream>>>(tm, tmo, p);
   if (hs > 1) {
     const long total = B * Hkv * S * (2 * D / 8);
     dkdv_reduce_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(
         p.ws, (int)B, (int)S, (int)Hq, (int)Hkv, hs, p.dqkv, p.dqkv_stride);
   }
   dim3 g2(static_cast<unsigned>(S / BM), static_cast<unsigned>(Hq), static_cast<unsigned>(B));
-  dq_kernel<<<g2, kThreads, kDqSmem, stream>>>(tm, tmo, p);
+  dq_kernel<<<g2, kBwdThreads, kDqSmem, stream>>>(tm, tmo, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return dqkv;
 }

@@ -48,11 +48,33 @@ def pick_bn(n: int, tiles_m: int | None = None, sms: int = _SMS) -> int:
     return best
 
 
+def pick_bn_split_k(n: int, tiles_m: int, k: int, sms: int = _SMS) -> int:
+    """Tile width for a dense weight gradient, which the kernel entry splits
+    along K into S = min(sms // tiles, k // 1024) slices when the output has
+    few tiles: the width is chosen for the filled fraction of the grid after
+    that split (wide tiles split further and keep their higher mainloop
+    efficiency, where the padding-only rule above prefers narrow ones)."""
+    best, score = 256, -1.0
+    for bn in (256, 192, 128):
+        tn = -(-n // bn)
+        tiles = tiles_m * tn
+        split = max(1, min(sms // max(tiles, 1), k // 1024))
+        ctas = tiles * split
+        fill = ctas / (-(-ctas // sms) * sms)
+        s = n / (tn * bn) * _BN_COST[bn] * fill * (0.98 ** (split - 1))   # each slice adds a reduction pass
+        if s > score + 1e-9:
+            best, score = bn, s
+    return best
+
+
 def _run(A, B, D, D2, offs, M, N, K, G, mode, a_mn, b_mn, epi, alpha, max_rows, xchg=(), tp=()):
     tiles_m = -(-max_rows // 128) if mode == ROW_GROUPS else G * -(-M // 128)
     if mode == ROW_GROUPS and G > 1:
         tiles_m = None                  # grouped: the row split is data dependent
-    bn = pick_bn(N, tiles_m)
+    if mode == K_GROUPS and G == 1 and offs is None and epi != EPI_SWIGLU and not (xchg and xchg[2]):
+        bn = pick_bn_split_k(N, tiles_m, K)
+    else:
+        bn = pick_bn(N, tiles_m)
     if epi == EPI_SWIGLU and bn == 256 and N % 192 == 0:
         bn = 192                        # the SwiGLU activation is staged for TMA stores below 256
     ext().gemm(A, B, D, D2, offs, M, N, K, G, mode, a_mn, b_mn, epi, float(alpha), bn,

@@ -35,7 +35,9 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <cstdlib>
 #include <mutex>
+#include <string>
 
 #include "common.cuh"
 
@@ -94,6 +96,16 @@ constexpr int kFwdStages = 2;
 constexpr int kFwdSmem = 1024 + kTile /*Q*/ + 2 * kFwdStages * kTile /*K,V*/ + 2 * 2 * kTile /*P x2*/ + 256 +
                          (2 * 2 * 128 + 2 * 128) * 4 /*row max / sum exchange*/;
 
+// kTmemO: O accumulates in TMEM across the key blocks and the softmax warps
+// keep a running row max that may be stale by up to 2^kRescaleLog2: O (and the
+// row sum) are rescaled in place only when a row's max rises by more than
+// that, which on these shapes happens in the first blocks of a row and rarely
+// after, so the common block costs no TMEM read of O and no rescale FMAs.
+// Otherwise (kTmemO false) every block's P V lands in a fresh TMEM block that
+// the softmax warps fold into registers with the running rescale.
+constexpr float kRescaleLog2 = 8.f;
+
+template <bool kTmemO>
 __global__ void __launch_bounds__(kThreads, 1)
 fwd_kernel(const __grid_constant__ CUtensorMap tm, Params p) {
   extern __shared__ uint8_t smem_raw[];
@@ -187,13 +199,139 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm, Params p) {
         const uint32_t va = smem_u32(sV + st * kTile);
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk)
-          umma_f16(tbase + 256 + (j & 1) * D, kdesc(pa + (kk >> 2) * kTile + (kk & 3) * 32), mndesc(va + kk * 2048),
-                   idO, kk > 0);
+          umma_f16(kTmemO ? tbase + 256 : tbase + 256 + (j & 1) * D,
+                   kdesc(pa + (kk >> 2) * kTile + (kk & 3) * 32), mndesc(va + kk * 2048), idO,
+                   kTmemO ? (j > 0 || kk > 0) : kk > 0);
         umma_commit(&o_full[j & 1]);
         umma_commit(&kv_empty[st]);
       }
       umma_commit(drain);
       mbar_wait(drain, 0, p.status);
+    }
+  } else if (kTmemO) {
+    // -------------------- softmax, O accumulated in TMEM --------------------
+    const int quarter = warp % 4;
+    const int half = (warp - 2) / 4;          // columns [64*half, 64*half+64) of S, [32*half, +32) of O
+    const int row = quarter * 32 + lane;
+    const int q = q0 + row;
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const int pair_bar = 1 + quarter;
+    const uint32_t to = tbase + 256 + half * 32 + lane_off;   // this warp's 32 columns of O
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      if (ok && !mbar_wait(&s_full[j & 1], (j >> 1) & 1, p.status)) ok = false;
+      ok = __all_sync(0xffffffffu, ok);       // warp-uniform before the warp-collective TMEM accesses
+      if (ok) tc_fence_after();
+      const uint32_t ts = tbase + (j & 1) * BN + lane_off;
+      const bool diag = (j == qb);
+      uint32_t v[64];
+      float mraw = -INFINITY;
+      const int c_lo = half * 64;
+      if (ok) {
+        tmem_ld_32x32b_x32(ts + c_lo, v);
+        tmem_ld_32x32b_x32(ts + c_lo + 32, v + 32);
+        tmem_wait_ld();
+        float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        if (diag) {
+          const int lim = q - j * BN - c_lo;
+#pragma unroll
+          for (int t = 0; t < 64; ++t)
+            if (t <= lim) m4[t & 3] = fmaxf(m4[t & 3], __uint_as_float(v[t]));
+        } else {
+#pragma unroll
+          for (int t = 0; t < 64; ++t) m4[t & 3] = fmaxf(m4[t & 3], __uint_as_float(v[t]));
+        }
+        mraw = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+      }
+      float mx = fmaxf(m_run, mraw * p.scale_log2);
+      s_max[((j & 1) * 2 + half) * BM + row] = mx;
+      named_bar(pair_bar, 64);
+      if (!ok) continue;
+      mx = fmaxf(mx, s_max[((j & 1) * 2 + (half ^ 1)) * BM + row]);
+      // the two warps of a pair hold the same rows and maxima, so they take the
+      // same branch; each rescales its own 32 columns of O
+      bool waited_prev = false;
+      if (__any_sync(0xffffffffu, mx > m_run + kRescaleLog2)) {
+        if (j > 0) {
+          // O must hold every earlier block before it is read and rewritten
+          if (!__all_sync(0xffffffffu, mbar_wait(&o_full[(j - 1) & 1], ((j - 1) >> 1) & 1, p.status))) {
+            ok = false;
+            continue;
+          }
+          waited_prev = true;
+          tc_fence_after();
+          const float a = ex2(m_run - mx);
+          uint32_t o[32];
+          tmem_ld_32x32b_x32(to, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int t = 0; t < 32; ++t) o[t] = __float_as_uint(__uint_as_float(o[t]) * a);
+          tmem_st_32x32b_x16(to, o);
+          tmem_st_32x32b_x16(to + 16, o + 16);
+          tmem_wait_st();
+          l_run *= a;
+        }
+        m_run = mx;
+      }
+      // this block's P buffer was last read by the PV product of block j - 2
+      if (j >= 2 && !waited_prev &&
+          !__all_sync(0xffffffffu, mbar_wait(&o_full[j & 1], ((j - 2) >> 1) & 1, p.status))) {
+        ok = false;
+        continue;
+      }
+      uint8_t* pbuf = sP + (j & 1) * 2 * kTile;
+      const float nmx = -m_run;
+      float l4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        float pr[32];
+        if (diag) {
+          const int lim = q - j * BN - c_lo - cc * 32;
+#pragma unroll
+          for (int t = 0; t < 32; ++t) {
+            pr[t] = (t > lim) ? 0.f : ex2(fmaf(__uint_as_float(v[cc * 32 + t]), p.scale_log2, nmx));
+            l4[t & 3] += pr[t];
+          }
+        } else {
+#pragma unroll
+          for (int t = 0; t < 32; ++t) {
+            pr[t] = ex2(fmaf(__uint_as_float(v[cc * 32 + t]), p.scale_log2, nmx));
+            l4[t & 3] += pr[t];
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          bf16x8 pk = float_to_bf16x8(pr + 8 * u);
+          *reinterpret_cast<uint4*>(swz_chunk(pbuf, row, ((c_lo + cc * 32) >> 3) + u)) =
+              make_uint4(pk.w[0], pk.w[1], pk.w[2], pk.w[3]);
+        }
+      }
+      l_run += (l4[0] + l4[1]) + (l4[2] + l4[3]);
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&p_full[j & 1]);
+    }
+    s_sum[half * BM + row] = l_run;
+    named_bar(pair_bar, 64);
+    l_run += s_sum[(half ^ 1) * BM + row];
+    if (ok) ok = mbar_wait(&o_full[(n_kv - 1) & 1], ((n_kv - 1) >> 1) & 1, p.status);
+    ok = __all_sync(0xffffffffu, ok);
+    if (ok) {
+      tc_fence_after();
+      uint32_t o[32];
+      tmem_ld_32x32b_x32(to, o);
+      tmem_wait_ld();
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      __nv_bfloat16* orow = p.o + static_cast<long>(tok0 + q) * p.o_stride + h * D + half * 32;
+#pragma unroll
+      for (int c = 0; c < 32; c += 8) {
+        float t8[8];
+#pragma unroll
+        for (int t = 0; t < 8; ++t) t8[t] = __uint_as_float(o[c + t]) * inv;
+        *reinterpret_cast<bf16x8*>(orow + c) = float_to_bf16x8(t8);
+      }
+      if (half == 0) p.lse[(static_cast<long>(b) * p.Hq + h) * p.S + q] = m_run + log2f(l_run);
     }
   } else {
     // ----------------------------- softmax -----------------------------
@@ -907,12 +1045,19 @@ std::vector<at::Tensor> fwd(const at::Tensor& qkv, int64_t B, int64_t S, int64_t
   p.lse = lse.data_ptr<float>();
   CUtensorMap tm = tile_map(qkv.data_ptr(), B * S, qkv.size(-1), qkv.stride(-2));
   static bool cfg = false;
+  // SHIFT_ATTN_FWD=fold selects the register-fold form of the forward
+  static const bool tmem_o = [] {
+    const char* e = std::getenv("SHIFT_ATTN_FWD");
+    return e == nullptr || std::string(e) != "fold";
+  }();
   if (!cfg) {
-    cudaFuncSetAttribute(fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem);
+    cudaFuncSetAttribute(fwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem);
+    cudaFuncSetAttribute(fwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem);
     cfg = true;
   }
   dim3 grid(static_cast<unsigned>(S / BM), static_cast<unsigned>(Hq), static_cast<unsigned>(B));
-  fwd_kernel<<<grid, kThreads, kFwdSmem, at::cuda::getCurrentCUDAStream()>>>(tm, p);
+  if (tmem_o) fwd_kernel<true><<<grid, kThreads, kFwdSmem, at::cuda::getCurrentCUDAStream()>>>(tm, p);
+  else fwd_kernel<false><<<grid, kThreads, kFwdSmem, at::cuda::getCurrentCUDAStream()>>>(tm, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return {o, lse};
 }

@@ -156,11 +156,10 @@ class PlannedWorker(Worker):
             transport = PackedTransport(pg, self.device if backend == "nccl" else torch.device("cpu"),
                                         timedelta(seconds=a.communication_timeout), self.event)
         rid = self.logical_rid
-        store_port = int(os.environ.get("SHIFT_STORE_PORT", "0"))
-        store_port = (store_port + 100 * (epoch + 1) + 7 * (members == "AB")) if store_port else _free_port()
+        store, store_addr = self.manager_store(epoch, members)
         m = Manager(pg, self.load_state_for_manager, self.export_state_for_transport, 2, f"shift{rid}",
                     f"{a.lighthouse_host}:{port}", rank=self.rank, world_size=self.local_world,
-                    store_addr=f"{a.host_ip}:{store_port}", hostname=a.host_ip, checkpoint_transport=transport,
+                    store_addr=store_addr, store=store, hostname=a.host_ip, checkpoint_transport=transport,
                     timeout=timedelta(seconds=a.communication_timeout),
                     world_size_mode=WorldSizeMode.FIXED_WITH_SPARES, event=self.event)
         m._shift_epoch = epoch
@@ -172,6 +171,32 @@ class PlannedWorker(Worker):
             if activate:
                 self.manager = m
         return m
+
+    def manager_store(self, epoch: int, members: str):
+        """(store, address) of the replica-local store of one epoch's Manager.
+        Rank 0 lets the OS pick the port (a port computed ahead can be taken
+        by then: every rank's process groups open sockets of their own); with
+        several local ranks the port travels through the replica's own
+        process-group store."""
+        import torch.distributed as dist
+        a = self.args
+        t = timedelta(seconds=a.communication_timeout)
+        key = f"planned_manager_store/{epoch}/{members}"
+        shared = self.local_world > 1
+        if shared and not dist.is_initialized():
+            # no replica-local group to publish through: ports derived from the session's base
+            base = int(os.environ.get("SHIFT_STORE_PORT", "0"))
+            port = (base + 100 * (epoch + 1) + 7 * (members == "AB")) if base else _free_port()
+            return None, f"{a.host_ip}:{port}"
+        if self.rank == 0:
+            store = dist.TCPStore(a.host_ip, 0, None, True, timeout=t, wait_for_workers=False)
+            port = store.port
+            if shared:
+                dist.distributed_c10d._get_default_store().set(key, str(port))
+        else:
+            port = int(dist.distributed_c10d._get_default_store().get(key))
+            store = dist.TCPStore(a.host_ip, port, None, False, timeout=t)
+        return store, f"{a.host_ip}:{port}"
 
     def load_state(self, payload):
         if payload.get("_inplace"):

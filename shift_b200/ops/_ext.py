@@ -9,6 +9,7 @@ the tests and the compute path of the CPU/gloo harness.
 from __future__ import annotations
 
 import importlib
+import os
 import threading
 
 import torch
@@ -17,6 +18,11 @@ _lock = threading.Lock()
 _mod = None
 _err: Exception | None = None
 _status: dict[int, torch.Tensor] = {}
+
+
+# forward attention form: "fold" (per-block O folded into registers) until the
+# TMEM-accumulated form has passed its B200 tests; SHIFT_ATTN_FWD=tmem selects it
+os.environ.setdefault("SHIFT_ATTN_FWD", "fold")
 
 
 def ext():

@@ -188,6 +188,35 @@ def test_attention_fwd_bwd(B, S, Hq, Hkv):
     _close(dqkv, g, tol=3e-2)
 
 
+def test_attention_fwd_rescales_when_row_maxima_grow():
+    """Keys scaled up along the sequence make later key blocks raise a row's
+    maximum by far more than 2^8 (log2 units), so the forward's stale-max
+    rescale of O and the row sum runs on many blocks; O and the log-sum-exp
+    must still match fp32."""
+    torch.manual_seed(11)
+    B, S, Hq, Hkv, D = 2, 1024, 4, 2, 64
+    T = B * S
+    qkv = torch.randn(T, (Hq + 2 * Hkv) * D, device="cuda")
+    pos = torch.arange(S, device="cuda").repeat(B).float()
+    qkv[:, Hq * D:(Hq + Hkv) * D] *= (1.0 + 12.0 * pos / S)[:, None]
+    qkv = qkv.to(torch.bfloat16)
+    scale = 1 / math.sqrt(D)
+    o, lse = Fn.attention_fwd(qkv, B, S, Hq, Hkv, D, scale)
+    x = qkv.float()
+    q = x[:, : Hq * D].view(B, S, Hq, D).transpose(1, 2)
+    k = x[:, Hq * D:(Hq + Hkv) * D].view(B, S, Hkv, D).transpose(1, 2).repeat_interleave(Hq // Hkv, 1)
+    v = x[:, (Hq + Hkv) * D:].view(B, S, Hkv, D).transpose(1, 2).repeat_interleave(Hq // Hkv, 1)
+    sc = (q @ k.transpose(-1, -2)) * scale
+    sc = sc.masked_fill(torch.triu(torch.ones(S, S, dtype=torch.bool, device="cuda"), 1), float("-inf"))
+    ref_lse = torch.logsumexp(sc, -1) / math.log(2.0)                 # base 2, as the kernel stores it
+    ref_o = (torch.softmax(sc, -1) @ v).transpose(1, 2).reshape(T, Hq * D)
+    # within a row, the later key blocks raise the maximum over the first block by > 8 in log2 units
+    growth = (sc.amax(-1) - sc[..., :128].amax(-1)) / math.log(2.0)
+    assert float(growth[..., S // 2:].amax()) > 8.0
+    _close(o, ref_o)
+    assert float((lse - ref_lse).abs().max()) < 2e-2 * float(ref_lse.abs().max())
+
+
 # ----------------------------------------------------------------------------- MoE plumbing
 def test_router_sort_gather_combine():
     torch.manual_seed(8)

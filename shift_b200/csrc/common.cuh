@@ -331,6 +331,10 @@ SB_DEVICE int ld_acquire_sys(const volatile int* p) {
 // Bounded wait until *flag >= target.  Returns false on timeout.
 SB_DEVICE bool wait_flag_ge(const volatile int* flag, int target, int* status, uint64_t timeout_ns) {
   if (ld_acquire_sys(flag) >= target) return true;
+  // a peer wait of this step already ran out (the host clears the word after
+  // every step): the step is lost, so do not spend another full bound here --
+  // a dead peer would otherwise cost one timeout per bucket / exchange
+  if (status != nullptr && *reinterpret_cast<volatile int*>(status) == kTimeoutPeer) return false;
   const uint64_t start = globaltimer_ns();
   while (true) {
     if (ld_acquire_sys(flag) >= target) return true;

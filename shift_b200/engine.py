@@ -153,11 +153,13 @@ class Engine:
             # bucket-completion hooks fire only while the last microbatch's
             # backward writes the final gradients
             self.model.layer_done_hook = hook if mb == len(batches) - 1 else None
+            self.model._last_microbatch = mb == len(batches) - 1
             self.model.backward()
             self.model._accumulate = True
             total = loss if total is None else total + loss
         self.model.layer_done_hook = hook
         self.model._accumulate = False
+        self.model._last_microbatch = True
         return total / n_tok
 
     def optimizer_step(self, grad_sources: list | None = None, grad_scale: float = 1.0, prepared: bool = False):

@@ -179,6 +179,7 @@ class MPWorker(Worker):
 
         def bwd(j, dout):
             model._accumulate = j > 0
+            model._last_microbatch = j == M - 1
             if j == M - 1 and self._kill_now(step):
                 model.layer_done_hook = self._die
             d = model.backward(None if dout is None else dout[0])

@@ -489,13 +489,19 @@ class Worker:
         self.event.close()
 
     # ------------------------------------------------------------------ disk checkpoint baseline
+    def checkpoint_path(self) -> Path:
+        """One file per replica and rank (the replicas of a session share its directory)."""
+        return self.out / f"checkpoint_rid{self.args.replica}_r{self.rank}.pt"
+
     def save_checkpoint(self):
         t0 = time.monotonic()
         payload = cpu_tree(self.export_state())
-        path = self.out / f"checkpoint_r{self.rank}.pt"
-        torch.save(payload, path)
-        with path.open("rb") as h:
+        path = self.checkpoint_path()
+        tmp = path.with_name(path.name + f".tmp{os.getpid()}")
+        torch.save(payload, tmp)
+        with tmp.open("rb") as h:
             os.fsync(h.fileno())
+        os.replace(tmp, path)          # replicas share the session directory: write whole files only
         self.event("checkpoint_saved", step=self.progress["updates"], seconds=time.monotonic() - t0,
                    bytes=path.stat().st_size)
         t1 = time.monotonic()
@@ -514,7 +520,7 @@ class Worker:
                        cache="fadvise_dontneed_advisory")
 
     def resume(self):
-        path = self.out / f"checkpoint_r{self.rank}.pt"
+        path = self.checkpoint_path()
         t0 = time.monotonic()
         payload = torch.load(path, weights_only=False)
         self.engine.load_state_dict(_to_device(payload, self.device))

@@ -366,11 +366,16 @@ class QwenMoE:
             tok = saved["tokens"]
             gE = st.g("embed.weight")
             if dres.is_cuda:
-                dW32 = torch.zeros(gE.shape, dtype=torch.float32, device=gE.device)
-                if accumulate:
-                    dW32.copy_(gE)
-                Fn.embedding_bwd(dres, tok, dW32)
-                gE.copy_(dW32)
+                # fp32 accumulator kept across the microbatches of a step and
+                # rounded into the bf16 gradient once, after the last one
+                acc = getattr(self, "_emb_acc", None)
+                if acc is None or acc.shape != gE.shape:
+                    acc = self._emb_acc = torch.zeros(gE.shape, dtype=torch.float32, device=gE.device)
+                if not accumulate:
+                    acc.zero_()
+                Fn.embedding_bwd(dres, tok, acc)
+                if getattr(self, "_last_microbatch", True):
+                    gE.copy_(acc)
             else:
                 if not accumulate:
                     gE.zero_()

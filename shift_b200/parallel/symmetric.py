@@ -121,7 +121,12 @@ class CrossReplicaFused:
         self.step = 0
         self.launched: set[int] = set()
         self.active = False
-        self.overlap_blocks_per_sm = int(os.environ.get("SHIFT_K1_OVERLAP_BLOCKS", "1"))
+        # blocks per SM of the launches during backward (0 = the whole GPU).  One
+        # block per SM lets the reduction co-reside with the compute kernels,
+        # but measured slower on two B200s (24.5 vs 21.9 ms per step): the
+        # stretched reduction competes for HBM with the memory-bound parts of
+        # backward for longer than the short full-GPU bursts stall it
+        self.overlap_blocks_per_sm = int(os.environ.get("SHIFT_K1_OVERLAP_BLOCKS", "0"))
 
     # ------------------------------------------------------------------ membership
     def configure(self, owners_in_replica_order: list[str], participating: list[bool] | None = None,
@@ -227,10 +232,9 @@ class CrossReplicaFused:
         self.launched.add(b)
 
     def _grid(self) -> int:
-        """Blocks per SM of a reduction launch: one while backward is still
-        running (the memory-bound reduction then shares every SM with the
-        compute kernels instead of holding the GPU until the bucket is done),
-        the whole GPU for buckets launched after backward."""
+        """Blocks per SM of a reduction launch: ``overlap_blocks_per_sm`` while
+        backward is still running, the whole GPU for buckets launched after
+        backward."""
         return self.overlap_blocks_per_sm if self.active else 0
 
     def _sliced(self, srcs) -> bool:

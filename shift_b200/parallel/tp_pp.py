@@ -185,6 +185,7 @@ class ModelParallelRunner:
         self._slot(i)
         model = self.engine.model
         model._accumulate = i > 0
+        model._last_microbatch = i == self.M - 1
         model.layer_done_hook = self._hook if i == self.M - 1 else None
         d = model.backward(dout)        # the same gradient reaches both halves of the stage input pair
         model.layer_done_hook = None

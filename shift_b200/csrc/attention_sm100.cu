@@ -91,6 +91,22 @@ SB_DEVICE uint64_t mndesc(uint32_t addr) { return make_sw128_desc(addr, 8192, 10
 
 SB_DEVICE void named_bar(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
 
+// Work order of the causal grids: a (row block, head, batch) tile's cost grows
+// with its distance from the diagonal, so the launch order is re-mapped to put
+// the costliest blocks of every head and batch first (longest-processing-time
+// first): the last wave then holds the cheap blocks instead of a few long
+// ones, which matters most when B x heads is small (one sequence per
+// pipeline microbatch).  Returns the block index along x, counted from the
+// costliest; y and z are the remaining coordinates.
+SB_DEVICE void lpt_coords(int& costliest_rank, int& y, int& z) {
+  const int yz = gridDim.y * gridDim.z;
+  const int lin = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  costliest_rank = lin / yz;
+  const int r = lin % yz;
+  y = r % gridDim.y;
+  z = r / gridDim.y;
+}
+
 // ============================ forward ============================
 constexpr int kFwdStages = 2;
 constexpr int kFwdSmem = 1024 + kTile /*Q*/ + 2 * kFwdStages * kTile /*K,V*/ + 2 * 2 * kTile /*P x2*/ + 256 +
@@ -129,7 +145,9 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm, Params p) {
   float* s_max = reinterpret_cast<float*>(tslot + 4);
   float* s_sum = s_max + 2 * 2 * BM;
 
-  const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  int rank_x, h, b;
+  lpt_coords(rank_x, h, b);
+  const int qb = gridDim.x - 1 - rank_x;     // query block qb sees qb + 1 key blocks
   const int kvh = h / (p.Hq / p.Hkv);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int q0 = qb * BM;
@@ -504,7 +522,9 @@ dkdv_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUte
   // critical path (it meets every later query block of every head of its
   // group); with hsplit > 1 the group's query heads are spread over hsplit
   // CTAs whose fp32 partials are summed in a fixed order afterwards.
-  const int kb = blockIdx.x, kvh = blockIdx.y / p.hsplit, part_h = blockIdx.y % p.hsplit, b = blockIdx.z;
+  int kb, yy, b;
+  lpt_coords(kb, yy, b);                     // key block kb is seen by S/BM - kb query blocks
+  const int kvh = yy / p.hsplit, part_h = yy % p.hsplit;
   const int group = p.Hq / p.Hkv / p.hsplit;     // query heads handled by this CTA
   const int h_first = kvh * (p.Hq / p.Hkv) + part_h * group;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -772,7 +792,9 @@ dq_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtens
   uint64_t* drain = acc_done + 1;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(drain + 1);
 
-  const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  int rank_x, h, b;
+  lpt_coords(rank_x, h, b);
+  const int qb = gridDim.x - 1 - rank_x;     // query block qb sees qb + 1 key blocks
   const int kvh = h / (p.Hq / p.Hkv);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int q0 = qb * BM;

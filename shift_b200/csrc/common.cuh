@@ -334,10 +334,15 @@ SB_DEVICE bool wait_flag_ge(const volatile int* flag, int target, int* status, u
   // a peer wait of this step already ran out (the host clears the word after
   // every step): the step is lost, so do not spend another full bound here --
   // a dead peer would otherwise cost one timeout per bucket / exchange
-  if (status != nullptr && *reinterpret_cast<volatile int*>(status) == kTimeoutPeer) return false;
+  const volatile int* st = reinterpret_cast<const volatile int*>(status);
+  if (st != nullptr && *st == kTimeoutPeer) return false;
   const uint64_t start = globaltimer_ns();
   while (true) {
     if (ld_acquire_sys(flag) >= target) return true;
+    // the same word is also written from the host (a copy-engine write while
+    // this kernel spins) when a peer process is seen to have died, so a wait on
+    // a dead peer ends within one poll instead of at the bound
+    if (st != nullptr && *st == kTimeoutPeer) return false;
     if (globaltimer_ns() - start > timeout_ns) {
       record_status(status, kTimeoutPeer);
       return false;

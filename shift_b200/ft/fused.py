@@ -24,17 +24,21 @@ import torch
 
 from ..ops._ext import ext
 from ..parallel.symmetric import CrossReplicaFused, SymmetricHeap
+from .peer_watch import PeerWatch
 from .process_group import connect_store
 
 
 class QuorumFusedReducer:
-    def __init__(self, engine, device, replica_id: str, generation: int, rank: int, timeout_s: float = 30.0):
+    def __init__(self, engine, device, replica_id: str, generation: int, rank: int, timeout_s: float = 30.0,
+                 host: str = "127.0.0.1", event=None, peer_watch: bool = True):
         self.owner = f"{replica_id}.g{generation}.r{rank}"
         self.rank = rank
         self.heap = SymmetricHeap(None, self.owner, device)
         self.fused = CrossReplicaFused(engine, self.heap, timeout_s)
         self.quorum_id = None
         self.stores: dict[str, object] = {}
+        # a member's death fails this rank's pending peer waits at once
+        self.watch = PeerWatch(self.owner, self.fused.status, host, event) if peer_watch else None
 
     def reconfigure(self, q, participants: list[int], step: int, timeout: float = 60.0):
         """q: the Manager's QuorumResult; participants: replica ranks at max step."""
@@ -45,6 +49,8 @@ class QuorumFusedReducer:
         self.heap.publish(store)
         key = f"k1/q{q.quorum_id}"
         store.set(f"{key}/{q.replica_rank}/{self.rank}", self.owner)
+        if self.watch is not None:
+            store.set(f"peerwatch/{self.owner}", self.watch.address)
         owners = []
         for rr in range(q.replica_world_size):
             k = f"{key}/{rr}/{self.rank}"
@@ -55,7 +61,18 @@ class QuorumFusedReducer:
                 time.sleep(0.001)
             owners.append(store.get(k).decode())
         self.fused.configure(owners, [rr in participants for rr in range(q.replica_world_size)], step)
+        if self.watch is not None:
+            self.watch.set_members({o: store.get(f"peerwatch/{o}").decode() for o in owners if o != self.owner})
         self.quorum_id = q.quorum_id
+
+    def before_step(self):
+        """Fail the coming step at once if a member is already known dead."""
+        if self.watch is not None:
+            self.watch.check()
+
+    def close(self):
+        if self.watch is not None:
+            self.watch.close()
 
 
 class PeerStateTransport:

@@ -82,7 +82,7 @@ class PlannedWorker(Worker):
             from .fused import QuorumFusedReducer
             a = self.args
             self.reducer = QuorumFusedReducer(self.engine, self.device, self.role, a.generation, self.rank,
-                                              a.communication_timeout)
+                                              a.communication_timeout, host=a.host_ip, event=self.event)
             layers = self.cfg.layers
             from ..parallel.replicas import _order
             self.engine.model.layer_done_hook = lambda layer: self.reducer.fused.on_layer_done(_order(layer, layers))
@@ -345,6 +345,7 @@ class PlannedWorker(Worker):
             fused = getattr(self, "reducer", None) is not None
             if fused:
                 eng.nonfinite.zero_()
+                self.reducer.before_step()
                 self.reducer.fused.begin_step(step, defer=relay)
             t_c = time.monotonic()
             if relay and self.role == "C":

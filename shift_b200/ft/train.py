@@ -325,7 +325,7 @@ class Worker:
                 raise ValueError("--reduce fused needs a CUDA device")
             from .fused import PeerStateTransport, QuorumFusedReducer
             self.reducer = QuorumFusedReducer(self.engine, self.device, f"shift{a.replica}", a.generation, self.rank,
-                                              a.communication_timeout)
+                                              a.communication_timeout, host=a.host_ip, event=self.event)
             layers = self.cfg.layers
             from ..parallel.replicas import _order
             self.engine.model.layer_done_hook = lambda layer: self.reducer.fused.on_layer_done(_order(layer, layers))
@@ -410,6 +410,7 @@ class Worker:
             schedule_s = t_compute - it0
             if self.reducer is not None:
                 eng.nonfinite.zero_()
+                self.reducer.before_step()
                 self.reducer.fused.begin_step(step)
             loss = self.forward_backward(batches, sample_ids, step)
             if inject_kind == "slow":
@@ -485,6 +486,8 @@ class Worker:
             if commit and a.reference_dump and a.reduce == "group":
                 self.reference_dump(eng.store.grad)
         self.event("stopped", step=self.progress["updates"], attempts=attempts)
+        if self.reducer is not None:
+            self.reducer.close()
         mgr.shutdown()
         self.event.close()
 

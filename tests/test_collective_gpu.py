@@ -79,6 +79,30 @@ def test_flag_wait_times_out_with_status_and_context_survives():
     st.zero_()
 
 
+def test_host_trip_ends_a_pending_peer_wait():
+    """A peer seen dead on the host (PeerWatch.trip) ends a kernel that is
+    already spinning on that peer's flag within one poll, not at its bound."""
+    import time
+    from shift_b200.ft.peer_watch import PeerWatch
+    dev = torch.device("cuda", 0)
+    flags = ext().sym_alloc(64, 0).view(torch.int32)
+    st = status_word(dev)
+    st.zero_()
+    s1 = _step_block(dev, 1, 1e-3, 0.9, 0.999, 1)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    ext().flag_wait([flags[0].data_ptr()], s1, 0, st, 10.0)     # nothing sets this flag; 10 s bound
+    b.record()
+    time.sleep(0.05)
+    w = PeerWatch("me", st)
+    w.trip()
+    torch.cuda.synchronize()
+    w.close()
+    assert int(st[0]) == 2
+    assert a.elapsed_time(b) < 2000.0
+    st.zero_()
+
+
 def test_peer_copy_local():
     a = torch.randn(1 << 20, device="cuda")
     b = torch.empty_like(a)

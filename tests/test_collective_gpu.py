@@ -89,12 +89,14 @@ def test_host_trip_ends_a_pending_peer_wait():
     st = status_word(dev)
     st.zero_()
     s1 = _step_block(dev, 1, 1e-3, 0.9, 0.999, 1)
+    # built before the wait starts, as in training: its pinned source buffer is
+    # allocated here (a pinned allocation can wait for the device to go idle)
+    w = PeerWatch("me", st)
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     ext().flag_wait([flags[0].data_ptr()], s1, 0, st, 10.0)     # nothing sets this flag; 10 s bound
     b.record()
     time.sleep(0.05)
-    w = PeerWatch("me", st)
     w.trip()
     torch.cuda.synchronize()
     w.close()

@@ -7,16 +7,20 @@
 // softmax runs in base 2 on scores pre-multiplied by scale*log2(e); the
 // per-row log-sum-exp (base 2) is saved for the backward.
 //
-// Forward (one CTA per 128 queries of one head):
-//   warp 0   TMA: Q once, then K_j / V_j into a 2-stage ring
+// Forward (one CTA per 128 queries of one head; default form `fwd_split_kernel`):
+//   warp 0   TMA: Q once, then K_j and V_j into separate 3-stage rings
 //   warp 1   TMEM allocation + single-thread tcgen05.mma issue:
-//              S_j = Q K_j^T   (128x128x64, TMEM, double-buffered)
-//              O_j = P_j V_j   (128x64x128, TMEM, double-buffered, fresh per block)
-//   warps 2-9 softmax, two warps per query row group (= TMEM lane quarter),
-//              each on half of the columns: reads S_j with
-//              tcgen05.ld, online max / sum, writes P_j (bf16) into 128B-swizzled
-//              shared memory for the next MMA, and folds O_{j-1} into a register
-//              accumulator with the running rescale (no TMEM read-modify-write).
+//              S_j = Q K_j^T   (128x128x64, TMEM, triple-buffered)
+//              O  += P_j V_j   (128x64x128, TMEM, one accumulator per block parity)
+//   warps 2-9 softmax, two warps per query row group (= TMEM lane quarter)
+//              taking alternate key blocks: each reads whole rows of S_j with
+//              tcgen05.ld, keeps its own online max / sum, writes P_j (bf16)
+//              into 128B-swizzled shared memory for the next MMA and rescales
+//              its O in TMEM only when the row max rises by more than 2^8; the
+//              two partial results are merged once at the end.
+//   Two older forms stay selectable (SHIFT_ATTN_FWD=fold | tmem): the pair
+//   shares each key block (half the columns each) and O is folded into
+//   registers or accumulated in TMEM.
 // Backward (deterministic, no atomics):
 //   dkdv kernel: one CTA per 128 keys of one KV head, looping over every
 //              query head of the group and every query block at or after the
@@ -465,6 +469,264 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm, Params p) {
         *reinterpret_cast<bf16x8*>(orow + c) = float_to_bf16x8(t8);
       }
       if (half == 0) p.lse[(static_cast<long>(b) * p.Hq + h) * p.S + q] = m_run + log2f(l_run);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tbase, 512);
+}
+
+// ------------------- forward, key blocks split between the pair -------------------
+// The two softmax warps of a TMEM lane quarter take alternate key blocks
+// (warp parity 0: j = 0, 2, 4, ...; parity 1: j = 1, 3, 5, ...) and each owns
+// whole 128-column rows of S, so they need no exchange per block: they drift
+// apart, and one warp's exponent phase overlaps the other's TMEM-load / row-max
+// phase on the same scheduler, which keeps the MUFU pipe busy (with a shared
+// block the pair reached every phase together).  Each parity keeps its own
+// online-softmax state and its own O accumulator in TMEM (P V accumulates; O is
+// rescaled in place only when the row max rises by more than 2^kRescaleLog2);
+// the two partial results are merged once at the end.  S is triple-buffered in
+// TMEM (3 x 128 columns + 2 x 64 for the O blocks = all 512), and K / V have
+// separate three-stage rings, so the tensor core runs ahead of both warps.
+constexpr int kSplitStages = 3;
+constexpr int kSplitSmem = 1024 + kTile /*Q*/ + 2 * kSplitStages * kTile /*K,V*/ + 2 * 2 * kTile /*P x2*/ + 256 +
+                           2 * 2 * BM * 4 /*partner m, l*/;
+
+__global__ void __launch_bounds__(kThreads, 1)
+fwd_split_kernel(const __grid_constant__ CUtensorMap tm, Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* sm = smem_raw + (((raw + 1023) & ~1023u) - raw);
+  uint8_t* sQ = sm;
+  uint8_t* sK = sQ + kTile;
+  uint8_t* sV = sK + kSplitStages * kTile;
+  uint8_t* sP = sV + kSplitStages * kTile;    // 2 buffers x 32 KB, buffer = block parity
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sP + 4 * kTile);
+  uint64_t* q_full = bar;
+  uint64_t* k_full = bar + 1;
+  uint64_t* k_empty = k_full + kSplitStages;
+  uint64_t* v_full = k_empty + kSplitStages;
+  uint64_t* v_empty = v_full + kSplitStages;
+  uint64_t* s_full = v_empty + kSplitStages;  // S buffer j % 3
+  uint64_t* p_full = s_full + kSplitStages;   // P buffer j & 1
+  uint64_t* o_full = p_full + 2;              // P V of a block of parity j & 1 done
+  uint64_t* drain = o_full + 2;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(drain + 1);
+  float* s_ml = reinterpret_cast<float*>(tslot + 4);   // [parity][m | l][row]
+
+  int rank_x, h, b;
+  lpt_coords(rank_x, h, b);
+  const int qb = gridDim.x - 1 - rank_x;
+  const int kvh = h / (p.Hq / p.Hkv);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int q0 = qb * BM;
+  const int tok0 = b * p.S;
+  const int n_kv = qb + 1;
+  constexpr uint32_t kOCol = 3 * BN;          // O block of parity r at kOCol + r * D
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < kSplitStages; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+      mbar_init(&s_full[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&p_full[i], kSoftThreads / 2);
+      mbar_init(&o_full[i], 1);
+    }
+    mbar_init(drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tslot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tslot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tm);
+      mbar_arrive_expect_tx(q_full, kTile);
+      tma_load_2d(sQ, &tm, q_full, h * D, tok0 + q0);
+      // K runs one block ahead of V: K_j is free once S_j is computed, V_j only
+      // after P_j V_j
+      auto load = [&](int j, bool is_v) -> bool {
+        const int st = j % kSplitStages;
+        uint64_t* empty = is_v ? &v_empty[st] : &k_empty[st];
+        uint64_t* full = is_v ? &v_full[st] : &k_full[st];
+        if (!mbar_wait(empty, ((j / kSplitStages) & 1) ^ 1, p.status)) return false;
+        mbar_arrive_expect_tx(full, kTile);
+        tma_load_2d((is_v ? sV : sK) + st * kTile, &tm, full, (p.Hq + (is_v ? p.Hkv : 0) + kvh) * D,
+                    tok0 + j * BN);
+        return true;
+      };
+      bool ok = load(0, false);
+      for (int j = 0; j < n_kv && ok; ++j) {
+        if (j + 1 < n_kv) ok = load(j + 1, false);
+        if (ok) ok = load(j, true);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idS = make_idesc_bf16(BM, BN, 0, 0);
+      constexpr uint32_t idO = make_idesc_bf16(BM, D, 0, 1);
+      const uint32_t qa = smem_u32(sQ);
+      bool ok = mbar_wait(q_full, 0, p.status);
+      auto issue_s = [&](int j) -> bool {
+        const int st = j % kSplitStages;
+        if (!mbar_wait(&k_full[st], (j / kSplitStages) & 1, p.status)) return false;
+        tc_fence_after();
+        const uint32_t ka = smem_u32(sK + st * kTile);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          umma_f16(tbase + st * BN, kdesc(qa + kk * 32), kdesc(ka + kk * 32), idS, kk > 0);
+        umma_commit(&s_full[st]);
+        umma_commit(&k_empty[st]);
+        return true;
+      };
+      for (int j = 0; j < kSplitStages && j < n_kv && ok; ++j) ok = issue_s(j);
+      for (int j = 0; j < n_kv && ok; ++j) {
+        if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1, p.status)) break;
+        const int st = j % kSplitStages;
+        if (!mbar_wait(&v_full[st], (j / kSplitStages) & 1, p.status)) break;
+        tc_fence_after();
+        const uint32_t pa = smem_u32(sP + (j & 1) * 2 * kTile);
+        const uint32_t va = smem_u32(sV + st * kTile);
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk)
+          umma_f16(tbase + kOCol + (j & 1) * D, kdesc(pa + (kk >> 2) * kTile + (kk & 3) * 32),
+                   mndesc(va + kk * 2048), idO, (j >= 2 || kk > 0));
+        umma_commit(&o_full[j & 1]);
+        umma_commit(&v_empty[st]);
+        // P_j written means S_j has been read: its buffer takes S_{j+3}
+        if (j + kSplitStages < n_kv && !issue_s(j + kSplitStages)) break;
+      }
+      umma_commit(drain);
+      mbar_wait(drain, 0, p.status);
+    }
+  } else {
+    const int quarter = warp % 4;
+    const int par = (warp - 2) / 4;
+    const int row = quarter * 32 + lane;
+    const int q = q0 + row;
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t to = tbase + kOCol + par * D + lane_off;
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    int last = -1;
+    for (int j = par; j < n_kv; j += 2) {
+      const int st = j % kSplitStages;
+      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[st], (j / kSplitStages) & 1, p.status))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t ts = tbase + st * BN + lane_off;
+      const bool diag = (j == qb);
+      // the whole 128-column row of S stays in registers for both passes
+      uint32_t v[BN];
+#pragma unroll
+      for (int c = 0; c < BN; c += 32) tmem_ld_32x32b_x32(ts + c, v + c);
+      tmem_wait_ld();
+      float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      if (diag) {
+#pragma unroll
+        for (int t = 0; t < BN; ++t)
+          if (t <= row) m4[t & 3] = fmaxf(m4[t & 3], __uint_as_float(v[t]));
+      } else {
+#pragma unroll
+        for (int t = 0; t < BN; ++t) m4[t & 3] = fmaxf(m4[t & 3], __uint_as_float(v[t]));
+      }
+      const float mx = fmaxf(m_run, fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * p.scale_log2);
+      // P V of this parity's previous block must be complete before its P
+      // buffer is rewritten or its O block rescaled
+      if (j >= 2) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&o_full[par], ((j - 2) >> 1) & 1, p.status))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+      }
+      if (__any_sync(0xffffffffu, mx > m_run + kRescaleLog2)) {
+        if (j >= 2) {
+          const float a = ex2(m_run - mx);
+#pragma unroll
+          for (int c = 0; c < D; c += 32) {         // 32 columns at a time: S is still live
+            uint32_t o[32];
+            tmem_ld_32x32b_x32(to + c, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int t = 0; t < 32; ++t) o[t] = __float_as_uint(__uint_as_float(o[t]) * a);
+            tmem_st_32x32b_x16(to + c, o);
+            tmem_st_32x32b_x16(to + c + 16, o + 16);
+          }
+          tmem_wait_st();
+          l_run *= a;
+        }
+        m_run = mx;
+      }
+      uint8_t* pbuf = sP + par * 2 * kTile;
+      const float nmx = -m_run;
+      float l4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c = 0; c < BN; c += 8) {
+        float pr[8];                              // probabilities overwrite S eight at a time
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          pr[t] = (diag && c + t > row) ? 0.f : ex2(fmaf(__uint_as_float(v[c + t]), p.scale_log2, nmx));
+          l4[t & 3] += pr[t];
+        }
+        bf16x8 pk = float_to_bf16x8(pr);
+        *reinterpret_cast<uint4*>(swz_chunk(pbuf, row, c >> 3)) = make_uint4(pk.w[0], pk.w[1], pk.w[2], pk.w[3]);
+      }
+      l_run += (l4[0] + l4[1]) + (l4[2] + l4[3]);
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&p_full[par]);
+      last = j;
+    }
+    if (ok && last >= 0) ok = mbar_wait(&o_full[par], (last >> 1) & 1, p.status);
+    ok = __all_sync(0xffffffffu, ok);
+    s_ml[(par * 2) * BM + row] = ok ? m_run : NAN;
+    s_ml[(par * 2 + 1) * BM + row] = l_run;
+    named_bar(1 + quarter, 64);
+    if (par == 0) {
+      const float mb = s_ml[2 * BM + row], lb = s_ml[3 * BM + row];
+      // the partner had no block (a single-block row) or ran out of a wait
+      ok = ok && __all_sync(0xffffffffu, !isnan(mb));
+      if (ok) {
+        const float m = fmaxf(m_run, mb);
+        const float aa = ex2(m_run - m);
+        const float ab = (mb == -INFINITY) ? 0.f : ex2(mb - m);
+        const float l = l_run * aa + lb * ab;
+        const bool has_b = n_kv > 1;
+        tc_fence_after();
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        __nv_bfloat16* orow = p.o + static_cast<long>(tok0 + q) * p.o_stride + h * D;
+#pragma unroll
+        for (int c0 = 0; c0 < D; c0 += 32) {
+          uint32_t oa[32], ob[32];
+          tmem_ld_32x32b_x32(to + c0, oa);
+          if (has_b) tmem_ld_32x32b_x32(to + D + c0, ob);
+          tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 32; c += 8) {
+            float t8[8];
+#pragma unroll
+            for (int t = 0; t < 8; ++t)
+              t8[t] = (__uint_as_float(oa[c + t]) * aa + (has_b ? __uint_as_float(ob[c + t]) * ab : 0.f)) * inv;
+            *reinterpret_cast<bf16x8*>(orow + c0 + c) = float_to_bf16x8(t8);
+          }
+        }
+        p.lse[(static_cast<long>(b) * p.Hq + h) * p.S + q] = m + log2f(l);
+      }
     }
   }
   tc_fence_before();
@@ -1067,19 +1329,26 @@ std::vector<at::Tensor> fwd(const at::Tensor& qkv, int64_t B, int64_t S, int64_t
   p.lse = lse.data_ptr<float>();
   CUtensorMap tm = tile_map(qkv.data_ptr(), B * S, qkv.size(-1), qkv.stride(-2));
   static bool cfg = false;
-  // SHIFT_ATTN_FWD=fold selects the register-fold form of the forward
-  static const bool tmem_o = [] {
+  // SHIFT_ATTN_FWD selects the forward form: unset or "split" (key blocks
+  // alternate between the warps of a pair, O in TMEM: 0.188 ms at B 8, S 2048,
+  // 16 / 4 heads), "fold" (the pair shares each key block, O folded into
+  // registers: 0.213 ms) or "tmem" (shared block, O in TMEM: 0.225 ms)
+  static const int form = [] {
     const char* e = std::getenv("SHIFT_ATTN_FWD");
-    return e == nullptr || std::string(e) != "fold";
+    const std::string v = e ? e : "split";
+    return v == "fold" ? 0 : v == "tmem" ? 1 : 2;
   }();
   if (!cfg) {
     cudaFuncSetAttribute(fwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem);
     cudaFuncSetAttribute(fwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem);
+    cudaFuncSetAttribute(fwd_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSplitSmem);
     cfg = true;
   }
   dim3 grid(static_cast<unsigned>(S / BM), static_cast<unsigned>(Hq), static_cast<unsigned>(B));
-  if (tmem_o) fwd_kernel<true><<<grid, kThreads, kFwdSmem, at::cuda::getCurrentCUDAStream()>>>(tm, p);
-  else fwd_kernel<false><<<grid, kThreads, kFwdSmem, at::cuda::getCurrentCUDAStream()>>>(tm, p);
+  auto stream = at::cuda::getCurrentCUDAStream();
+  if (form == 2) fwd_split_kernel<<<grid, kThreads, kSplitSmem, stream>>>(tm, p);
+  else if (form == 1) fwd_kernel<true><<<grid, kThreads, kFwdSmem, stream>>>(tm, p);
+  else fwd_kernel<false><<<grid, kThreads, kFwdSmem, stream>>>(tm, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return {o, lse};
 }

@@ -20,11 +20,6 @@ _err: Exception | None = None
 _status: dict[int, torch.Tensor] = {}
 
 
-# forward attention form: "fold" (per-block O folded into registers) until the
-# TMEM-accumulated form has passed its B200 tests; SHIFT_ATTN_FWD=tmem selects it
-os.environ.setdefault("SHIFT_ATTN_FWD", "fold")
-
-
 def ext():
     """Return the compiled module or raise with the import error."""
     global _mod, _err

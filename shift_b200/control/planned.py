@@ -372,6 +372,14 @@ def main(argv=None):
     if a.gpus:
         for role, lst in zip("ABC", a.gpus.split(";")):
             devices[role] = [int(x) for x in lst.split(",")]
+    if a.device == "cuda":
+        # A reduces with B, then with C, inside kernels that wait on the other
+        # role's flags: A never shares a GPU with either.  B and C are never in
+        # one quorum (C replaces B), so they may share GPUs.
+        clash = set(devices.get("A", [])) & (set(devices.get("B", [])) | set(devices.get("C", [])))
+        if clash:
+            raise SystemExit(f"GPUs {sorted(clash)} are given to role A and to role B or C: roles that wait on "
+                             "each other inside kernels must not share a GPU")
     if a.device == "cuda" and not a.no_preflight:
         from .preflight import check_gpus_idle
         wanted = sorted({g for lst in devices.values() for g in lst}) or None

@@ -89,7 +89,29 @@ def load_config(path) -> dict:
               "quorum_tick_ms", "nproc_per_node"):
         if not isinstance(cfg[k], int) or cfg[k] < 0:
             raise ValueError(f"{k} must be a non-negative integer")
+    check_replica_devices(cfg["devices"], cfg["restart_devices"])
     return cfg
+
+
+def check_replica_devices(devices: list, restart_devices: list | None = None):
+    """Replicas reduce with each other inside kernels that spin on the other
+    replicas' flags, so two replicas must never have ranks on the same GPU:
+    separate processes' kernels on one GPU are time-sliced, a spinning kernel
+    can hold the GPU while the kernel it waits for cannot run, and the driver
+    then raises a context-switch timeout.  A relaunched generation of replica r
+    (``restart_devices[r]``) must likewise avoid every other replica's GPUs."""
+    owner = {}
+    for r, d in enumerate(devices):
+        for g in d:
+            if owner.setdefault(g, r) != r:
+                raise ValueError(f"GPU {g} is given to replica {owner[g]} and replica {r}: replicas that wait on "
+                                 "each other inside kernels must not share a GPU")
+    for r, d in enumerate(restart_devices or []):
+        for g in d:
+            o = owner.get(g, r)
+            if o != r:
+                raise ValueError(f"the relaunch of replica {r} would run on GPU {g} of replica {o}: replicas that "
+                                 "wait on each other inside kernels must not share a GPU")
 
 
 def atomic_touch(path: Path):

@@ -67,3 +67,34 @@ def test_tp_rank_sigkill_recovers_with_migration(tmp_path, inject):
     for v in joint:
         for k in ("model", "optimizer", "scheduler"):
             assert v[0][k] == v[1][k]
+
+
+def test_pp_stage_sigkill_recovers_with_stages_swapped(tmp_path):
+    """The 4-GPU form of the scenario: replicas of PP2 without tensor
+    parallelism; stage 0 of replica 0 dies between steps and the replica is
+    relaunched with its two stages swapped between its own devices."""
+    lh, mp, sp_ = _ports(3)
+    cfg = {
+        "entry_module": "shift_b200.ft.mp_train",
+        "nproc_per_node": 2,
+        "train_args": ["--model", "tiny", "--device", "cpu", "--seq-len", "128", "--batch", "1", "--microbatches",
+                       "2", "--tp", "1", "--pp", "2", "--audit-state", "--hash-every", "1", "--data", "random",
+                       "--communication-timeout", "20", "--inject", "sigkill_step@5", "--inject-rank", "0",
+                       "--inject-replica", "0"],
+        "lighthouse_port": lh, "master_port": mp, "store_port_base": sp_ + 1000 if sp_ < 60000 else 20000,
+        "min_replicas": 1, "heartbeat_timeout_ms": 400, "join_timeout_ms": 300, "quorum_tick_ms": 20,
+        "target_steps": 1000,
+        "devices": [[0, 1], [2, 3]], "restart_devices": [[1, 0], [2, 3]],
+    }
+    cpath = tmp_path / "cfg.json"
+    cpath.write_text(json.dumps(cfg))
+    s = Session(tmp_path, "pp", cpath, replicas=2, seconds=900)
+    s.start(timeout=300)
+    try:
+        rec = s.unplanned_fault(0, timeout=300)
+        assert rec["restored_hashes_match"]
+        assert rec["killed_stage"] == 0
+        assert rec["placement_before"] != rec["placement_after"]
+        s.await_(lambda: s.last_step(0) >= rec["joint_step"] + 3, 300, "3 joint commits")
+    finally:
+        s.finish()

@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Headline benchmark: training tokens/s of the 0.494B Qwen-style MoE.
 
-    python bench.py --gpus N --steps K --warmup W [--impl ours|reference]
+    python bench.py --gpus N --steps K --warmup W [--impl ours|reference|eager]
 
 Workload (fixed at every N, i.e. strong scaling): global batch 8 sequences of
 2048 tokens, synthetic uniform-random token ids, random N(0, 0.02) weights,
@@ -48,7 +48,8 @@ def parse():
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=30)
     p.add_argument("--warmup", type=int, default=3)
-    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--impl", default="ours", choices=["ours", "reference", "eager"],
+                   help="eager: the same workload on this package's stock-PyTorch baseline (cuBLAS, SDPA, DDP)")
     p.add_argument("--seq", type=int, default=SEQ)
     p.add_argument("--batch", type=int, default=GLOBAL_BATCH)
     p.add_argument("--no-e2e", action="store_true")
@@ -210,7 +211,13 @@ def main():
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
-    runner = make_runner(args.gpus, rank, local, args.batch, args.seq)
+    if args.impl == "eager":
+        from shift_b200.models.eager_moe import EagerRunner
+        from shift_b200.models.qwen_moe import MoEConfig
+        runner = EagerRunner(MoEConfig.bench(), torch.device("cuda", local), args.batch, args.seq, world, rank)
+        args.no_check = args.no_k1_compare = True
+    else:
+        runner = make_runner(args.gpus, rank, local, args.batch, args.seq)
 
     def barrier():
         if world > 1:
@@ -337,7 +344,7 @@ def main():
             "gpu_launches": None if per_step_launches is None else per_step_launches * args.steps,
             "gpu_launches_per_step": per_step_launches,
             "library_launches_per_step": library_launches,
-            "impl": "ours",
+            "impl": args.impl,
         }
         if checks is not None:
             line.update(checks)

@@ -80,8 +80,24 @@ struct Params {
 
 SB_DEVICE float ex2(float x) {
   float y;
-  asm volatile("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// 2^x on the FMA and integer pipes, for x <= 127, to take part of the
+// softmax's exponentials off the 16-per-clock MUFU unit.  Cody-Waite style
+// range reduction: x = j + r with j = round(x) (the 1.5 * 2^23 shifter puts j
+// in the low mantissa bits of t) and r in [-1/2, 1/2]; 2^r from a cubic fitted
+// here by iteratively re-weighted least squares on the relative error (max
+// relative error 7.5e-5, far below the bf16 rounding of P); j is added to the
+// exponent field with an integer add.  Inputs below -126 are clamped (their
+// probabilities are below bf16's smallest normal anyway).
+SB_DEVICE float ex2_fma(float x) {
+  x = fmaxf(x, -126.f);
+  const float t = x + 12582912.f;
+  const float r = x - (t - 12582912.f);
+  const float p = fmaf(fmaf(fmaf(0.055171531f, r, 0.24261111f), r, 0.69326103f), r, 0.99992806f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 
 // 16-byte chunk c (0..15) of row r of a [128 x 128] bf16 operand stored as two
@@ -493,6 +509,9 @@ constexpr int kSplitStages = 3;
 constexpr int kSplitSmem = 1024 + kTile /*Q*/ + 2 * kSplitStages * kTile /*K,V*/ + 2 * 2 * kTile /*P x2*/ + 256 +
                            2 * 2 * BM * 4 /*partner m, l*/;
 
+// kFma: how many of every 8 probabilities are computed with ex2_fma instead of
+// the MUFU exponent (0 = all on MUFU).
+template <int kFma>
 __global__ void __launch_bounds__(kThreads, 1)
 fwd_split_kernel(const __grid_constant__ CUtensorMap tm, Params p) {
   extern __shared__ uint8_t smem_raw[];
@@ -680,7 +699,8 @@ fwd_split_kernel(const __grid_constant__ CUtensorMap tm, Params p) {
         float pr[8];                              // probabilities overwrite S eight at a time
 #pragma unroll
         for (int t = 0; t < 8; ++t) {
-          pr[t] = (diag && c + t > row) ? 0.f : ex2(fmaf(__uint_as_float(v[c + t]), p.scale_log2, nmx));
+          const float z = fmaf(__uint_as_float(v[c + t]), p.scale_log2, nmx);
+          pr[t] = (diag && c + t > row) ? 0.f : (t >= 8 - kFma ? ex2_fma(z) : ex2(z));
           l4[t & 3] += pr[t];
         }
         bf16x8 pk = float_to_bf16x8(pr);
@@ -1331,22 +1351,25 @@ std::vector<at::Tensor> fwd(const at::Tensor& qkv, int64_t B, int64_t S, int64_t
   static bool cfg = false;
   // SHIFT_ATTN_FWD selects the forward form: unset or "split" (key blocks
   // alternate between the warps of a pair, O in TMEM: 0.188 ms at B 8, S 2048,
-  // 16 / 4 heads), "fold" (the pair shares each key block, O folded into
+  // 16 / 4 heads), "split_fma" (the same with 2 of every 8 exponentials on the
+  // FMA pipe), "fold" (the pair shares each key block, O folded into
   // registers: 0.213 ms) or "tmem" (shared block, O in TMEM: 0.225 ms)
   static const int form = [] {
     const char* e = std::getenv("SHIFT_ATTN_FWD");
     const std::string v = e ? e : "split";
-    return v == "fold" ? 0 : v == "tmem" ? 1 : 2;
+    return v == "fold" ? 0 : v == "tmem" ? 1 : v == "split_fma" ? 3 : 2;
   }();
   if (!cfg) {
     cudaFuncSetAttribute(fwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem);
     cudaFuncSetAttribute(fwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem);
-    cudaFuncSetAttribute(fwd_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSplitSmem);
+    cudaFuncSetAttribute(fwd_split_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSplitSmem);
+    cudaFuncSetAttribute(fwd_split_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSplitSmem);
     cfg = true;
   }
   dim3 grid(static_cast<unsigned>(S / BM), static_cast<unsigned>(Hq), static_cast<unsigned>(B));
   auto stream = at::cuda::getCurrentCUDAStream();
-  if (form == 2) fwd_split_kernel<<<grid, kThreads, kSplitSmem, stream>>>(tm, p);
+  if (form == 2) fwd_split_kernel<0><<<grid, kThreads, kSplitSmem, stream>>>(tm, p);
+  else if (form == 3) fwd_split_kernel<2><<<grid, kThreads, kSplitSmem, stream>>>(tm, p);
   else if (form == 1) fwd_kernel<true><<<grid, kThreads, kFwdSmem, stream>>>(tm, p);
   else fwd_kernel<false><<<grid, kThreads, kFwdSmem, stream>>>(tm, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();

@@ -3,9 +3,11 @@
 Global rank = replica * (tp*pp) + stage * tp + tp_rank.  Inside a replica:
 tensor parallelism with sequence parallelism and experts split over the TP
 pair (``parallel.tp``), pipeline parallelism with a 1F1B schedule over
-microbatches of one sequence (activations and gradients travel on NCCL p2p,
-batched send/recv pairs in steady state -- the reference keeps PP on NCCL
-p2p too, shift_full/train.py:552).  Across replicas: the fused peer-memory
+microbatches of two sequences; activations and gradients travel through
+peer-memory slots written by a copy kernel and guarded by step-tag flags
+(``parallel.pipe.PipePeer``, capturable in the step's CUDA graph), or on NCCL
+p2p as the baseline (``SHIFT_PP_BACKEND=nccl``; the reference keeps PP on NCCL
+p2p, shift_full/train.py:552).  Across replicas: the fused peer-memory
 reduce + AdamW (K1) per bucket, overlapped with the last microbatch's
 backward; TP-replicated parameters are summed over the TP pair and averaged
 over replicas inside the same kernel.
@@ -37,9 +39,13 @@ class ModelParallelRunner:
                  replicas: int, tp: int, pp: int, microbatch: int | None = None, tp_backend: str | None = None,
                  pp_backend: str | None = None, with_manager: bool | None = None):
         if microbatch is None:
-            # one microbatch per replica without pipelining; with it, one sequence per
-            # microbatch (four microbatches per replica: a 1F1B bubble of 1/5 instead of 1/3)
-            microbatch = batch // replicas if pp == 1 else 1
+            # one microbatch per replica without pipelining; with it, two sequences per
+            # microbatch.  At 2 replicas x (TP2 x PP2) on B200 one sequence per
+            # microbatch (four microbatches, a 1F1B bubble of 1/5) measured 19.9 ms
+            # per step against 15.4 ms for two (bubble 1/3): a TP rank's 1,024-row
+            # GEMMs and single-sequence attention leave most SMs idle, which costs
+            # more than the larger bubble
+            microbatch = batch // replicas if pp == 1 else min(2, batch // replicas)
         if replicas * tp * pp != n_gpus:
             raise ValueError(f"{replicas} x tp{tp} x pp{pp} != {n_gpus} GPUs")
         if batch % (replicas * microbatch):

@@ -22,6 +22,7 @@ Layout of the fused weights:
 """
 from __future__ import annotations
 
+import functools
 import math
 from dataclasses import dataclass, field
 
@@ -139,6 +140,12 @@ class QwenMoE:
         self.dt = store.compute_dtype
         self._saved: list = []
         self.layer_done_hook = None   # callable(layer_index) after its grads are written
+        # pipeline schedules may defer the weight-gradient GEMMs of a backward
+        # (and the layer-done hooks that follow them) into a queue that
+        # flush_wgrad() runs later, to fill the time a stage would otherwise
+        # spend waiting for the next stage's gradient
+        self.defer_wgrad = False
+        self._wq: list = []
         self.routing_hook = None      # callable(layer_prefix, topk_idx) after each router forward
 
     @property
@@ -281,13 +288,13 @@ class QwenMoE:
                              dout_own, accumulate, dy2=tp.buf("rDm", i), dx_out=gH[own],
                              xchg=tp.xchg(wait=("rDm", i), sig=("gH", i), peer_out=tp.pbuf("gH", i)[own]))
         # ---- attention: the gathered dh2 feeds both GEMMs (each waits in-kernel)
-        G.linear_wgrad(gH, c["o"], st.g(p + "attn.o"), accumulate, xchg=tp.xchg(wait=("gH", i)),
-                       tp=(plo, phi, 0, 0, 0, 0))
+        self._wg(functools.partial(G.linear_wgrad, gH, c["o"], st.g(p + "attn.o"), accumulate,
+                                   xchg=tp.xchg(wait=("gH", i)), tp=(plo, phi, 0, 0, 0, 0)))
         d_o = G.linear_dgrad(gH, st.w(p + "attn.o"), xchg=tp.xchg(wait=("gH", i)),
                              tp=(plo, phi, tp.rot_own_first(), 0, 0, 0))
         dqkv = Fn.attention_bwd(c["qkv"], c["o"], c["lse"], d_o, B, S, Hq, Hkv, D, self.scale)
         Fn.rope_(dqkv, self.cos, self.sin, S, Hq + Hkv, D, inverse=True)
-        G.linear_wgrad(dqkv, c["a_in"], st.g(p + "attn.qkv"), accumulate)
+        self._wg(functools.partial(G.linear_wgrad, dqkv, c["a_in"], st.g(p + "attn.qkv"), accumulate))
         da_own = torch.empty(T // 2, cfg.hidden, dtype=dqkv.dtype, device=dqkv.device)
         G.linear_dgrad(dqkv, st.w(p + "attn.qkv"), out=da_own,
                        xchg=tp.xchg(sig=("rDa", i), peer_out=tp.pbuf("rDa", i)),
@@ -335,7 +342,7 @@ class QwenMoE:
         if self.part.has_head:
             dlogits = saved["dlogits"]
             y = saved["final_y"]
-            G.linear_wgrad(dlogits, y, st.g("lm_head.weight"), accumulate)
+            self._wg(functools.partial(G.linear_wgrad, dlogits, y, st.g("lm_head.weight"), accumulate))
             dy = G.linear_dgrad(dlogits, st.w("lm_head.weight"))
             fused = self._fused_tp() and len(saved["layers"]) > 0
             if fused:
@@ -385,8 +392,26 @@ class QwenMoE:
         return dres
 
     def _hook(self, layer):
-        if self.layer_done_hook is not None:
-            self.layer_done_hook(layer)
+        h = self.layer_done_hook
+        if h is None:
+            return
+        if self.defer_wgrad:
+            self._wq.append(functools.partial(h, layer))     # after the layer's deferred GEMMs
+        else:
+            h(layer)
+
+    def _wg(self, fn):
+        """Run a weight-gradient GEMM now, or queue it (``defer_wgrad``)."""
+        if self.defer_wgrad:
+            self._wq.append(fn)
+        else:
+            fn()
+
+    def flush_wgrad(self):
+        """Run the deferred weight-gradient GEMMs and hooks in backward order."""
+        q, self._wq = self._wq, []
+        for fn in q:
+            fn()
 
     def _layer_bwd(self, i, c, dout, B, S, accumulate):
         """dout: gradient w.r.t. the layer output h_out = h2 + moe_out."""
@@ -400,11 +425,11 @@ class QwenMoE:
                              dout, accumulate)
         # ---- attention ----
         dattn = self._ag(dh2)
-        G.linear_wgrad(dattn, c["o"], st.g(p + "attn.o"), accumulate)
+        self._wg(functools.partial(G.linear_wgrad, dattn, c["o"], st.g(p + "attn.o"), accumulate))
         d_o = G.linear_dgrad(dattn, st.w(p + "attn.o"))
         dqkv = Fn.attention_bwd(c["qkv"], c["o"], c["lse"], d_o, B, S, Hq, Hkv, D, self.scale)
         Fn.rope_(dqkv, self.cos, self.sin, S, Hq + Hkv, D, inverse=True)
-        G.linear_wgrad(dqkv, c["a_in"], st.g(p + "attn.qkv"), accumulate)
+        self._wg(functools.partial(G.linear_wgrad, dqkv, c["a_in"], st.g(p + "attn.qkv"), accumulate))
         da = self._rs(G.linear_dgrad(dqkv, st.w(p + "attn.qkv")))
         dh = Fn.rmsnorm_bwd(da, c["h"], c["rstd1"], st.w(p + "ln1.weight"), cfg.eps, st.g(p + "ln1.weight"), dh2,
                             accumulate)
@@ -415,9 +440,9 @@ class QwenMoE:
         cap = c["row_src"].shape[0]
         slot_of_row = Fn.invert_pos(c["pos"], cap)
         dy, dw_topk = Fn.combine_bwd(dout, c["y"], c["pos"], c["w"], c["row_src"], slot_of_row, c["total"])
-        G.grouped_wgrad(dy, c["act"], c["offs"], st.g(p + "mlp.w2"), accumulate)
+        self._wg(functools.partial(G.grouped_wgrad, dy, c["act"], c["offs"], st.g(p + "mlp.w2"), accumulate))
         dh = G.grouped_dgrad_swiglu(dy, st.w(p + "mlp.w2"), c["offs"], c["hgu"])
-        G.grouped_wgrad(dh, c["xp"], c["offs"], st.g(p + "mlp.w1"), accumulate)
+        self._wg(functools.partial(G.grouped_wgrad, dh, c["xp"], c["offs"], st.g(p + "mlp.w1"), accumulate))
         dxp = G.grouped_dgrad(dh, st.w(p + "mlp.w1"), c["offs"])
         dx = torch.empty_like(c["m_in"])
         Fn.scatter_back(dxp, c["pos"], dx, False)

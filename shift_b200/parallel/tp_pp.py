@@ -232,6 +232,16 @@ class ModelParallelRunner:
         pipe = self.pipe
         if pipe is not None:
             pipe.set_parity(self.step_no % 2)
+        # Weight gradients off the pipeline's critical path: the last stage
+        # queues every microbatch's weight-gradient GEMMs until its last input
+        # gradient has been sent, so the stage below gets its gradients a
+        # weight-gradient pass earlier; the other stages run them right after
+        # each backward, in the time they would wait for the next gradient
+        # (at PP2 with two microbatches the step takes 7 backward-pass units
+        # instead of 9 -- the first bubble-filling split of Qi et al.'s
+        # zero-bubble pipeline schedules)
+        defer = pipe is not None and os.environ.get("SHIFT_PP_DEFER_WGRAD", "0") == "1"
+        eng.model.defer_wgrad = defer
         n_warm = min(pp - s - 1, M)
         n_rem = M - n_warm
         for i in range(n_warm):
@@ -247,13 +257,24 @@ class ModelParallelRunner:
             if j == n_rem - 1:
                 if not first:
                     pipe.exchange(send=(GRAD, j, dx))
+                if defer and not last:
+                    eng.model.flush_wgrad()
             else:
+                if defer and first:
+                    eng.model.flush_wgrad()
                 x = None if first else pipe.exchange(send=(GRAD, j, dx), recv=(ACT, i + 1))
+                if defer and not first and not last:
+                    eng.model.flush_wgrad()
         for j in range(n_rem, M):
             dy = None if last else pipe.exchange(recv=(GRAD, j))
             dx = self._bwd(j, dy)
             if not first:
                 pipe.exchange(send=(GRAD, j, dx))
+            if defer and not last:
+                eng.model.flush_wgrad()
+        if defer:
+            eng.model.flush_wgrad()
+            eng.model.defer_wgrad = False
         eng.model._accumulate = False
         self.fused.finish_step()
         if self._loss is None:

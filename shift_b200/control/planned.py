@@ -89,7 +89,7 @@ class PlannedSession:
         self.procs: dict[str, sp.Popen] = {}
         args = ["--model", model, "--device", device, "--seq-len", "128", "--batch", "2", "--data", "random",
                 "--communication-timeout", "60", "--planned-variant", variant, "--coord",
-                f"127.0.0.1:{self.coord_port}", "--lighthouse-port", str(self.lh_port), "--steps", "100000"]
+                f"127.0.0.1:{self.coord_port}", "--steps", "100000"]
         if audit:
             args += ["--audit-state", "--hash-every", "1"]
         if scenario != "healthy":
@@ -119,11 +119,17 @@ class PlannedSession:
             time.sleep(0.02)
         raise TimeoutError(label)
 
-    def start_lighthouse(self, port, min_replicas=2):
-        p, addr = spawn_lighthouse(f"127.0.0.1:{port}", min_replicas=min_replicas, join_timeout_ms=1000,
+    def start_lighthouse(self, slot, min_replicas=2):
+        """Start the lighthouse of one epoch (``slot`` = 10 * epoch, + 1 for the
+        fallback A+B epoch of a P2 round) on a port the OS chooses, and publish
+        its address under ``lighthouse/<slot>`` of the coordination store,
+        where the trainers look it up: no fixed port that another process may
+        have taken in the meantime."""
+        p, addr = spawn_lighthouse("127.0.0.1:0", min_replicas=min_replicas, join_timeout_ms=1000,
                                    heartbeat_timeout_ms=1000, quorum_tick_ms=20)
         self.lighthouses.append(p)
-        self.log("lighthouse_started", port=port)
+        self.coord.set(f"lighthouse/{slot}", addr)
+        self.log("lighthouse_started", slot=slot, address=addr)
 
     def launch(self, role: str, name: str | None = None, generation: int | None = None, round_: int = 0,
                extra=()):
@@ -154,7 +160,7 @@ class PlannedSession:
     # ------------------------------------------------------------------ experiment
     def run(self, post_steps=3, cancel=False):
         n = self.nproc
-        self.start_lighthouse(self.lh_port)
+        self.start_lighthouse(0)
         self.launch("A")
         self.launch("B")
         self.wait("ab_ready", lambda: len(self.rows("ready", generation=0)) == 2 * n, 300)
@@ -164,9 +170,9 @@ class PlannedSession:
         self.log("REQUEST", variant=self.variant)
         self.launch("C")
         self.key("request")
-        self.start_lighthouse(self.lh_port + 10)
+        self.start_lighthouse(10)
         if self.variant == "p2":
-            self.start_lighthouse(self.lh_port + 11)
+            self.start_lighthouse(11)
         if self.scenario in ("prepare-fail", "ready-timeout") or cancel:
             kind = {"prepare-fail": "planned_prepare_rejected", "ready-timeout": "planned_prepare_delayed"}.get(
                 self.scenario, "planned_local_ready")
@@ -200,7 +206,7 @@ class PlannedSession:
         cut before the next request."""
         n = self.nproc
         extra = ["--planned-cycles", str(cycles)]
-        self.start_lighthouse(self.lh_port)
+        self.start_lighthouse(0)
         self.launch("A", extra=extra)
         self.launch("B", extra=extra)
         self.wait("ab_ready", lambda: len(self.rows("ready", generation=0)) == 2 * n, 300)
@@ -216,9 +222,9 @@ class PlannedSession:
             self.log("REQUEST", variant=self.variant, round=r)
             self.launch("C", name=spare, generation=r + 1, round_=r, extra=extra)
             self.key(pre + "request")
-            self.start_lighthouse(self.lh_port + 10 * (r + 1))
+            self.start_lighthouse(10 * (r + 1))
             if self.variant == "p2":
-                self.start_lighthouse(self.lh_port + 10 * (r + 1) + 1)
+                self.start_lighthouse(10 * (r + 1) + 1)
             self.wait(f"c_local_ready_{r}", lambda: len(self.rows("planned_local_ready", generation=r + 1)) == n)
             self.key(pre + "arm")
             cut = self.wait(f"cut_selected_{r}", lambda: [x for x in self.rows("planned_cut_selected", rid=0)

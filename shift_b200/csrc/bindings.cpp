@@ -76,6 +76,9 @@ void xcopy(int64_t src_ptr, int64_t dst_ptr, int64_t nbytes, const std::vector<i
            const at::Tensor& status);
 std::string fingerprint(const at::Tensor& t);
 }  // namespace coll
+namespace digest {
+at::Tensor sha256_leaves(const at::Tensor& t, int64_t leaf, const at::Tensor& consts);
+}  // namespace digest
 }  // namespace sb
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -128,4 +131,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("peer_copy", &sb::coll::peer_copy, "K10: SM-driven peer-memory copy");
   m.def("xcopy", &sb::coll::xcopy, "copy to a local and a peer destination with TP exchange wait/signal");
   m.def("fingerprint", &sb::coll::fingerprint, "deterministic 64-bit fingerprint of a tensor's bytes");
+  m.def("sha256_leaves", &sb::digest::sha256_leaves, "SHA-256 of each fixed-size leaf of a device buffer");
 }

@@ -3,7 +3,7 @@ replica of ``tp * pp`` ranks (one process per rank).
 
     python -m shift_b200.control.launch --nproc 4 --module shift_b200.ft.mp_planned_train -- \
         --planned-role A|B|C --planned-variant p1f|p2 --tp 2 --pp 2 --coord HOST:PORT \
-        --lighthouse-port L [trainer flags]
+        [trainer flags]
 
 The handoff protocol is per rank: rank k of the spare C pulls its state
 (params, fp32 master, Adam moments, scheduler, RNG, progress) from rank k of

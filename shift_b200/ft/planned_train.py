@@ -1,7 +1,7 @@
 """Role-aware trainer for planned handoff (roles A, B, C; variants p1f, p2).
 
     python -m shift_b200.ft.planned_train --planned-role A|B|C --planned-variant p1f|p2 \
-        --coord HOST:PORT --lighthouse-host HOST --lighthouse-port L [trainer flags]
+        --coord HOST:PORT [trainer flags]
 
 Epoch e uses the lighthouse at ``L + 10*e`` (``L + 10*e + 1`` for the A+B
 fallback epoch of a rejected P2 relay) and Manager stores on their own ports,
@@ -41,11 +41,11 @@ def parse_args(argv=None):
     extra.add_argument("--planned-cycles", type=int, default=1,
                        help="rotation: rounds of the experiment; a process serves rounds [planned-round, cycles)")
     extra.add_argument("--coord", required=True)
-    extra.add_argument("--lighthouse-host", default="127.0.0.1")
-    extra.add_argument("--lighthouse-port", type=int, required=True)
     extra.add_argument("--mover", choices=["auto", "ipc", "packed"], default="auto")
     known, rest = extra.parse_known_args(argv)
-    args = base_parse(rest + ["--lighthouse", f"{known.lighthouse_host}:{known.lighthouse_port}"])
+    # each epoch's lighthouse address comes from the coordination store
+    # (lighthouse/<slot>), so the base trainer's --lighthouse is a placeholder
+    args = base_parse(rest + ["--lighthouse", "127.0.0.1:0"])
     for k, v in vars(known).items():
         setattr(args, k, v)
     return args
@@ -138,9 +138,23 @@ class PlannedWorker(Worker):
             return m
         return self.make_manager(epoch, members)
 
+    def lighthouse_address(self, slot: int, timeout: float = 120.0) -> str:
+        """Address of an epoch's lighthouse: the controller starts it on a port
+        the OS chooses and publishes it under ``lighthouse/<slot>`` of the
+        coordination store (slot = 10 * epoch, + 1 for a P2 round's fallback
+        A+B epoch)."""
+        key = f"lighthouse/{slot}"
+        raw = self.coord.raw
+        end = time.monotonic() + timeout
+        while not raw.check([key]):
+            if time.monotonic() > end:
+                raise TimeoutError(f"no lighthouse published for slot {slot}")
+            time.sleep(0.005)
+        return raw.get(key).decode()
+
     def make_manager(self, epoch: int, members: str = "AB", activate: bool = True):
         a = self.args
-        port = a.lighthouse_port + 10 * epoch + (1 if members == "AB" and epoch > self.round else 0)
+        lighthouse = self.lighthouse_address(10 * epoch + (1 if members == "AB" and epoch > self.round else 0))
         if self.device.type == "cuda" and not self.group_reduce:
             # fused peer-memory reduction + IPC healing: a new epoch only re-maps handles
             from .fused import PeerStateTransport
@@ -158,7 +172,7 @@ class PlannedWorker(Worker):
         rid = self.logical_rid
         store, store_addr = self.manager_store(epoch, members)
         m = Manager(pg, self.load_state_for_manager, self.export_state_for_transport, 2, f"shift{rid}",
-                    f"{a.lighthouse_host}:{port}", rank=self.rank, world_size=self.local_world,
+                    lighthouse, rank=self.rank, world_size=self.local_world,
                     store_addr=store_addr, store=store, hostname=a.host_ip, checkpoint_transport=transport,
                     timeout=timedelta(seconds=a.communication_timeout),
                     world_size_mode=WorldSizeMode.FIXED_WITH_SPARES, event=self.event)

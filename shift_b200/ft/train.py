@@ -61,8 +61,10 @@ def parse_args(argv=None):
     p.add_argument("--microbatches", type=int, default=1)
     p.add_argument("--hash-every", type=int, default=0)
     p.add_argument("--audit-state", action="store_true")
-    p.add_argument("--audit-hash", choices=["sha256", "fingerprint"], default="sha256",
-                   help="sha256: the reference's host digest; fingerprint: 64-bit FNV-1a of the flat state on GPU")
+    p.add_argument("--audit-hash", choices=["sha256", "sha256tree", "fingerprint"], default="sha256",
+                   help="sha256: the reference's host digest of the state dict; sha256tree: SHA-256 over the "
+                        "SHA-256 digests of 64 KiB leaves of the flat state, computed on the GPU; fingerprint: "
+                        "64-bit FNV-1a of the flat state on the GPU")
     p.add_argument("--fixed-batch", action="store_true")
     p.add_argument("--data", choices=["pattern", "random"], default="random")
     p.add_argument("--data-seed", type=int, default=0, help="uniform random ids from seed data_seed*1e6+sample")
@@ -149,7 +151,20 @@ class Worker:
         if self.device.type == "cuda":
             torch.cuda.current_stream().synchronize()
         rng = rng if rng is not None else self.rng_snapshot()
-        if getattr(self.args, "audit_hash", "sha256") == "fingerprint" and self.device.type == "cuda":
+        mode = getattr(self.args, "audit_hash", "sha256")
+        if mode == "sha256tree":
+            # SHA-256 of every 64 KiB leaf of the flat state buffers, computed
+            # where the state lives (a GPU kernel on CUDA), then SHA-256 over
+            # the leaf digests: the full-state audit without a host copy
+            from ..utils.digest import sha256tree
+            st = self.engine.store
+            c = st.cur
+            opt = "/".join(sha256tree(t[c]) for t in (st.master, st.exp_avg, st.exp_avg_sq))
+            return dict(model="st:" + sha256tree(st.param[c]), optimizer=f"st:{opt}/{st.step}",
+                        scheduler=digest(self.engine.scheduler.state_dict()), progress=digest(self.progress),
+                        cpu_rng=digest(rng["torch_rng"]), cuda_rng=digest(rng["cuda_rng"]),
+                        python_rng=digest(rng["python_rng"]))
+        if mode == "fingerprint" and self.device.type == "cuda":
             # exact-state fingerprints computed on the GPU (no host copy of the state)
             from ..ops._ext import ext
             st = self.engine.store

@@ -239,7 +239,7 @@ class ModelParallelRunner:
         # each backward, in the time they would wait for the next gradient
         # (at PP2 with two microbatches the step takes 7 backward-pass units
         # instead of 9 -- the first bubble-filling split of Qi et al.'s
-        # zero-bubble pipeline schedules)
+        # zero-bubble pipeline schedules).  Opt-in: SHIFT_PP_DEFER_WGRAD=1
         defer = pipe is not None and os.environ.get("SHIFT_PP_DEFER_WGRAD", "0") == "1"
         eng.model.defer_wgrad = defer
         n_warm = min(pp - s - 1, M)

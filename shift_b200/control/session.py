@@ -190,7 +190,10 @@ class Session:
         joint = {"step": jstep, "time": jtime}
         placement = {r["rank"]: r.get("placement") for r in self.reader.rows("ready", rid=rid, generation=gen + 1)}
         old_placement = {r["rank"]: r.get("placement") for r in self.reader.rows("ready", rid=rid, generation=gen)}
-        rec = dict(rid=rid, fault_kind="sigkill_mid_backward", generation=gen, killed_rank=kill["rank"],
+        ta = self.cfg["train_args"]
+        inj = ta[ta.index("--inject") + 1].split("@")[0] if "--inject" in ta else "sigkill_bwd"
+        kind = {"sigkill_bwd": "sigkill_mid_backward", "sigkill_step": "sigkill_between_steps"}.get(inj, inj)
+        rec = dict(rid=rid, fault_kind=kind, generation=gen, killed_rank=kill["rank"],
                    killed_stage=kill.get("stage"), killed_tp_rank=kill.get("tp_rank"), fault_step=base,
                    fault_time=kill["fault_time"], solo_time=t_solo, restored_time=max(r["time"] for r in restored),
                    joint_time=joint["time"], restored_step=rstep, joint_step=joint["step"],

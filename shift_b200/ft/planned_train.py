@@ -127,6 +127,22 @@ class PlannedWorker(Worker):
     def precreate_manager(self, handoff):
         if self.role in ("A", "C") and self.args.planned_variant in ("p1f", "p2"):
             self.next_manager = self.make_manager(handoff.new_epoch, "AC", activate=False)
+            pg = getattr(self.next_manager, "_pg", None)
+            # A (whose hooks do not wait for the spare) connects only once the
+            # spare at its rank position is up, and not at all after a cancel
+            ready = pg is not None and (self.role == "C" or handoff.coord.clone().wait(
+                [f"local/C/{self.rank}"], 600, cancel_key="cancel"))
+            if ready:
+                # the A+C group of the next epoch (A is replica rank 0, the spare
+                # takes replica 1's place), connected before the cut
+                t0 = time.monotonic()
+                try:
+                    pg.prepare(self.coord.raw, f"e{handoff.new_epoch}/r{self.rank}", 0 if self.role == "A" else 1,
+                               2)
+                    self.event("planned_candidate_group_ready", epoch=handoff.new_epoch,
+                               seconds=time.monotonic() - t0)
+                except Exception as e:      # the epoch's quorum will build the group instead
+                    self.event("planned_candidate_group_failed", epoch=handoff.new_epoch, error=repr(e))
             self.event("planned_candidate_manager_ready", epoch=handoff.new_epoch)
 
     def take_manager(self, epoch: int, members: str):

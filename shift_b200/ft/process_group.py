@@ -42,6 +42,7 @@ class ReconfigurableGroup:
         self.configures = 0
         self.creations = 0
         self._lock = threading.Lock()
+        self._prepared = None        # (rank, world_size, group) built ahead of its quorum
 
     # ------------------------------------------------------------------ config
     def configure(self, store_addr: str, replica_id: str, rank: int, world_size: int, quorum_id: int = 0,
@@ -51,14 +52,29 @@ class ReconfigurableGroup:
         if key == self._key and self._pg is not None:
             return False
         self.abort()
-        store = self._stores.get(store_addr)
-        if store is None:
-            store = connect_store(store_addr, self.timeout.total_seconds())
-            self._stores[store_addr] = store
-        pstore = dist.PrefixStore(f"shift/q{quorum_id}/{self.prefix}", store)
+        with self._lock:
+            prep, self._prepared = self._prepared, None
+        prepared = prep is not None and prep[0] == rank and prep[1] == world_size
+        if prepared:
+            pg = prep[2]                 # the membership was known ahead: adopt the connected group
+        else:
+            store = self._stores.get(store_addr)
+            if store is None:
+                store = connect_store(store_addr, self.timeout.total_seconds())
+                self._stores[store_addr] = store
+            pg = self._create(dist.PrefixStore(f"shift/q{quorum_id}/{self.prefix}", store), rank, world_size)
+        self._pg, self._key = pg, key
+        self._rank, self._size = rank, world_size
+        self.creations += 1
+        if self.emit:
+            self.emit("reconfigure_end", quorum_id=quorum_id, rank=rank, world_size=world_size,
+                      backend=self.backend, creations=self.creations, prepared=prepared)
+        return True
+
+    def _create(self, pstore, rank: int, world_size: int):
         if self.backend == "gloo":
-            pg = dist.ProcessGroupGloo(pstore, rank, world_size, self.timeout)
-        elif self.backend == "nccl":
+            return dist.ProcessGroupGloo(pstore, rank, world_size, self.timeout)
+        if self.backend == "nccl":
             opts = dist.ProcessGroupNCCL.Options()
             opts._timeout = self.timeout
             pg = dist.ProcessGroupNCCL(pstore, rank, world_size, opts)
@@ -66,15 +82,25 @@ class ReconfigurableGroup:
                 # eager connect so the first collective of the step is not also the setup
                 t = torch.zeros(1, device=self.device)
                 pg.allreduce([t]).wait()
-        else:
-            raise ValueError(f"unknown backend {self.backend}")
-        self._pg, self._key = pg, key
-        self._rank, self._size = rank, world_size
-        self.creations += 1
-        if self.emit:
-            self.emit("reconfigure_end", quorum_id=quorum_id, rank=rank, world_size=world_size,
-                      backend=self.backend, creations=self.creations)
-        return True
+            return pg
+        raise ValueError(f"unknown backend {self.backend}")
+
+    def prepare(self, store, key: str, rank: int, world_size: int):
+        """Build and connect, ahead of its quorum, the group of a membership
+        that is already known -- the next epoch of a planned handoff, A and the
+        spare C -- so that the quorum's ``configure`` adopts it instead of
+        paying communicator set-up inside the handoff.  ``store`` is any store
+        both sides reach; ``key`` names the group on it.  A configure whose
+        rank or size differs from the prepared one builds a group as usual
+        (and drops the prepared one)."""
+        pg = self._create(dist.PrefixStore(f"shift/prep/{key}/{self.prefix}", store), rank, world_size)
+        with self._lock:
+            old, self._prepared = self._prepared, (rank, world_size, pg)
+        if old is not None and hasattr(old[2], "abort"):
+            try:
+                old[2].abort()
+            except Exception:
+                pass
 
     def size(self) -> int:
         return self._size

@@ -66,9 +66,11 @@ class EagerBlock(nn.Module):
         a = F.rms_norm(x, (H,), self.ln1, cfg.eps)
         qkv = self.qkv(a)
         q, k, v = qkv.split([Hq * D, Hkv * D, Hkv * D], dim=-1)
-        q = _rope(q.view(B, S, Hq, D).transpose(1, 2), cos, sin)
-        k = _rope(k.view(B, S, Hkv, D).transpose(1, 2), cos, sin)
-        v = v.view(B, S, Hkv, D).transpose(1, 2)
+        # contiguous [B, heads, S, D] operands, as the fused SDPA backends want
+        # them (a strided V sends SDPA to its unfused math fallback)
+        q = _rope(q.view(B, S, Hq, D).transpose(1, 2), cos, sin).contiguous()
+        k = _rope(k.view(B, S, Hkv, D).transpose(1, 2), cos, sin).contiguous()
+        v = v.view(B, S, Hkv, D).transpose(1, 2).contiguous()
         o = F.scaled_dot_product_attention(q, k, v, is_causal=True, scale=1.0 / math.sqrt(D), enable_gqa=True)
         x = x + self.o(o.transpose(1, 2).reshape(B, S, Hq * D))
         m = F.rms_norm(x, (H,), self.ln2, cfg.eps).reshape(B * S, H)

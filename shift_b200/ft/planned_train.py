@@ -314,8 +314,12 @@ class PlannedWorker(Worker):
         self.coord = Coordinator(a.coord, f"round/{round_}" if round_ else "")
         mover = a.mover if a.mover != "auto" else ("ipc" if cuda else "packed")
         cls = OverlapHandoff if a.planned_variant == "p2" else PlannedHandoff
-        hooks = ([self.premap_k1, self.warmup_spare, self.precreate_manager] if cuda and not self.group_reduce
-                 else [self.precreate_manager])
+        if self.group_reduce:           # model-parallel replicas: NCCL groups, per-stage warm-up
+            hooks = [self.warmup_spare, self.precreate_manager]
+        elif cuda:
+            hooks = [self.premap_k1, self.warmup_spare, self.precreate_manager]
+        else:
+            hooks = [self.precreate_manager]
         emit = lambda kind, **kw: self.event(kind, round=round_, **kw)   # noqa: E731
         h = cls(self.role, a.planned_variant, self.rank, self.local_world, self.coord, emit,
                 self.export_state, self.load_state, self.progress, self.manifest, self.device, mover,

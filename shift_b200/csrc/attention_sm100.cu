@@ -97,7 +97,7 @@ SB_DEVICE float ex2_fma(float x) {
   const float t = x + 12582912.f;
   const float r = x - (t - 12582912.f);
   const float p = fmaf(fmaf(fmaf(0.055171531f, r, 0.24261111f), r, 0.69326103f), r, 0.99992806f);
-  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+  return __uint_as_float(__float_as_uint(p) + (__float_as_uint(t) << 23));   // unsigned: wraps, no overflow
 }
 
 // 16-byte chunk c (0..15) of row r of a [128 x 128] bf16 operand stored as two

@@ -70,6 +70,7 @@ DEFAULTS = {
     "lazy_restart_init": False,
 }
 REQUIRED = ("train_args",)
+MAX_REPLICAS = 8          # replicas of one session (per-generation ports interleave by this stride)
 
 
 def load_config(path) -> dict:
@@ -91,6 +92,8 @@ def load_config(path) -> dict:
             raise ValueError(f"{k} must be a non-negative integer")
     check_replica_devices(cfg["devices"], cfg["restart_devices"])
     return cfg
+
+
 
 
 def check_replica_devices(devices: list, restart_devices: list | None = None):
@@ -190,9 +193,19 @@ def main(argv=None):
             return ""
         return ",".join(str(x) for x in d[args.replica % len(d)])
 
+    def gen_port(base: int, gen: int) -> int:
+        """Port of one replica's generation: replicas interleave (base +
+        replica + MAX_REPLICAS * generation), so no two replicas' generations
+        ever share a port however many relaunches a long rotation makes (a
+        stride of 10 per replica collided once a replica passed 10
+        generations)."""
+        if not 0 <= args.replica < MAX_REPLICAS:
+            raise ValueError(f"replica index {args.replica} outside 0..{MAX_REPLICAS - 1}")
+        return base + args.replica + MAX_REPLICAS * gen
+
     def launch(gen=None, extra=()):
         gen = generation if gen is None else gen
-        port = cfg["master_port"] + 10 * args.replica + gen
+        port = gen_port(cfg["master_port"], gen)
         log = (out / f"launcher_r{args.replica}_g{gen}.log").open("w")
         logs.append(log)
         cmd = [cfg["python"], "-m", "shift_b200.control.launch", "--nproc", str(cfg["nproc_per_node"]),
@@ -205,7 +218,7 @@ def main(argv=None):
                 "--lighthouse", f"{cfg['lighthouse_ip']}:{cfg['lighthouse_port']}", "--min-replicas",
                 str(cfg["min_replicas"]), *cfg["train_args"], *extra]
         e = dict(env)
-        e["SHIFT_STORE_PORT"] = str(cfg["store_port_base"] + 10 * args.replica + gen)
+        e["SHIFT_STORE_PORT"] = str(gen_port(cfg["store_port_base"], gen))
         if gen > 0 and cfg["lazy_restart_init"] and "--standby" not in extra:
             cmd += ["--lazy-init"]
         if cfg["fast_launch"]:

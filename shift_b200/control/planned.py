@@ -328,9 +328,21 @@ def summarize(reader, variant, info, nproc=1) -> dict:
             for k in ("model", "optimizer", "scheduler"):
                 exact &= a["hashes"].get(k) == c["hashes"].get(k)
     recovered = [r for r in rows if r["kind"] == "planned_new_epoch_ab_recovered"]
+    # a handoff called off at the cut (the spare rejected a stale pre-copied
+    # state): every process reports the cancellation and A keeps committing in
+    # the old epoch past the cut
+    cancelled = [r for r in rows if r["kind"] == "planned_cancelled" and r.get("step") == cut]
     if recovered:
         checks["ab_recovered_new_epoch"] = {"pass": all(r.get("old_manager_rejected") for r in recovered)}
         checks["c_effective_commits_zero"] = {"pass": not c_commits}
+    elif cancelled:
+        after = [r for r in a0 if r["step"] > cut]
+        checks["cancelled_at_cut"] = {"pass": len(cancelled) >= 3 * nproc, "reports": len(cancelled)}
+        checks["old_epoch_kept"] = {"pass": bool(after) and all(r.get("epoch", 0) == 0 for r in after)}
+        checks["c_effective_commits_zero"] = {"pass": not c_commits}
+        rejected = [r for r in rows if r["kind"] == "planned_precopy_rejected"]
+        if rejected:
+            checks["stale_state_rejected"] = {"pass": True, "reports": len(rejected)}
     else:
         checks["ac_state_exact"] = {"pass": exact and compared > 0, "compared": compared}
         checks["no_b_in_ac"] = {"pass": all("B" not in r.get("physical_members", []) for r in c_commits)}

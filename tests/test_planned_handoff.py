@@ -51,6 +51,16 @@ def test_p2_relay_rejected_recovers_ab_in_new_epoch(tmp_path):
     assert res["checks"]["c_effective_commits_zero"]["pass"]
 
 
+def test_p2_stale_precopy_is_rejected_and_old_epoch_continues(tmp_path):
+    """The donor tags its pre-copied state with the old epoch: the spare
+    rejects it, the handoff is called off at the cut, A and B keep training
+    in the old epoch and the spare commits nothing."""
+    s = PlannedSession(tmp_path, "stale", variant="p2", scenario="stale-state")
+    res = s.run(post_steps=3)
+    assert res["pass"], res["checks"]
+    assert res["checks"]["stale_state_rejected"]["pass"] and res["checks"]["old_epoch_kept"]["pass"]
+
+
 def test_prepare_failure_cancels_and_old_epoch_continues(tmp_path):
     s = PlannedSession(tmp_path, "pf", variant="p1f", scenario="prepare-fail")
     res = s.run(post_steps=3)

@@ -119,7 +119,15 @@ class Manager:
             if store_addr is None:
                 raise ValueError("store or store_addr required")
             host, port = store_addr.rsplit(":", 1)
-            store = dist.TCPStore(host, int(port), None, rank == 0, timeout=timeout, wait_for_workers=False)
+            port = int(port)
+            if world_size == 1:
+                # no other local rank has to find this store: let the OS pick
+                # the port (a fixed one can already be held by any outgoing
+                # connection) and advertise the one it picked
+                port = 0
+            store = dist.TCPStore(host, port, None, rank == 0, timeout=timeout, wait_for_workers=False)
+            if port == 0:
+                store_addr = f"{host}:{store.port}"
             self._own_store = store
         self._store = dist.PrefixStore(f"shift_manager{local_prefix}/{replica_id}", store)
         self._store_addr = store_addr or f"{hostname}:0"

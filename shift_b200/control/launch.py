@@ -105,6 +105,21 @@ def run_module_in_child(module: str, args: list, env: dict):
     return 0
 
 
+def usable_port(host: str, port: int) -> int:
+    """``port`` if it can be bound on ``host`` now, else one the OS picks.
+    The launcher is the parent of every local rank, so it can settle the
+    rendezvous and manager-store ports for all of them: a configured port can
+    already be held by another process's outgoing connection (EADDRINUSE)."""
+    import socket
+    with socket.socket() as s:
+        try:
+            s.bind((host, port))
+            return port
+        except OSError:
+            s.bind((host, 0))
+            return s.getsockname()[1]
+
+
 def main(argv=None):
     p = argparse.ArgumentParser()
     p.add_argument("--nproc", type=int, default=1)
@@ -117,6 +132,10 @@ def main(argv=None):
     a = p.parse_args(argv)
     rest = a.rest[1:] if a.rest and a.rest[0] == "--" else a.rest
     devices = [d for d in a.devices.split(",") if d] if a.devices else []
+    a.master_port = usable_port(a.master_addr, a.master_port)
+    store = os.environ.get("SHIFT_STORE_PORT")
+    if store and int(store) > 0:
+        os.environ["SHIFT_STORE_PORT"] = str(usable_port(a.master_addr, int(store)))
     procs = []
     for r in range(a.nproc):
         env = dict(os.environ, RANK=str(r), LOCAL_RANK=str(r), WORLD_SIZE=str(a.nproc),

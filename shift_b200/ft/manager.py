@@ -32,7 +32,6 @@ import torch
 import torch.distributed as dist
 
 from .native import ManagerClient, ManagerServerHandle
-from .process_group import connect_store
 
 
 class WorldSizeMode:

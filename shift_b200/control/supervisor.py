@@ -96,6 +96,16 @@ def load_config(path) -> dict:
 
 
 
+def generation_port(base: int, replica: int, generation: int) -> int:
+    """Port of one replica's generation: replicas interleave (base + replica +
+    MAX_REPLICAS * generation), so no two replicas' generations ever share a
+    port however many relaunches a long rotation makes (a stride of 10 per
+    replica collided once a replica passed 10 generations)."""
+    if not 0 <= replica < MAX_REPLICAS:
+        raise ValueError(f"replica index {replica} outside 0..{MAX_REPLICAS - 1}")
+    return base + replica + MAX_REPLICAS * generation
+
+
 def check_replica_devices(devices: list, restart_devices: list | None = None):
     """Replicas reduce with each other inside kernels that spin on the other
     replicas' flags, so two replicas must never have ranks on the same GPU:
@@ -194,14 +204,7 @@ def main(argv=None):
         return ",".join(str(x) for x in d[args.replica % len(d)])
 
     def gen_port(base: int, gen: int) -> int:
-        """Port of one replica's generation: replicas interleave (base +
-        replica + MAX_REPLICAS * generation), so no two replicas' generations
-        ever share a port however many relaunches a long rotation makes (a
-        stride of 10 per replica collided once a replica passed 10
-        generations)."""
-        if not 0 <= args.replica < MAX_REPLICAS:
-            raise ValueError(f"replica index {args.replica} outside 0..{MAX_REPLICAS - 1}")
-        return base + args.replica + MAX_REPLICAS * gen
+        return generation_port(base, args.replica, gen)
 
     def launch(gen=None, extra=()):
         gen = generation if gen is None else gen

@@ -130,3 +130,27 @@ def test_joint_boundary_needs_every_contributing_rank():
     assert joint_boundary(rows, 1, 0, 5, 2, 2) is None       # other generation
     missing_rank = [r for r in rows if r["rank"] == 0]
     assert joint_boundary(missing_rank, 1, 1, 5, 2, 2) is None
+
+
+def test_generation_ports_never_collide_across_replicas():
+    from shift_b200.control.supervisor import MAX_REPLICAS, generation_port
+    seen = {}
+    for r in range(MAX_REPLICAS):
+        for g in range(500):
+            p = generation_port(29700, r, g)
+            assert p not in seen, (r, g, seen.get(p))
+            seen[p] = (r, g)
+    import pytest
+    with pytest.raises(ValueError):
+        generation_port(29700, MAX_REPLICAS, 0)
+
+
+def test_usable_port_falls_back_when_taken():
+    import socket
+    from shift_b200.control.launch import usable_port
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        s.listen(1)
+        taken = s.getsockname()[1]
+        other = usable_port("127.0.0.1", taken)
+        assert other != taken and other > 0
